@@ -1,0 +1,260 @@
+/*
+ * mingcuda.h -- C ABI of libmingcuda.so, the B200 (sm_100a) kernels and host engine for the
+ * per-step inference loop of Ming-3.0-tts-0.5B.
+ *
+ * The operator entry points mirror the reference's `Encoder` methods one for one
+ * (Sources/MingTTS/Engine/Kernels.swift:89-283): same argument meaning, same row-stride views,
+ * same epilogue flag bits. Each appends device work to the caller's stream and returns a status;
+ * nothing synchronises and nothing allocates. All device pointers are caller-owned.
+ * The engine entry points mirror `MingEngine.generate` / `encodeStep`
+ * (Sources/MingTTS/Engine/Engine.swift:302-415) for R concurrent requests.
+ *
+ * Types: weights are bf16 (mt_bf16 = raw uint16 bits), activations, KV caches and outputs fp32.
+ * `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ * Errors never cross the ABI as exceptions: every function returns an mt_status; the message of
+ * the last failure on a context is mt_last_error(ctx).
+ */
+#ifndef MINGCUDA_H
+#define MINGCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t mt_bf16;
+typedef struct mt_ctx mt_ctx;
+typedef struct mt_model mt_model;
+typedef struct mt_engine mt_engine;
+
+/* Status codes. Replaces the Swift `MingTTSError` enum (Sources/MingTTS/Engine/MetalContext.swift:6-26)
+ * and the `precondition` crashes on shape misuse (Kernels.swift:105, 217). */
+typedef enum {
+    MT_OK = 0,
+    MT_ERR_ARG = 1,       /* null pointer, bad stride or flag combination */
+    MT_ERR_SHAPE = 2,     /* a shape the kernel does not support */
+    MT_ERR_CAPACITY = 3,  /* KV cache or workspace would overflow */
+    MT_ERR_CUDA = 4,      /* a CUDA runtime error (message has the CUDA string) */
+    MT_ERR_TIMEOUT = 5,   /* a bounded device wait gave up (status word set by a kernel) */
+    MT_ERR_NOMEM = 6,     /* a library allocation failed (engine/model creation only) */
+    MT_ERR_STATE = 7      /* call out of order (engine not begun, already flushed, ...) */
+} mt_status;
+
+/* Epilogue flags of a linear, same bits as GemvFlags (Kernels.swift:21-27, Shaders.swift:40-44).
+ * Applied in this order: +bias, silu(v)*(x.W2^T), gelu_tanh, silu, +=y. */
+enum {
+    MT_LINEAR_BIAS = 1,
+    MT_LINEAR_ACCUM = 2,
+    MT_LINEAR_GELU = 4,
+    MT_LINEAR_SILU_GATE = 8,
+    MT_LINEAR_SILU = 16
+};
+
+/* ---------------------------------------------------------------------------------------------
+ * Model description (plain structs of caller-owned pointers)
+ * ------------------------------------------------------------------------------------------- */
+
+/* QwenConfig (Sources/MingTTS/Engine/Weights.swift:81-92). Head dim is fixed at 64. */
+typedef struct {
+    int hidden;        /* 896 */
+    int heads;         /* 14 query heads */
+    int kv_heads;      /* 2 */
+    int intermediate;  /* 4864 */
+    int layers;        /* 24 */
+    int window;        /* 0 = full causal; 65 for the VAE decoder stack (Weights.swift:216-217) */
+    float rope_theta;  /* 1e6 */
+    float eps;         /* 1e-6 */
+} mt_qwen_config;
+
+/* One Qwen2 layer (QwenLayerWeights, Weights.swift:94-102, 116-131). */
+typedef struct {
+    const mt_bf16* norm1;   /* input_layernorm [hidden] */
+    const mt_bf16* qkv_w;   /* q_proj, k_proj, v_proj rows concatenated [(heads+2*kv)*64, hidden] */
+    const mt_bf16* qkv_b;   /* [(heads+2*kv)*64] */
+    const mt_bf16* o_w;     /* [hidden, heads*64] */
+    const mt_bf16* norm2;   /* post_attention_layernorm [hidden] */
+    const mt_bf16* gate_w;  /* [intermediate, hidden] */
+    const mt_bf16* up_w;    /* [intermediate, hidden] */
+    const mt_bf16* down_w;  /* [hidden, intermediate] */
+} mt_qwen_layer;
+
+typedef struct {
+    mt_qwen_config cfg;
+    const mt_qwen_layer* layers;  /* host array of cfg.layers entries */
+    const mt_bf16* final_norm;    /* [hidden] */
+} mt_qwen_weights;
+
+/* DiT stack (DiTWeights, Weights.swift:145-172); head dim 64, hidden = heads * 64. */
+typedef struct {
+    int hidden;   /* 1024 */
+    int heads;    /* 16 */
+    int depth;    /* 8 */
+    int ff;       /* 4096, GELU-tanh MLP */
+    int out_dim;  /* 64 for the flow head, 896 for the aggregator */
+    float eps;    /* 1e-6 */
+} mt_dit_config;
+
+typedef struct {
+    const mt_bf16 *norm1, *qkv_w, *qkv_b;  /* qkv: to_q,to_k,to_v concatenated [3*hidden, hidden] */
+    const mt_bf16 *out_w, *out_b;          /* attn.to_out.0 [hidden, hidden] */
+    const mt_bf16 *norm2;
+    const mt_bf16 *ff1_w, *ff1_b;          /* mlp.ff.0.0 [ff, hidden] */
+    const mt_bf16 *ff2_w, *ff2_b;          /* mlp.ff.2 [hidden, ff] */
+} mt_dit_block;
+
+typedef struct {
+    mt_dit_config cfg;
+    const mt_dit_block* blocks;                    /* host array of cfg.depth entries */
+    const mt_bf16 *final_norm, *final_w, *final_b; /* final_layer.norm_final, final_layer.linear [out_dim, hidden] */
+    const float* inv_freq;                         /* rotary_embed.inv_freq [32] */
+} mt_dit_weights;
+
+/* Every dimension of the per-step loop. mt_model_config_default gives Ming-3.0-tts-0.5B. */
+typedef struct {
+    mt_qwen_config llm;   /* LLM stack */
+    mt_qwen_config vae;   /* VAE decoder stack (window 65) */
+    mt_dit_config flow;   /* flow-matching head DiT (out_dim = latent_dim) */
+    mt_dit_config agg;    /* aggregator DiT (out_dim = llm.hidden) */
+    int latent_dim;       /* 64 */
+    int time_dim;         /* 256: sinusoidal timestep embedding width */
+    int vocab;            /* 151936 */
+    int nfft;             /* 3528 */
+    int hop;              /* 882 */
+    int flow_steps;       /* 10 Euler steps */
+    int llm_capacity;     /* 512 positions */
+} mt_model_config;
+
+/* All weights of the per-step loop, as device (engine) or host (oracle) pointers. Names follow the
+ * checkpoint tensors listed in Weights.swift:174-263. */
+typedef struct {
+    mt_qwen_weights llm;
+    const mt_bf16 *stop_w, *stop_b;          /* stop_head [2, llm.hidden] */
+    const mt_bf16 *flow_x_w, *flow_x_b;      /* flowloss.cfm.model.x_embedder [flow.hidden, latent] */
+    const mt_bf16 *flow_c_w, *flow_c_b;      /* c_embedder.cond_embedder [flow.hidden, llm.hidden] */
+    const mt_bf16 *flow_t1_w, *flow_t1_b;    /* t_embedder.time_mlp.0 [flow.hidden, time_dim] */
+    const mt_bf16 *flow_t2_w, *flow_t2_b;    /* t_embedder.time_mlp.2 [flow.hidden, flow.hidden] */
+    mt_dit_weights flow;
+    const mt_bf16 *agg_x_w, *agg_x_b;        /* linear_proj_audio.x_embedder [agg.hidden, latent] */
+    const float* agg_cls;                    /* linear_proj_audio.word_embedder.weight [agg.hidden] */
+    mt_dit_weights agg;
+    const mt_bf16 *vae_fc1_w, *vae_fc1_b;    /* audio.decoder.fc1 [vae.hidden, latent] */
+    mt_qwen_weights vae;
+    const mt_bf16 *vae_head_w, *vae_head_b;  /* audio.decoder.head.out [nfft+2, vae.hidden] */
+    const float* vae_window;                 /* audio.decoder.head.istft.window [nfft] */
+    const mt_bf16* embed_tokens;             /* model.model.embed_tokens [vocab, llm.hidden] */
+} mt_model_weights;
+
+/* ---------------------------------------------------------------------------------------------
+ * Context
+ * ------------------------------------------------------------------------------------------- */
+
+/* Binds to CUDA device `device` (makes it current on the calling thread) and allocates the
+ * context's device status word. Replaces MetalContext (Sources/MingTTS/Engine/MetalContext.swift:28-111). */
+mt_status mt_ctx_create(int device, mt_ctx** out);
+void mt_ctx_destroy(mt_ctx* ctx);
+/* Message of the last failing call on ctx ("" if none). Valid until the next call on ctx. */
+const char* mt_last_error(const mt_ctx* ctx);
+/* Library version string, e.g. "mingcuda 0.1.0 sm_100a". */
+const char* mt_version(void);
+/* Synchronises `stream`, then reads and clears the device status word that bounded waits set.
+ * Returns MT_ERR_TIMEOUT if a kernel gave up a wait, MT_ERR_CUDA on a CUDA error.
+ * Replaces the command-buffer error check of StepRecorder.finish (Engine.swift:70-85). */
+mt_status mt_ctx_check(mt_ctx* ctx, void* stream);
+
+/* Which kernel family mt_linear routes a shape to: 0 = CUDA-core GEMV (rows in registers),
+ * 1 = tcgen05 tensor-core GEMM. Mirrors Kernels.usesGemm (Kernels.swift:81-86). */
+int mt_linear_route(int m, int n, int k);
+
+/* ---------------------------------------------------------------------------------------------
+ * Operators (one per Encoder method, Kernels.swift:89-283)
+ * ------------------------------------------------------------------------------------------- */
+
+/* y[m, n] = epi(x[m, :k] . w[n, :k]^T), x row stride ldx floats, y row stride ldy floats.
+ * w2 is the up projection for MT_LINEAR_SILU_GATE (else ignored, may be NULL); bias is read only
+ * with MT_LINEAR_BIAS. Rows of x past m are never read.
+ * Replaces Encoder.linear (Kernels.swift:132-161) and the gemv/gemm8/gemm kernels
+ * (Shaders.swift:47-108, 191-277, 304-408). Requires k % 8 == 0, 16-byte aligned x/w/w2 rows. */
+mt_status mt_linear(mt_ctx* ctx, void* stream, const float* x, int ldx, int m,
+                    const mt_bf16* w, const mt_bf16* w2, const mt_bf16* bias, int n, int k,
+                    float* y, int ldy, uint32_t flags);
+
+/* y = x * rsqrt(mean(x^2) + eps) * w per row. Replaces Encoder.rmsnorm (Kernels.swift:163-171),
+ * kernel rmsnorm (Shaders.swift:418-441). width % 4 == 0. */
+mt_status mt_rmsnorm(mt_ctx* ctx, void* stream, const float* x, int ldx, int rows, int width,
+                     const mt_bf16* w, float* y, int ldy, float eps);
+
+/* y[i] = x[i], i < count. Replaces Encoder.copy (Kernels.swift:173-178), copy_rows (Shaders.swift:443-447). */
+mt_status mt_copy(mt_ctx* ctx, void* stream, const float* x, int count, float* y);
+
+/* NeoX RoPE (pairs i, i+32) on the q heads of qkv in place; rotated k and raw v appended to the
+ * fp32 caches [hkv, capacity, 64] at positions pos0..pos0+m-1 (slot = position % capacity).
+ * Replaces Encoder.ropeCache (Kernels.swift:182-191), rope_cache (Shaders.swift:456-486). */
+mt_status mt_rope_cache(mt_ctx* ctx, void* stream, float* qkv, int ldq, int m, int hq, int hkv,
+                        int pos0, float* k_cache, float* v_cache, int capacity, const float* inv_freq);
+
+/* Causal GQA attention of the m query rows at positions pos0.. over the cache, scale 1/8,
+ * window = 0 for full causal else keys (pos - window, pos]. out[m, hq*64] row stride ldo.
+ * Replaces Encoder.attention (Kernels.swift:195-206), attention_cache (Shaders.swift:500-591). */
+mt_status mt_attention(mt_ctx* ctx, void* stream, const float* q, int ldq, int m, int hq, int hkv,
+                       int pos0, int window, const float* k_cache, const float* v_cache,
+                       int capacity, float* out, int ldo);
+
+/* Full attention over `batch` sequences of `seq` <= 8 rows with interleaved RoPE (pairs 2l, 2l+1,
+ * angle = row * inv_freq[l]). qkv rows are [q | k | v] of heads*64 each, row stride ld.
+ * Replaces Encoder.ditAttention (Kernels.swift:210-220), dit_attention (Shaders.swift:613-648). */
+mt_status mt_dit_attention(mt_ctx* ctx, void* stream, const float* qkv, int ld, int batch, int seq,
+                           int heads, const float* inv_freq, float* out, int ldo);
+
+/* The 6 flow DiT input rows: r%3==0 -> temb + (r<3 ? cemb : cond_bias), r%3==1 -> x_emb(history),
+ * r%3==2 -> x_emb(y), x_emb(v) = x_w . v + x_b. x is [6, hidden] dense.
+ * Replaces Encoder.flowAssemble (Kernels.swift:222-235), flow_assemble (Shaders.swift:654-677). */
+mt_status mt_flow_assemble(mt_ctx* ctx, void* stream, const float* y, const float* history,
+                           const float* cemb, const mt_bf16* cond_bias, const float* temb,
+                           const mt_bf16* x_w, const mt_bf16* x_b, int hidden, int latent_dim,
+                           float* x);
+
+/* y += (c + (c - u) * cfg) * dt with c = pred[pred_row], u = pred[null_row]; capture = [c, u].
+ * Replaces Encoder.flowEuler (Kernels.swift:237-245), flow_euler (Shaders.swift:682-693). */
+mt_status mt_flow_euler(mt_ctx* ctx, void* stream, float* y, const float* pred, int ldp,
+                        int pred_row, int null_row, int latent_dim, float cfg, float dt,
+                        float* capture);
+
+/* Four frames [4, hidden] of linear x4 upsampling (align_corners=False) from h[n-1], h[n], h[n+1];
+ * prev/next may be NULL (clamped to cur). Replaces Encoder.upsample4 (Kernels.swift:247-257),
+ * upsample4 (Shaders.swift:704-719). */
+mt_status mt_upsample4(mt_ctx* ctx, void* stream, const float* prev, const float* cur,
+                       const float* next, int hidden, float* frames);
+
+/* `count` windowed ISTFT frames from spectrum rows [logmag (nfft/2+1) | phase (nfft/2+1)] into
+ * ring slots (frame0 + f) % ring of `frames` [ring, nfft]. cos_table is unused by this
+ * implementation (kept for signature parity, may be NULL). nfft % 4 == 0.
+ * Replaces Encoder.istftFrames (Kernels.swift:260-269), istft_frames (Shaders.swift:726-764). */
+mt_status mt_istft_frames(mt_ctx* ctx, void* stream, const float* spec, int ld_spec, int count,
+                          int nfft, const float* cos_table, const float* window, float* frames,
+                          int frame0, int ring);
+
+/* Overlap-add of stream samples s0..s0+count from the ring, divided by the window^2 envelope,
+ * pad = (nfft - hop) / 2. Replaces Encoder.istftEmit (Kernels.swift:272-281), istft_emit
+ * (Shaders.swift:770-788). count == 0 is a no-op. */
+mt_status mt_istft_emit(mt_ctx* ctx, void* stream, const float* frames, const float* window,
+                        int nfft, int hop, int s0, int count, int last_frame, int ring, float* out);
+
+/* ---------------------------------------------------------------------------------------------
+ * Synthetic data (seeded random-init weights and noise)
+ * ------------------------------------------------------------------------------------------- */
+
+/* Standard normal samples from a SplitMix64 stream with Box-Muller in double, as
+ * MingEngine.gaussianNoise (Engine.swift:433-453): out[i] = N(0,1) as fp32. Host. */
+void mt_gaussian_noise_host(float* out, size_t count, uint64_t seed);
+/* std * N(0,1) from the same stream, rounded to bf16 (round-to-nearest-even). Host (OpenMP)
+ * and device versions produce identical bits. */
+void mt_randn_bf16_host(mt_bf16* out, size_t count, uint64_t seed, float std);
+mt_status mt_randn_bf16(mt_ctx* ctx, void* stream, mt_bf16* out, size_t count, uint64_t seed,
+                        float std);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MINGCUDA_H */

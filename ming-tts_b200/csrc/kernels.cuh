@@ -1,0 +1,86 @@
+// kernels.cuh -- argument blocks and launchers of the device kernels (internal to libmingcuda.so).
+#pragma once
+
+#include "common.cuh"
+
+namespace mt {
+
+struct RmsArgs {
+    const float* x; int ldx; int rows; int width;
+    const uint16_t* w;
+    float* y; int ldy;                 // optional fp32 output
+    uint16_t* y_hi; uint16_t* y_lo;    // optional bf16 hi/lo planes
+    int ld_split;
+    float eps;
+};
+void launch_rmsnorm(const RmsArgs& a, cudaStream_t s);
+void launch_split(const float* x, int ldx, int rows, int cols, uint16_t* hi, uint16_t* lo, int ld_split,
+                  int sm_count, cudaStream_t s);
+
+// Rows are grouped by request: row m belongs to request m / rows_per_req and sits at position
+// pos0 + pos_dev[request] (pos_dev optional) + m % rows_per_req. Request r's caches start at
+// kc/vc + r * req_stride floats; cache slot = position % cap.
+struct RopeArgs {
+    float* qkv; int ldq; int rows; int rows_per_req; int hq; int hkv;
+    int pos0; const int* pos_dev;
+    float* kc; float* vc; long long req_stride; int cap;
+    const float* inv_freq;
+};
+void launch_rope_cache(const RopeArgs& a, cudaStream_t s);
+
+struct AttnArgs {
+    const float* q; int ldq; int rows; int rows_per_req; int hq; int hkv;
+    int pos0; const int* pos_dev; int window;
+    const float* kc; const float* vc; long long req_stride; int cap;
+    float* out; int ldo;                      // optional fp32 output
+    uint16_t* out_hi; uint16_t* out_lo; int ld_split;  // optional bf16 hi/lo output
+    int max_keys;                             // upper bound of keys any row attends to
+};
+size_t attention_smem(int G, int max_keys);
+void launch_attention(const AttnArgs& a, cudaStream_t s);
+
+struct DitAttnArgs {
+    const float* qkv; int ld; int batch; int seq; int heads;
+    const float* inv_freq;
+    float* out; int ldo;
+    uint16_t* out_hi; uint16_t* out_lo; int ld_split;
+};
+void launch_dit_attention(const DitAttnArgs& a, cudaStream_t s);
+
+// ISTFT frames: spectrum row f belongs to request f / frames_per_req and lands in that request's
+// ring (frames + request * req_stride) at slot (frame0 + frame0_dev[request] + f % frames_per_req) % ring.
+struct IstftArgs {
+    const float* spec; int ld_spec; int count; int nfft;
+    const float* window;
+    float* frames; long long req_stride; int frames_per_req;
+    int frame0; const int* frame0_dev; int ring;
+};
+size_t istft_frames_smem(int nfft);
+void launch_istft_frames(const IstftArgs& a, cudaStream_t s);
+
+// Emission: request r (grid y) writes count (or count_dev[r]) samples of its stream starting at
+// s0 (+ s0_dev[r]) to out + r * ld_out, from its ring frames + r * req_stride.
+struct EmitArgs {
+    const float* frames; long long req_stride;
+    const float* window; int nfft; int hop;
+    int s0; const int* s0_dev; int count; const int* count_dev;
+    int last_frame; const int* last_dev; int ring;
+    float* out; long long ld_out;
+};
+void launch_istft_emit(const EmitArgs& a, int max_count, int requests, cudaStream_t s);
+
+// Linear Y[m, n] = epi(X[m, :k] . W[n, :k]^T) -- see linear.cu / gemm_tc.cu.
+struct LinearArgs {
+    const float* x; int ldx;                   // fp32 activations (GEMV route)
+    const uint16_t* x_hi; const uint16_t* x_lo; int ld_split;  // bf16 planes (tensor-core route)
+    int m, n, k;
+    const uint16_t* w; const uint16_t* w2; const uint16_t* bias;
+    float* y; int ldy;                         // fp32 output (optional on the tensor-core route)
+    uint16_t* y_hi; uint16_t* y_lo; int ld_ysplit;  // bf16 hi/lo output planes (optional)
+    uint32_t flags;
+    int split_k;                               // tensor-core route: >1 = atomically reduced K splits
+};
+void launch_gemv(const LinearArgs& a, cudaStream_t s);
+mt_status launch_gemm_tc(mt_ctx* ctx, const LinearArgs& a, cudaStream_t s);
+
+}  // namespace mt

@@ -1,0 +1,232 @@
+// linear.cu -- Y[m, n] = epi(X[m, :k] . W[n, :k]^T) for small m on CUDA cores, and the mt_linear
+// dispatcher (CUDA-core GEMV for m <= 8, tcgen05 tensor-core GEMM above).
+//
+// Reference semantics: gemv_kernel / gemm8_kernel / gemm_kernel (Shaders.swift:47-108, 191-277,
+// 304-408), routing Encoder.linear (Kernels.swift:132-161). fp32 X, bf16 W, fp32 accumulate,
+// epilogue order +bias -> silu gate -> gelu -> silu -> accumulate.
+//
+// GEMV design: the weight matrix is streamed exactly once with 16-byte non-caching loads; a group
+// of G threads (8..256, a power of two) owns one output column for all MR rows, G sized so each
+// thread keeps about four 16-byte loads in flight; partial sums meet through warp shuffles (and
+// shared memory when G spans warps).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mt {
+
+constexpr int GEMV_THREADS = 256;
+
+template <int MR, int G, bool GATED>
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(LinearArgs a) {
+    constexpr int C = GEMV_THREADS / G;  // columns per block
+    __shared__ float red[GATED ? 2 : 1][GEMV_THREADS / 32][MR];
+    const int tid = threadIdx.x;
+    const int group = tid / G, gl = tid % G;
+    const int n = blockIdx.x * C + group;
+    const int row0 = blockIdx.y * MR;
+    const int rows = min(MR, a.m - row0);
+    const bool live = n < a.n;
+    const int chunks = a.k >> 3;
+
+    float acc[MR], acc2[MR];
+#pragma unroll
+    for (int r = 0; r < MR; r++) { acc[r] = 0.f; acc2[r] = 0.f; }
+
+    if (live) {
+        const uint16_t* wrow = a.w + (size_t)n * a.k;
+        const uint16_t* w2row = GATED ? a.w2 + (size_t)n * a.k : nullptr;
+        const float* x = a.x + (size_t)row0 * a.ldx;
+        int c = gl;
+        // Four chunks per iteration keep four independent 16-byte weight loads in flight.
+        for (; c + 3 * G < chunks; c += 4 * G) {
+            uint4 wv[4], wv2[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                wv[u] = ld_stream_u4(wrow + (size_t)(c + u * G) * 8);
+                if (GATED) wv2[u] = ld_stream_u4(w2row + (size_t)(c + u * G) * 8);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int k0 = (c + u * G) * 8;
+#pragma unroll
+                for (int r = 0; r < MR; r++) {
+                    if (r < rows) {
+                        const float4 x0 = *reinterpret_cast<const float4*>(x + (size_t)r * a.ldx + k0);
+                        const float4 x1 = *reinterpret_cast<const float4*>(x + (size_t)r * a.ldx + k0 + 4);
+                        acc[r] += x0.x * bf16_lo(wv[u].x) + x0.y * bf16_hi(wv[u].x) + x0.z * bf16_lo(wv[u].y) +
+                                  x0.w * bf16_hi(wv[u].y) + x1.x * bf16_lo(wv[u].z) + x1.y * bf16_hi(wv[u].z) +
+                                  x1.z * bf16_lo(wv[u].w) + x1.w * bf16_hi(wv[u].w);
+                        if (GATED)
+                            acc2[r] += x0.x * bf16_lo(wv2[u].x) + x0.y * bf16_hi(wv2[u].x) + x0.z * bf16_lo(wv2[u].y) +
+                                       x0.w * bf16_hi(wv2[u].y) + x1.x * bf16_lo(wv2[u].z) + x1.y * bf16_hi(wv2[u].z) +
+                                       x1.z * bf16_lo(wv2[u].w) + x1.w * bf16_hi(wv2[u].w);
+                    }
+                }
+            }
+        }
+        for (; c < chunks; c += G) {
+            const uint4 wv = ld_stream_u4(wrow + (size_t)c * 8);
+            uint4 wv2 = make_uint4(0, 0, 0, 0);
+            if (GATED) wv2 = ld_stream_u4(w2row + (size_t)c * 8);
+            const int k0 = c * 8;
+#pragma unroll
+            for (int r = 0; r < MR; r++) {
+                if (r < rows) {
+                    const float4 x0 = *reinterpret_cast<const float4*>(x + (size_t)r * a.ldx + k0);
+                    const float4 x1 = *reinterpret_cast<const float4*>(x + (size_t)r * a.ldx + k0 + 4);
+                    acc[r] += x0.x * bf16_lo(wv.x) + x0.y * bf16_hi(wv.x) + x0.z * bf16_lo(wv.y) + x0.w * bf16_hi(wv.y) +
+                              x1.x * bf16_lo(wv.z) + x1.y * bf16_hi(wv.z) + x1.z * bf16_lo(wv.w) + x1.w * bf16_hi(wv.w);
+                    if (GATED)
+                        acc2[r] += x0.x * bf16_lo(wv2.x) + x0.y * bf16_hi(wv2.x) + x0.z * bf16_lo(wv2.y) +
+                                   x0.w * bf16_hi(wv2.y) + x1.x * bf16_lo(wv2.z) + x1.y * bf16_hi(wv2.z) +
+                                   x1.z * bf16_lo(wv2.w) + x1.w * bf16_hi(wv2.w);
+                }
+            }
+        }
+    }
+
+    // Reduce over the G threads of the column group.
+    constexpr int WG = G < 32 ? G : 32;
+#pragma unroll
+    for (int r = 0; r < MR; r++) {
+#pragma unroll
+        for (int o = WG / 2; o > 0; o >>= 1) {
+            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+            if (GATED) acc2[r] += __shfl_xor_sync(0xffffffffu, acc2[r], o);
+        }
+    }
+    if (G > 32) {
+        const int warp = tid >> 5, lane = tid & 31;
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < MR; r++) {
+                red[0][warp][r] = acc[r];
+                if (GATED) red[GATED ? 1 : 0][warp][r] = acc2[r];
+            }
+        }
+        __syncthreads();
+        if (gl != 0) return;
+        const int w0 = group * (G / 32);
+#pragma unroll
+        for (int r = 0; r < MR; r++) {
+            float s = 0.f, s2 = 0.f;
+            for (int w = 0; w < G / 32; w++) {
+                s += red[0][w0 + w][r];
+                if (GATED) s2 += red[GATED ? 1 : 0][w0 + w][r];
+            }
+            acc[r] = s;
+            acc2[r] = s2;
+        }
+    } else if (gl != 0) {
+        return;
+    }
+    if (!live) return;
+
+    const float bval = (a.flags & MT_LINEAR_BIAS) ? bf16f(a.bias[n]) : 0.f;
+#pragma unroll
+    for (int r = 0; r < MR; r++) {
+        if (r < rows) {
+            float v = acc[r] + bval;
+            if (GATED) v = silu(v) * acc2[r];
+            if (a.flags & MT_LINEAR_GELU) v = gelu_tanh(v);
+            if (a.flags & MT_LINEAR_SILU) v = silu(v);
+            float* yp = a.y + (size_t)(row0 + r) * a.ldy + n;
+            if (a.flags & MT_LINEAR_ACCUM) v += *yp;
+            *yp = v;
+        }
+    }
+}
+
+template <int MR, bool GATED>
+static void launch_gemv_g(const LinearArgs& a, int G, cudaStream_t s) {
+    const int C = GEMV_THREADS / G;
+    dim3 grid((a.n + C - 1) / C, (a.m + MR - 1) / MR);
+    switch (G) {
+        case 8: gemv_kernel<MR, 8, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
+        case 16: gemv_kernel<MR, 16, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
+        case 32: gemv_kernel<MR, 32, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
+        case 64: gemv_kernel<MR, 64, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
+        case 128: gemv_kernel<MR, 128, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
+        default: gemv_kernel<MR, 256, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
+    }
+}
+
+// Threads per column: about four 16-byte chunks per thread, 8..256.
+static int gemv_group(int k) {
+    const int chunks = k / 8;
+    int g = 8;
+    while (g < 256 && g * 4 < chunks) g *= 2;
+    return g;
+}
+
+void launch_gemv(const LinearArgs& a, cudaStream_t s) {
+    const int G = gemv_group(a.k);
+    const bool gated = (a.flags & MT_LINEAR_SILU_GATE) != 0;
+    const int mr = a.m <= 1 ? 1 : a.m <= 2 ? 2 : a.m <= 4 ? 4 : 8;
+    if (gated) {
+        switch (mr) {
+            case 1: launch_gemv_g<1, true>(a, G, s); break;
+            case 2: launch_gemv_g<2, true>(a, G, s); break;
+            case 4: launch_gemv_g<4, true>(a, G, s); break;
+            default: launch_gemv_g<8, true>(a, G, s); break;
+        }
+    } else {
+        switch (mr) {
+            case 1: launch_gemv_g<1, false>(a, G, s); break;
+            case 2: launch_gemv_g<2, false>(a, G, s); break;
+            case 4: launch_gemv_g<4, false>(a, G, s); break;
+            default: launch_gemv_g<8, false>(a, G, s); break;
+        }
+    }
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+// Rows up to this many stay on CUDA cores: at these row counts the weight stream, not the
+// multiply-adds, bounds the op, and the tensor-core route would pad the rows to its tile.
+static const int kGemvMaxRows = 8;
+
+extern "C" {
+
+int mt_linear_route(int m, int n, int k) {
+    (void)n;
+    (void)k;
+    return m <= kGemvMaxRows ? 0 : 1;
+}
+
+mt_status mt_linear(mt_ctx* ctx, void* stream, const float* x, int ldx, int m, const mt_bf16* w,
+                    const mt_bf16* w2, const mt_bf16* bias, int n, int k, float* y, int ldy, uint32_t flags) {
+    MT_REQUIRE(ctx, ctx && x && w && y, MT_ERR_ARG, "mt_linear: null argument");
+    MT_REQUIRE(ctx, (flags & ~31u) == 0, MT_ERR_ARG, "mt_linear: unknown flag bits 0x%x", flags);
+    MT_REQUIRE(ctx, !(flags & MT_LINEAR_SILU_GATE) || w2, MT_ERR_ARG, "mt_linear: SILU_GATE needs w2");
+    MT_REQUIRE(ctx, !(flags & MT_LINEAR_BIAS) || bias, MT_ERR_ARG, "mt_linear: BIAS needs bias");
+    MT_REQUIRE(ctx, m >= 0 && n > 0 && k > 0 && k % 8 == 0 && ldx >= k && ldy >= n && ldx % 4 == 0, MT_ERR_SHAPE,
+               "mt_linear: m %d n %d k %d ldx %d ldy %d (need k %% 8 == 0, ldx %% 4 == 0)", m, n, k, ldx, ldy);
+    MT_REQUIRE(ctx, ((uintptr_t)x & 15u) == 0 && ((uintptr_t)w & 15u) == 0 && (!w2 || ((uintptr_t)w2 & 15u) == 0),
+               MT_ERR_ARG, "mt_linear: x, w, w2 need 16-byte alignment");
+    if (m == 0) return MT_OK;
+    cudaStream_t s = as_stream(stream);
+    LinearArgs a{};
+    a.x = x; a.ldx = ldx; a.m = m; a.n = n; a.k = k; a.w = w; a.w2 = w2; a.bias = bias;
+    a.y = y; a.ldy = ldy; a.flags = flags; a.split_k = 1;
+    if (mt_linear_route(m, n, k) == 0) {
+        launch_gemv(a, s);
+        return check_launch(ctx, "mt_linear (gemv)");
+    }
+    // Tensor-core route: split X into bf16 hi/lo planes in the context scratch, then the GEMM.
+    void* buf = nullptr;
+    const size_t plane = (size_t)m * k;
+    mt_status st = mt::scratch(ctx, s, plane * 2 * sizeof(uint16_t), &buf);
+    if (st != MT_OK) return st;
+    uint16_t* hi = static_cast<uint16_t*>(buf);
+    uint16_t* lo = hi + plane;
+    launch_split(x, ldx, m, k, hi, lo, k, ctx->sm_count, s);
+    st = check_launch(ctx, "mt_linear (split)");
+    if (st != MT_OK) return st;
+    a.x_hi = hi; a.x_lo = lo; a.ld_split = k;
+    return launch_gemm_tc(ctx, a, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,460 @@
+// ops.cu -- element-wise, normalisation and attention kernels, and their C-ABI entry points.
+//
+// Reference kernels restated (semantics, not code): rmsnorm / copy_rows (Shaders.swift:418-447),
+// rope_cache (Shaders.swift:456-486), attention_cache (Shaders.swift:500-591), dit_attention
+// (Shaders.swift:613-648), flow_assemble / flow_euler (Shaders.swift:654-693), upsample4
+// (Shaders.swift:704-719).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mt {
+
+// ------------------------------------------------------------------------------------------------
+// RMSNorm: one warp per row, fp32 sum of squares, optional fp32 and/or bf16 hi/lo outputs.
+// ------------------------------------------------------------------------------------------------
+__global__ void rmsnorm_kernel(RmsArgs a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (row >= a.rows) return;
+    const float4* x = reinterpret_cast<const float4*>(a.x + (size_t)row * a.ldx);
+    const int n4 = a.width >> 2;
+    float ss = 0.f;
+    for (int i = lane; i < n4; i += 32) {
+        const float4 v = x[i];
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum(ss);
+    const float scale = rsqrtf(ss / (float)a.width + a.eps);
+    const uint2* w = reinterpret_cast<const uint2*>(a.w);
+    for (int i = lane; i < n4; i += 32) {
+        const float4 v = x[i];
+        const uint2 wv = w[i];
+        float4 o;
+        o.x = v.x * scale * bf16_lo(wv.x);
+        o.y = v.y * scale * bf16_hi(wv.x);
+        o.z = v.z * scale * bf16_lo(wv.y);
+        o.w = v.w * scale * bf16_hi(wv.y);
+        if (a.y) reinterpret_cast<float4*>(a.y + (size_t)row * a.ldy)[i] = o;
+        if (a.y_hi) {
+            uint16_t h[4], l[4];
+            split_bf16(o.x, h[0], l[0]);
+            split_bf16(o.y, h[1], l[1]);
+            split_bf16(o.z, h[2], l[2]);
+            split_bf16(o.w, h[3], l[3]);
+            uint2 hv = make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
+            uint2 lv = make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
+            reinterpret_cast<uint2*>(a.y_hi + (size_t)row * a.ld_split)[i] = hv;
+            reinterpret_cast<uint2*>(a.y_lo + (size_t)row * a.ld_split)[i] = lv;
+        }
+    }
+}
+
+void launch_rmsnorm(const RmsArgs& a, cudaStream_t s) {
+    const int warps = 4;
+    rmsnorm_kernel<<<(a.rows + warps - 1) / warps, warps * 32, 0, s>>>(a);
+}
+
+// fp32 [rows, cols] (row stride ldx) -> bf16 hi/lo planes [rows, cols] (row stride ld_split).
+__global__ void split_kernel(const float* __restrict__ x, int ldx, int rows, int cols,
+                             uint16_t* __restrict__ hi, uint16_t* __restrict__ lo, int ld_split) {
+    const int c4 = cols >> 2;
+    const long long total = (long long)rows * c4;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / c4), c = (int)(i % c4);
+        const float4 v = reinterpret_cast<const float4*>(x + (size_t)r * ldx)[c];
+        uint16_t h[4], l[4];
+        split_bf16(v.x, h[0], l[0]);
+        split_bf16(v.y, h[1], l[1]);
+        split_bf16(v.z, h[2], l[2]);
+        split_bf16(v.w, h[3], l[3]);
+        reinterpret_cast<uint2*>(hi + (size_t)r * ld_split)[c] =
+            make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
+        reinterpret_cast<uint2*>(lo + (size_t)r * ld_split)[c] =
+            make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
+    }
+}
+
+void launch_split(const float* x, int ldx, int rows, int cols, uint16_t* hi, uint16_t* lo,
+                  int ld_split, int sm_count, cudaStream_t s) {
+    long long total = (long long)rows * (cols / 4);
+    long long blocks = (total + 255) / 256;
+    if (blocks > sm_count * 8LL) blocks = sm_count * 8LL;
+    if (blocks < 1) blocks = 1;
+    split_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, ldx, rows, cols, hi, lo, ld_split);
+}
+
+__global__ void copy_kernel(const float* __restrict__ x, int count, float* __restrict__ y) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) y[i] = x[i];
+}
+
+// ------------------------------------------------------------------------------------------------
+// NeoX RoPE + KV append. Block = one query row, thread (slot, i): slot over q, k, v heads,
+// i over the 32 rotation pairs. Requests: row m belongs to request m / rows_per_req, whose caches
+// start at kc/vc + request * req_stride and whose first position is pos0 (+ pos_dev[request]).
+// ------------------------------------------------------------------------------------------------
+__global__ void rope_cache_kernel(RopeArgs a) {
+    const int m = blockIdx.x;
+    const int slot = threadIdx.x >> 5, i = threadIdx.x & 31;
+    if (slot >= a.hq + 2 * a.hkv) return;
+    const int req = m / a.rows_per_req;
+    const int pos = a.pos0 + (a.pos_dev ? a.pos_dev[req] : 0) + (m % a.rows_per_req);
+    const int cslot = pos % a.cap;
+    float* row = a.qkv + (size_t)m * a.ldq + slot * 64;
+    float* kc = a.kc + (size_t)req * a.req_stride;
+    float* vc = a.vc + (size_t)req * a.req_stride;
+    if (slot >= a.hq + a.hkv) {
+        float* dst = vc + ((size_t)(slot - a.hq - a.hkv) * a.cap + cslot) * 64;
+        dst[i] = row[i];
+        dst[i + 32] = row[i + 32];
+        return;
+    }
+    const float angle = (float)pos * a.inv_freq[i];
+    float s, c;
+    sincosf(angle, &s, &c);
+    const float x0 = row[i], x1 = row[i + 32];
+    const float r0 = x0 * c - x1 * s;
+    const float r1 = x1 * c + x0 * s;
+    if (slot < a.hq) {
+        row[i] = r0;
+        row[i + 32] = r1;
+    } else {
+        float* dst = kc + ((size_t)(slot - a.hq) * a.cap + cslot) * 64;
+        dst[i] = r0;
+        dst[i + 32] = r1;
+    }
+}
+
+void launch_rope_cache(const RopeArgs& a, cudaStream_t s) {
+    rope_cache_kernel<<<a.rows, (a.hq + 2 * a.hkv) * 32, 0, s>>>(a);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Causal GQA attention over the fp32 cache. One block per (query row, kv head): the G = hq / hkv
+// query heads of the group share every K and V load. Keys are staged through shared memory in
+// chunks of 64; scores for all keys live in shared memory (two-pass softmax), then P.V.
+// ------------------------------------------------------------------------------------------------
+constexpr int ATT_THREADS = 256;
+constexpr int ATT_CHUNK = 64;
+
+__global__ void __launch_bounds__(ATT_THREADS) attention_kernel(AttnArgs a) {
+    extern __shared__ float smem[];
+    const int m = blockIdx.x, kvh = blockIdx.y;
+    const int G = a.hq / a.hkv;
+    const int req = m / a.rows_per_req;
+    const int qpos = a.pos0 + (a.pos_dev ? a.pos_dev[req] : 0) + (m % a.rows_per_req);
+    const int jEnd = qpos + 1;
+    const int jStart = (a.window > 0 && jEnd > a.window) ? jEnd - a.window : 0;
+    const int nKeys = jEnd - jStart;
+    const float* kc = a.kc + (size_t)req * a.req_stride + (size_t)kvh * a.cap * 64;
+    const float* vc = a.vc + (size_t)req * a.req_stride + (size_t)kvh * a.cap * 64;
+
+    float* qs = smem;                       // [G][64]
+    float* ks = qs + G * 64;                // [ATT_CHUNK][65]
+    float* sc = ks + ATT_CHUNK * 65;        // [G][nKeys]
+    float* red = sc + (size_t)G * a.max_keys;  // [G][2]
+    const int tid = threadIdx.x;
+    for (int i = tid; i < G * 64; i += ATT_THREADS)
+        qs[i] = a.q[(size_t)m * a.ldq + (kvh * G + i / 64) * 64 + (i % 64)];
+
+    // Scores.
+    for (int c0 = 0; c0 < nKeys; c0 += ATT_CHUNK) {
+        const int cn = min(ATT_CHUNK, nKeys - c0);
+        __syncthreads();
+        for (int i = tid; i < cn * 16; i += ATT_THREADS) {
+            const int kk = i >> 4, d4 = i & 15;
+            const int slot = (jStart + c0 + kk) % a.cap;
+            const float4 v = reinterpret_cast<const float4*>(kc + (size_t)slot * 64)[d4];
+            float* dst = ks + kk * 65 + d4 * 4;
+            dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+        }
+        __syncthreads();
+        for (int i = tid; i < cn * G; i += ATT_THREADS) {
+            const int kk = i % cn, g = i / cn;
+            const float* qg = qs + g * 64;
+            const float* kr = ks + kk * 65;
+            float s = 0.f;
+#pragma unroll 16
+            for (int d = 0; d < 64; d++) s += qg[d] * kr[d];
+            sc[(size_t)g * a.max_keys + c0 + kk] = s * 0.125f;
+        }
+    }
+    __syncthreads();
+    // Softmax per head: warp g handles head g (G <= 8 warps).
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int g = warp; g < G; g += ATT_THREADS / 32) {
+        float* sg = sc + (size_t)g * a.max_keys;
+        float mx = -INFINITY;
+        for (int j = lane; j < nKeys; j += 32) mx = fmaxf(mx, sg[j]);
+        mx = warp_max(mx);
+        float sum = 0.f;
+        for (int j = lane; j < nKeys; j += 32) {
+            const float e = expf(sg[j] - mx);
+            sg[j] = e;
+            sum += e;
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) red[g] = 1.0f / sum;
+    }
+    __syncthreads();
+    // P.V: thread (g, d); V rows read straight from the cache (coalesced over d).
+    for (int i = tid; i < G * 64; i += ATT_THREADS) {
+        const int g = i / 64, d = i % 64;
+        const float* sg = sc + (size_t)g * a.max_keys;
+        float acc = 0.f;
+        for (int j = 0; j < nKeys; j++) acc += sg[j] * vc[(size_t)((jStart + j) % a.cap) * 64 + d];
+        const float o = acc * red[g];
+        const size_t off = (size_t)m * a.ldo + (kvh * G + g) * 64 + d;
+        if (a.out) a.out[off] = o;
+        if (a.out_hi) {
+            uint16_t h, l;
+            split_bf16(o, h, l);
+            const size_t so = (size_t)m * a.ld_split + (kvh * G + g) * 64 + d;
+            a.out_hi[so] = h;
+            a.out_lo[so] = l;
+        }
+    }
+}
+
+size_t attention_smem(int G, int max_keys) {
+    return sizeof(float) * ((size_t)G * 64 + ATT_CHUNK * 65 + (size_t)G * max_keys + (size_t)G * 2);
+}
+
+void launch_attention(const AttnArgs& a, cudaStream_t s) {
+    const int G = a.hq / a.hkv;
+    const size_t smem = attention_smem(G, a.max_keys);
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        configured = true;
+    }
+    attention_kernel<<<dim3(a.rows, a.hkv), ATT_THREADS, smem, s>>>(a);
+}
+
+// ------------------------------------------------------------------------------------------------
+// DiT attention: one warp per (sequence, row, head); lane l owns dims 2l, 2l+1 = one interleaved
+// RoPE pair, so q and k rotate with one sincos per position.
+// ------------------------------------------------------------------------------------------------
+__global__ void dit_attention_kernel(DitAttnArgs a) {
+    const int work = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (work >= a.batch * a.seq * a.heads) return;
+    const int h = work % a.heads, i = (work / a.heads) % a.seq, b = work / (a.heads * a.seq);
+    const int D = a.heads * 64;
+    const float freq = a.inv_freq[lane];
+    const float* rows = a.qkv + (size_t)b * a.seq * a.ld + h * 64 + 2 * lane;
+    float s, c;
+    sincosf((float)i * freq, &s, &c);
+    const float2 qr = *reinterpret_cast<const float2*>(rows + (size_t)i * a.ld);
+    const float q0 = qr.x * c - qr.y * s, q1 = qr.y * c + qr.x * s;
+    float sc[8];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        if (j < a.seq) {
+            float sj, cj;
+            sincosf((float)j * freq, &sj, &cj);
+            const float2 kr = *reinterpret_cast<const float2*>(rows + (size_t)j * a.ld + D);
+            const float k0 = kr.x * cj - kr.y * sj, k1 = kr.y * cj + kr.x * sj;
+            sc[j] = warp_sum(q0 * k0 + q1 * k1) * 0.125f;
+            mx = fmaxf(mx, sc[j]);
+        }
+    }
+    float sum = 0.f, acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        if (j < a.seq) {
+            const float e = expf(sc[j] - mx);
+            sum += e;
+            const float2 v = *reinterpret_cast<const float2*>(rows + (size_t)j * a.ld + 2 * D);
+            acc0 += e * v.x;
+            acc1 += e * v.y;
+        }
+    }
+    const float o0 = acc0 / sum, o1 = acc1 / sum;
+    const size_t row = (size_t)(b * a.seq + i);
+    if (a.out) *reinterpret_cast<float2*>(a.out + row * a.ldo + h * 64 + 2 * lane) = make_float2(o0, o1);
+    if (a.out_hi) {
+        uint16_t h0, l0, h1, l1;
+        split_bf16(o0, h0, l0);
+        split_bf16(o1, h1, l1);
+        const size_t so = row * a.ld_split + h * 64 + 2 * lane;
+        *reinterpret_cast<uint32_t*>(a.out_hi + so) = h0 | ((uint32_t)h1 << 16);
+        *reinterpret_cast<uint32_t*>(a.out_lo + so) = l0 | ((uint32_t)l1 << 16);
+    }
+}
+
+void launch_dit_attention(const DitAttnArgs& a, cudaStream_t s) {
+    const int work = a.batch * a.seq * a.heads;
+    dit_attention_kernel<<<(work + 7) / 8, 256, 0, s>>>(a);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Flow pieces.
+// ------------------------------------------------------------------------------------------------
+__global__ void flow_assemble_kernel(const float* __restrict__ y, const float* __restrict__ history,
+                                     const float* __restrict__ cemb, const uint16_t* __restrict__ cbias,
+                                     const float* __restrict__ temb, const uint16_t* __restrict__ xw,
+                                     const uint16_t* __restrict__ xb, int hidden, int latent,
+                                     float* __restrict__ x) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
+    if (c >= hidden) return;
+    const int s = r % 3;
+    float v;
+    if (s == 0) {
+        v = temb[c] + (r < 3 ? cemb[c] : bf16f(cbias[c]));
+    } else {
+        const float* src = (s == 1) ? history : y;
+        const uint16_t* w = xw + (size_t)c * latent;
+        float acc = 0.f;
+        for (int d = 0; d < latent; d++) acc += bf16f(w[d]) * src[d];
+        v = bf16f(xb[c]) + acc;
+    }
+    x[(size_t)r * hidden + c] = v;
+}
+
+__global__ void flow_euler_kernel(float* __restrict__ y, const float* __restrict__ pred, int ldp,
+                                  int pred_row, int null_row, int latent, float cfg, float dt,
+                                  float* __restrict__ capture) {
+    const int d = blockIdx.x * blockDim.x + threadIdx.x;
+    if (d >= latent) return;
+    const float c = pred[(size_t)pred_row * ldp + d];
+    const float u = pred[(size_t)null_row * ldp + d];
+    if (capture) {
+        capture[d] = c;
+        capture[latent + d] = u;
+    }
+    y[d] += (c + (c - u) * cfg) * dt;
+}
+
+__global__ void upsample4_kernel(const float* __restrict__ prev, const float* __restrict__ cur,
+                                 const float* __restrict__ next, int hidden, float* __restrict__ frames) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
+    if (c >= hidden) return;
+    const float v0 = cur[c];
+    float v;
+    if (r == 0) v = prev ? 0.625f * v0 + 0.375f * prev[c] : v0;
+    else if (r == 1) v = prev ? 0.875f * v0 + 0.125f * prev[c] : v0;
+    else if (r == 2) v = next ? 0.875f * v0 + 0.125f * next[c] : v0;
+    else v = next ? 0.625f * v0 + 0.375f * next[c] : v0;
+    frames[(size_t)r * hidden + c] = v;
+}
+
+}  // namespace mt
+
+// ------------------------------------------------------------------------------------------------
+// C ABI
+// ------------------------------------------------------------------------------------------------
+using namespace mt;
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+extern "C" {
+
+mt_status mt_rmsnorm(mt_ctx* ctx, void* stream, const float* x, int ldx, int rows, int width,
+                     const mt_bf16* w, float* y, int ldy, float eps) {
+    MT_REQUIRE(ctx, ctx && x && w && y, MT_ERR_ARG, "mt_rmsnorm: null argument");
+    MT_REQUIRE(ctx, rows >= 0 && width > 0 && width % 4 == 0 && ldx % 4 == 0 && ldy % 4 == 0 &&
+                        ldx >= width && ldy >= width,
+               MT_ERR_SHAPE, "mt_rmsnorm: width %d ldx %d ldy %d (need width %% 4 == 0, ld >= width, ld %% 4 == 0)",
+               width, ldx, ldy);
+    MT_REQUIRE(ctx, aligned16(x) && aligned16(y) && ((uintptr_t)w & 7u) == 0, MT_ERR_ARG,
+               "mt_rmsnorm: x/y need 16-byte, w 8-byte alignment");
+    if (rows == 0) return MT_OK;
+    RmsArgs a{};
+    a.x = x; a.ldx = ldx; a.rows = rows; a.width = width; a.w = w; a.y = y; a.ldy = ldy; a.eps = eps;
+    launch_rmsnorm(a, as_stream(stream));
+    return check_launch(ctx, "mt_rmsnorm");
+}
+
+mt_status mt_copy(mt_ctx* ctx, void* stream, const float* x, int count, float* y) {
+    MT_REQUIRE(ctx, ctx && x && y, MT_ERR_ARG, "mt_copy: null argument");
+    MT_REQUIRE(ctx, count >= 0, MT_ERR_SHAPE, "mt_copy: count %d", count);
+    if (count == 0) return MT_OK;
+    int blocks = (count + 255) / 256;
+    if (blocks > 1024) blocks = 1024;
+    copy_kernel<<<blocks, 256, 0, as_stream(stream)>>>(x, count, y);
+    return check_launch(ctx, "mt_copy");
+}
+
+mt_status mt_rope_cache(mt_ctx* ctx, void* stream, float* qkv, int ldq, int m, int hq, int hkv,
+                        int pos0, float* k_cache, float* v_cache, int capacity, const float* inv_freq) {
+    MT_REQUIRE(ctx, ctx && qkv && k_cache && v_cache && inv_freq, MT_ERR_ARG, "mt_rope_cache: null argument");
+    MT_REQUIRE(ctx, m >= 0 && hq > 0 && hkv > 0 && hq % hkv == 0 && hq + 2 * hkv <= 32 && ldq >= (hq + 2 * hkv) * 64,
+               MT_ERR_SHAPE, "mt_rope_cache: hq %d hkv %d ldq %d", hq, hkv, ldq);
+    MT_REQUIRE(ctx, pos0 >= 0 && capacity > 0 && pos0 + m <= capacity, MT_ERR_CAPACITY,
+               "mt_rope_cache: positions %d..%d exceed capacity %d", pos0, pos0 + m, capacity);
+    if (m == 0) return MT_OK;
+    RopeArgs a{};
+    a.qkv = qkv; a.ldq = ldq; a.rows = m; a.rows_per_req = m; a.hq = hq; a.hkv = hkv; a.pos0 = pos0;
+    a.kc = k_cache; a.vc = v_cache; a.cap = capacity; a.inv_freq = inv_freq;
+    launch_rope_cache(a, as_stream(stream));
+    return check_launch(ctx, "mt_rope_cache");
+}
+
+mt_status mt_attention(mt_ctx* ctx, void* stream, const float* q, int ldq, int m, int hq, int hkv,
+                       int pos0, int window, const float* k_cache, const float* v_cache, int capacity,
+                       float* out, int ldo) {
+    MT_REQUIRE(ctx, ctx && q && k_cache && v_cache && out, MT_ERR_ARG, "mt_attention: null argument");
+    MT_REQUIRE(ctx, m >= 0 && hq > 0 && hkv > 0 && hq % hkv == 0 && hq / hkv <= 8 && ldq >= hq * 64 && ldo >= hq * 64 &&
+                        window >= 0 && ldq % 4 == 0,
+               MT_ERR_SHAPE, "mt_attention: hq %d hkv %d ldq %d ldo %d window %d", hq, hkv, ldq, ldo, window);
+    MT_REQUIRE(ctx, pos0 >= 0 && capacity > 0 && pos0 + m <= capacity, MT_ERR_CAPACITY,
+               "mt_attention: positions %d..%d exceed capacity %d", pos0, pos0 + m, capacity);
+    if (m == 0) return MT_OK;
+    const int max_keys = window > 0 ? (window < pos0 + m ? window : pos0 + m) : pos0 + m;
+    MT_REQUIRE(ctx, attention_smem(hq / hkv, max_keys) <= 200 * 1024, MT_ERR_SHAPE,
+               "mt_attention: %d keys exceed the shared-memory score buffer", max_keys);
+    MT_REQUIRE(ctx, aligned16(k_cache) && aligned16(v_cache), MT_ERR_ARG, "mt_attention: caches need 16-byte alignment");
+    AttnArgs a{};
+    a.q = q; a.ldq = ldq; a.rows = m; a.rows_per_req = m; a.hq = hq; a.hkv = hkv; a.pos0 = pos0;
+    a.window = window; a.kc = k_cache; a.vc = v_cache; a.cap = capacity; a.out = out; a.ldo = ldo;
+    a.max_keys = max_keys;
+    launch_attention(a, as_stream(stream));
+    return check_launch(ctx, "mt_attention");
+}
+
+mt_status mt_dit_attention(mt_ctx* ctx, void* stream, const float* qkv, int ld, int batch, int seq,
+                           int heads, const float* inv_freq, float* out, int ldo) {
+    MT_REQUIRE(ctx, ctx && qkv && inv_freq && out, MT_ERR_ARG, "mt_dit_attention: null argument");
+    MT_REQUIRE(ctx, seq >= 1 && seq <= 8, MT_ERR_SHAPE, "mt_dit_attention: seq %d (1..8)", seq);
+    MT_REQUIRE(ctx, batch >= 0 && heads > 0 && ld >= 3 * heads * 64 && ldo >= heads * 64 && ld % 2 == 0 && ldo % 2 == 0,
+               MT_ERR_SHAPE, "mt_dit_attention: heads %d ld %d ldo %d", heads, ld, ldo);
+    if (batch == 0) return MT_OK;
+    DitAttnArgs a{};
+    a.qkv = qkv; a.ld = ld; a.batch = batch; a.seq = seq; a.heads = heads; a.inv_freq = inv_freq;
+    a.out = out; a.ldo = ldo;
+    launch_dit_attention(a, as_stream(stream));
+    return check_launch(ctx, "mt_dit_attention");
+}
+
+mt_status mt_flow_assemble(mt_ctx* ctx, void* stream, const float* y, const float* history, const float* cemb,
+                           const mt_bf16* cond_bias, const float* temb, const mt_bf16* x_w, const mt_bf16* x_b,
+                           int hidden, int latent_dim, float* x) {
+    MT_REQUIRE(ctx, ctx && y && history && cemb && cond_bias && temb && x_w && x_b && x, MT_ERR_ARG,
+               "mt_flow_assemble: null argument");
+    MT_REQUIRE(ctx, hidden > 0 && latent_dim > 0, MT_ERR_SHAPE, "mt_flow_assemble: hidden %d latent %d", hidden, latent_dim);
+    flow_assemble_kernel<<<dim3((hidden + 255) / 256, 6), 256, 0, as_stream(stream)>>>(
+        y, history, cemb, cond_bias, temb, x_w, x_b, hidden, latent_dim, x);
+    return check_launch(ctx, "mt_flow_assemble");
+}
+
+mt_status mt_flow_euler(mt_ctx* ctx, void* stream, float* y, const float* pred, int ldp, int pred_row,
+                        int null_row, int latent_dim, float cfg, float dt, float* capture) {
+    MT_REQUIRE(ctx, ctx && y && pred, MT_ERR_ARG, "mt_flow_euler: null argument");
+    MT_REQUIRE(ctx, latent_dim > 0 && pred_row >= 0 && null_row >= 0 && ldp >= latent_dim, MT_ERR_SHAPE,
+               "mt_flow_euler: latent %d ldp %d", latent_dim, ldp);
+    flow_euler_kernel<<<(latent_dim + 255) / 256, 256, 0, as_stream(stream)>>>(y, pred, ldp, pred_row, null_row,
+                                                                           latent_dim, cfg, dt, capture);
+    return check_launch(ctx, "mt_flow_euler");
+}
+
+mt_status mt_upsample4(mt_ctx* ctx, void* stream, const float* prev, const float* cur, const float* next,
+                       int hidden, float* frames) {
+    MT_REQUIRE(ctx, ctx && cur && frames, MT_ERR_ARG, "mt_upsample4: null argument");
+    MT_REQUIRE(ctx, hidden > 0, MT_ERR_SHAPE, "mt_upsample4: hidden %d", hidden);
+    upsample4_kernel<<<dim3((hidden + 255) / 256, 4), 256, 0, as_stream(stream)>>>(prev, cur, next, hidden, frames);
+    return check_launch(ctx, "mt_upsample4");
+}
+
+}  // extern "C"

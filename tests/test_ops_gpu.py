@@ -1,0 +1,251 @@
+"""GPU parity of every operator entry point against the CPU oracle, through the C ABI.
+
+Shapes, seeds, NaN poisoning and tolerances follow the reference's kernel tests
+(Tests/MingTTSTests/KernelTests.swift): GEMV atol = 2e-4 * sqrt(K) / 30, rtol = 1e-4 (:102);
+RMSNorm 1e-5 (:202); attention 2e-5 (:267); ISTFT 2e-5 * max|y| (:378); upsample 1e-6 (:402).
+On top, every linear meets the parity bar: max|y - y_fp64| <= 1e-3 * max|y_fp64|.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import assert_close, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+class LCG:
+    """The reference test RNG (KernelTests.swift:21-28), as one stream across calls."""
+
+    def __init__(self, oracle, seed):
+        self.lib = oracle.lib()
+        self.state = ctypes.c_uint64(seed)
+
+    def floats(self, n, scale=1.0):
+        out = np.empty(n, np.float32)
+        self.lib.or_lcg_floats(ctypes.byref(self.state), out.ctypes.data, n, scale)
+        return out
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def gemv_case(ctx, mt, oracle, m, n, k, flags, bias, x_scale=1.0):
+    rng = LCG(oracle, m * 1000 + n * 7 + k)
+    x = np.concatenate([rng.floats(m * k, x_scale), np.full(8 * k, np.nan, np.float32)])
+    w = oracle.bf16_bits(rng.floats(n * k, 0.1))
+    w2 = oracle.bf16_bits(rng.floats(n * k, 0.1))
+    b = oracle.bf16_bits(rng.floats(n))
+    y0 = rng.floats(m * n)
+    f = flags | (mt.BIAS if bias else 0)
+    gated = bool(f & mt.SILU_GATE)
+    want = y0.copy()
+    oracle.linear(x, k, m, w, w2 if gated else None, b, n, k, want, n, f)
+    xd, wd, w2d, bd, yd = dev(x), dev(w), dev(w2), dev(b), dev(y0)
+    ctx.linear(xd, k, m, wd, w2d if gated else None, bd if bias else None, n, k, yd, n, f)
+    ctx.check()
+    got = host(yd)
+    what = f"linear m{m} n{n} k{k} flags {f} route {mt.lib().mt_linear_route(m, n, k)}"
+    assert_close(got.reshape(m, n), want.reshape(m, n), atol=2e-4 * np.sqrt(k) / 30, rtol=1e-4, what=what)
+    assert rel_err(got, want) <= 1e-3, what
+
+
+@pytest.mark.parametrize("m,n,k,flags,bias", [
+    (1, 1152, 896, 0, True), (2, 2, 896, 0, True), (4, 896, 4864, 2, False), (6, 4096, 1024, 4, True),
+    (3, 64, 1024, 0, True), (21, 300, 896, 0, False), (4, 3530, 896, 0, True), (1, 896, 64, 0, True),
+    (8, 2, 896, 0, True),
+])
+def test_gemv_shapes(ctx, mt, oracle, m, n, k, flags, bias):
+    gemv_case(ctx, mt, oracle, m, n, k, flags, bias)
+
+
+@pytest.mark.parametrize("m,n,k,flags,bias", [
+    (6, 1024, 1024, 4, True), (4, 896, 896, 8, False), (3, 1152, 896, 2, False), (6, 1024, 4096, 2, False),
+    (4, 896, 4864, 2, False), (2, 4864, 896, 0, False), (2, 896, 4864, 0, False), (2, 3072, 1024, 0, True),
+])
+def test_gemv_decode_shapes(ctx, mt, oracle, m, n, k, flags, bias):
+    gemv_case(ctx, mt, oracle, m, n, k, flags, bias)
+
+
+@pytest.mark.parametrize("m,n,k,flags,bias", [
+    (174, 1152, 896, 0, True), (40, 896, 4864, 2, False), (33, 4864, 896, 8, False), (16, 64, 32, 4, True),
+    (65, 128, 64, 16, True), (384, 3072, 1024, 0, True), (256, 3530, 896, 0, True), (130, 1024, 4096, 6, True),
+    (9, 200, 136, 8, False),
+])
+def test_tensor_core_shapes(ctx, mt, oracle, m, n, k, flags, bias):
+    assert mt.lib().mt_linear_route(m, n, k) == 1
+    gemv_case(ctx, mt, oracle, m, n, k, flags, bias)
+
+
+def test_gelu_silu_large_inputs(ctx, mt, oracle):
+    gemv_case(ctx, mt, oracle, 6, 256, 1024, mt.GELU, True, x_scale=8)
+    gemv_case(ctx, mt, oracle, 1, 256, 896, mt.SILU, False, x_scale=8)
+    gemv_case(ctx, mt, oracle, 24, 256, 1024, mt.GELU, True, x_scale=8)
+
+
+def test_silu_gate(ctx, mt, oracle):
+    gemv_case(ctx, mt, oracle, 1, 4864, 896, mt.SILU_GATE, False)
+    gemv_case(ctx, mt, oracle, 5, 256, 896, mt.SILU_GATE, False)
+
+
+def test_rmsnorm(ctx, mt, oracle):
+    rows, k = 5, 896
+    rng = LCG(oracle, 3)
+    x = rng.floats(rows * k, 3.0)
+    w = oracle.bf16_bits(rng.floats(k))
+    want = np.zeros_like(x)
+    oracle.rmsnorm(x, k, rows, k, w, want, k, 1e-6)
+    yd = dev(np.zeros_like(x))
+    ctx.rmsnorm(dev(x), k, rows, k, dev(w), yd, k, 1e-6)
+    ctx.check()
+    assert_close(host(yd), want, atol=1e-5, what="rmsnorm")
+
+
+def attention_case(ctx, oracle, t0, m, window):
+    hq, hkv, cap = 14, 2, 512
+    ld = (hq + 2 * hkv) * 64
+    rng = LCG(oracle, t0 * 31 + m + window)
+    total = t0 + m
+    qkv = rng.floats((total + 8) * ld)
+    inv = (1.0 / np.power(np.float32(1e6), np.arange(32, dtype=np.float32) * 2 / 64)).astype(np.float32)
+    kc, vc = np.zeros(hkv * cap * 64, np.float32), np.zeros(hkv * cap * 64, np.float32)
+    want = np.zeros(total * hq * 64, np.float32)
+    q_or = qkv.copy()
+    kcd, vcd, outd, qkvd, invd = dev(kc), dev(vc), dev(want), dev(qkv), dev(inv)
+    for pos0, rows in ((0, t0), (t0, m)):
+        if rows == 0:
+            continue
+        oracle.rope_cache(q_or[pos0 * ld:], ld, rows, hq, hkv, pos0, kc, vc, cap, inv)
+        oracle.attention(q_or[pos0 * ld:], ld, rows, hq, hkv, pos0, window, kc, vc, cap, want[pos0 * hq * 64:], hq * 64)
+        qv, ov = qkvd[pos0 * ld:], outd[pos0 * hq * 64:]
+        ctx.rope_cache(qv, ld, rows, hq, hkv, pos0, kcd, vcd, cap, invd)
+        ctx.attention(qv, ld, rows, hq, hkv, pos0, window, kcd, vcd, cap, ov, hq * 64)
+    ctx.check()
+    assert_close(host(outd), want, atol=2e-5, what=f"attention t0 {t0} m {m} window {window}")
+    assert_close(host(kcd), kc, atol=2e-6, what="k cache")
+    np.testing.assert_array_equal(host(vcd), vc)
+
+
+def test_attention_prefill_and_decode(ctx, oracle):
+    attention_case(ctx, oracle, 37, 1, 0)
+    attention_case(ctx, oracle, 130, 4, 0)
+    attention_case(ctx, oracle, 255, 2, 0)
+    attention_case(ctx, oracle, 510, 1, 0)
+
+
+def test_attention_sliding_window(ctx, oracle):
+    attention_case(ctx, oracle, 100, 4, 64)
+    attention_case(ctx, oracle, 20, 4, 64)
+    attention_case(ctx, oracle, 300, 4, 65)
+
+
+def test_dit_attention(ctx, oracle):
+    for B, S, H in ((2, 3, 16), (1, 2, 16), (3, 8, 4)):
+        D = H * 64
+        rng = LCG(oracle, 11)
+        qkv = rng.floats(B * S * 3 * D)
+        inv = (1.0 / np.power(np.float32(1e4), np.arange(32, dtype=np.float32) * 2 / 64)).astype(np.float32)
+        want = np.zeros(B * S * D, np.float32)
+        oracle.dit_attention(qkv, 3 * D, B, S, H, inv, want, D)
+        outd = dev(np.zeros_like(want))
+        ctx.dit_attention(dev(qkv), 3 * D, B, S, H, dev(inv), outd, D)
+        ctx.check()
+        assert_close(host(outd), want, atol=2e-5, what=f"dit attention B{B} S{S} H{H}")
+
+
+def test_istft_matches_direct_overlap_add(ctx, oracle):
+    nfft, hop, frames, ring = 3528, 882, 8, 8
+    bins = nfft // 2 + 1
+    rng = LCG(oracle, 5)
+    r = rng.floats(frames * bins * 2).reshape(frames, bins, 2)
+    spec = np.ascontiguousarray(np.concatenate([r[:, :, 0] * 2 - 1, r[:, :, 1] * 3], axis=1).astype(np.float32))
+    window = (0.5 - 0.5 * np.cos(2 * np.pi * np.arange(nfft) / nfft)).astype(np.float32)
+    pad = (nfft - hop) // 2
+    fr = np.zeros(ring * nfft, np.float32)
+    want = np.zeros(frames * hop, np.float32)
+    oracle.istft_frames(spec, 2 * bins, 4, nfft, window, fr, 0, ring)
+    oracle.istft_emit(fr, window, nfft, hop, 0, 4 * hop - pad, 3, ring, want)
+    oracle.istft_frames(np.ascontiguousarray(spec[4:]), 2 * bins, 4, nfft, window, fr, 4, ring)
+    oracle.istft_emit(fr, window, nfft, hop, 4 * hop - pad, 4 * hop, 7, ring, want[4 * hop - pad:])
+    oracle.istft_emit(fr, window, nfft, hop, 8 * hop - pad, pad, 7, ring, want[8 * hop - pad:])
+    specd, wd, frd, outd = dev(spec), dev(window), dev(np.zeros_like(fr)), dev(np.zeros_like(want))
+    c = ctx.call
+    c("istft_frames", specd, 2 * bins, 4, nfft, None, wd, frd, 0, ring)
+    c("istft_emit", frd, wd, nfft, hop, 0, 4 * hop - pad, 3, ring, outd)
+    c("istft_frames", specd[4 * 2 * bins:], 2 * bins, 4, nfft, None, wd, frd, 4, ring)
+    c("istft_emit", frd, wd, nfft, hop, 4 * hop - pad, 4 * hop, 7, ring, outd[4 * hop - pad:])
+    c("istft_emit", frd, wd, nfft, hop, 8 * hop - pad, pad, 7, ring, outd[8 * hop - pad:])
+    ctx.check()
+    got = host(outd)
+    assert_close(got, want, atol=2e-5 * np.abs(want).max(), rtol=1e-4, what="istft")
+    assert_close(host(frd), fr, atol=2e-5 * np.abs(fr).max(), rtol=1e-4, what="istft frames")
+
+
+def test_upsample(ctx, oracle):
+    hidden, n = 896, 5
+    rng = LCG(oracle, 9)
+    h = [rng.floats(hidden) for _ in range(n)]
+    hd = [dev(v) for v in h]
+    for i in range(n):
+        want = np.zeros(4 * hidden, np.float32)
+        oracle.upsample4(h[i - 1] if i > 0 else None, h[i], h[i + 1] if i + 1 < n else None, hidden, want)
+        outd = dev(np.zeros_like(want))
+        ctx.call("upsample4", hd[i - 1] if i > 0 else None, hd[i], hd[i + 1] if i + 1 < n else None, hidden, outd)
+        ctx.check()
+        assert_close(host(outd), want, atol=1e-6, what=f"upsample {i}")
+
+
+def test_flow_assemble_and_euler(ctx, oracle):
+    hidden, L = 1024, 64
+    rs = np.random.default_rng(1)
+    y, hist = rs.standard_normal(L).astype(np.float32), rs.standard_normal(L).astype(np.float32)
+    cemb, temb = rs.standard_normal(hidden).astype(np.float32), rs.standard_normal(hidden).astype(np.float32)
+    cbias = oracle.bf16_bits(0.02 * rs.standard_normal(hidden).astype(np.float32))
+    xw = oracle.bf16_bits(0.02 * rs.standard_normal(hidden * L).astype(np.float32))
+    xb = oracle.bf16_bits(0.02 * rs.standard_normal(hidden).astype(np.float32))
+    want = np.zeros(6 * hidden, np.float32)
+    oracle.flow_assemble(y, hist, cemb, cbias, temb, xw, xb, hidden, L, want)
+    xd = dev(np.zeros_like(want))
+    ctx.call("flow_assemble", dev(y), dev(hist), dev(cemb), dev(cbias), dev(temb), dev(xw), dev(xb), hidden, L, xd)
+    ctx.check()
+    assert_close(host(xd), want, atol=1e-5, what="flow_assemble")
+    pred = rs.standard_normal(6 * L).astype(np.float32)
+    y_or, cap = y.copy(), np.zeros(2 * L, np.float32)
+    oracle.flow_euler(y_or, pred, L, 2, 5, L, 2.0, 0.0625, cap)
+    yd, capd = dev(y), dev(np.zeros(2 * L, np.float32))
+    ctx.call("flow_euler", yd, dev(pred), L, 2, 5, L, 2.0, 0.0625, capd)
+    ctx.check()
+    assert_close(host(yd), y_or, atol=1e-6, what="euler")
+    np.testing.assert_array_equal(host(capd), cap)
+
+
+def test_device_randn_matches_host(ctx, mt, oracle):
+    import torch
+    n = 1_000_003
+    host_bits = oracle.randn_bf16(n, 77, 0.02)
+    d = torch.empty(n, dtype=torch.int16, device="cuda")
+    ctx.call("randn_bf16", d, n, 77, 0.02)
+    ctx.check()
+    got = host(d).view(np.uint16)
+    mismatch = int((got != host_bits).sum())
+    # Device and host log/sin/cos may differ in the last double ulp; that reaches a bf16 bit almost never.
+    assert mismatch <= 2, f"{mismatch} of {n} bf16 values differ"
+
+
+def test_copy(ctx):
+    x = np.arange(1000, dtype=np.float32)
+    yd = dev(np.zeros_like(x))
+    ctx.call("copy", dev(x), 1000, yd)
+    ctx.check()
+    np.testing.assert_array_equal(host(yd), x)
