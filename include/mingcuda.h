@@ -180,6 +180,14 @@ mt_status mt_linear(mt_ctx* ctx, void* stream, const float* x, int ldx, int m,
                     const mt_bf16* w, const mt_bf16* w2, const mt_bf16* bias, int n, int k,
                     float* y, int ldy, uint32_t flags);
 
+/* The tensor-core form of mt_linear with the activations already split into bf16 planes,
+ * x ~= x_hi + x_lo (row stride ld_x elements): the form the engine's producers write. Outputs: fp32 y
+ * (row stride ldy) and/or bf16 hi/lo planes (row stride ld_ysplit; NULL to skip). Same flags and
+ * epilogue as mt_linear; any m >= 1, k % 8 == 0. Replaces the tiled GEMM (Shaders.swift:304-408). */
+mt_status mt_linear_split(mt_ctx* ctx, void* stream, const mt_bf16* x_hi, const mt_bf16* x_lo, int ld_x, int m,
+                          const mt_bf16* w, const mt_bf16* w2, const mt_bf16* bias, int n, int k, float* y, int ldy,
+                          mt_bf16* y_hi, mt_bf16* y_lo, int ld_ysplit, uint32_t flags);
+
 /* y = x * rsqrt(mean(x^2) + eps) * w per row. Replaces Encoder.rmsnorm (Kernels.swift:163-171),
  * kernel rmsnorm (Shaders.swift:418-441). width % 4 == 0. */
 mt_status mt_rmsnorm(mt_ctx* ctx, void* stream, const float* x, int ldx, int rows, int width,
@@ -240,6 +248,96 @@ mt_status mt_istft_frames(mt_ctx* ctx, void* stream, const float* spec, int ld_s
  * (Shaders.swift:770-788). count == 0 is a no-op. */
 mt_status mt_istft_emit(mt_ctx* ctx, void* stream, const float* frames, const float* window,
                         int nfft, int hop, int s0, int count, int last_frame, int ring, float* out);
+
+/* ---------------------------------------------------------------------------------------------
+ * Model: one device arena holding every weight, described by a tensor table
+ * (replaces WeightArena + the *Weights structs, Sources/MingTTS/Engine/Weights.swift:8-263)
+ * ------------------------------------------------------------------------------------------- */
+
+enum { MT_DTYPE_BF16 = 0, MT_DTYPE_F32 = 1 };
+enum { MT_INIT_NORMAL = 0, MT_INIT_ONES = 1, MT_INIT_INV_FREQ = 2, MT_INIT_HANN = 3 };
+
+typedef struct {
+    char name[96];     /* checkpoint tensor name; q/k/v are one tensor "...qkv_proj" / "...to_qkv" */
+    size_t offset;     /* bytes from the arena base, 256-byte aligned */
+    size_t numel;
+    int dtype;         /* MT_DTYPE_* */
+    int init;          /* MT_INIT_* used by mt_model_create_random */
+    float std;         /* MT_INIT_NORMAL: standard deviation (0.02) */
+    uint64_t seed;     /* MT_INIT_NORMAL: stream seed of mt_randn_bf16 */
+} mt_tensor_info;
+
+/* Ming-3.0-tts-0.5B dimensions (Weights.swift:81-95, 145-148, 174-225; Engine.swift:91-92). */
+void mt_model_config_default(mt_model_config* cfg);
+/* Fills up to `cap` entries of the tensor table (if out != NULL); returns the tensor count. */
+int mt_model_tensors(const mt_model_config* cfg, uint64_t seed, int with_embeddings, mt_tensor_info* out, int cap);
+size_t mt_model_arena_bytes(const mt_model_config* cfg, int with_embeddings);
+/* Allocates the arena and fills it: bf16 N(0, 0.02) from per-tensor seeds, norm gains 1.0,
+ * DiT rotary inv_freq 1/10000^(2i/64), periodic Hann ISTFT window. */
+mt_status mt_model_create_random(mt_ctx* ctx, const mt_model_config* cfg, uint64_t seed, int with_embeddings,
+                                 mt_model** out);
+/* Wraps a caller-owned device arena laid out as mt_model_tensors describes (e.g. a loaded checkpoint). */
+mt_status mt_model_create_from_arena(mt_ctx* ctx, const mt_model_config* cfg, void* device_arena,
+                                     int with_embeddings, mt_model** out);
+const mt_model_weights* mt_model_get_weights(const mt_model* model);
+const mt_model_config* mt_model_get_config(const mt_model* model);
+mt_status mt_model_arena(const mt_model* model, void** ptr, size_t* bytes);
+void mt_model_destroy(mt_model* model);
+
+/* ---------------------------------------------------------------------------------------------
+ * Engine: the generation loop for R concurrent requests on one GPU
+ * (MingEngine.generate / encodeStep, Engine.swift:302-415; VAEDecoder, VAEDecoder.swift:64-107)
+ * ------------------------------------------------------------------------------------------- */
+
+typedef struct {
+    int max_requests;  /* R capacity */
+    int max_prompt;    /* prompt rows per request (all requests of a generation share it) */
+    int max_steps;     /* generation steps; prompt + steps <= llm_capacity */
+    int vae_ring;      /* VAE KV-cache ring positions (0 = 128); must be >= window + 3 */
+    int use_graphs;    /* 1: replay steady-state steps from a captured CUDA graph */
+} mt_engine_options;
+
+/* Buffers readable after a step (device pointers, request-major). */
+enum {
+    MT_BUF_Z = 0,          /* [R, llm.hidden]    LLM final-norm output of the last step */
+    MT_BUF_STOP_LOGITS,    /* [R, 2]             stop-head logits of the last step */
+    MT_BUF_LATENTS,        /* [R, max_steps, latent] every latent so far */
+    MT_BUF_AGG_OUT,        /* [R, llm.hidden]    aggregator output = next LLM input */
+    MT_BUF_VELOCITY0,      /* [R, flow_steps, 2, latent] step-0 cond/uncond DiT outputs */
+    MT_BUF_VAE_HIDDEN,     /* [R, 4, vae.hidden] decoder final-norm rows of the last decoded latent */
+    MT_BUF_PCM             /* [R, max_chunk]     samples of the last emission */
+};
+
+mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_options* opt, mt_engine** out);
+void mt_engine_destroy(mt_engine* engine);
+/* Starts a generation of `requests` requests with `prompt_rows` prompt rows each. Inputs are device
+ * pointers: embeds [R, T, llm.hidden] fp32, or token_ids [R, T] (int32, gathered from embed_tokens)
+ * when embeds is NULL; noise [R, steps, latent]; initial_history [R, latent] or NULL (zeros).
+ * Resets the KV caches and VAE counters (Engine.swift:312-317). */
+mt_status mt_engine_begin(mt_engine* engine, void* stream, int requests, int prompt_rows, const float* embeds,
+                          const int32_t* token_ids, const float* noise, const float* initial_history, int steps,
+                          float cfg);
+/* Prompt prefill (Engine.swift:323-333). */
+mt_status mt_engine_prefill(mt_engine* engine, void* stream);
+/* Enqueues generation step n (the next one): LLM token (n > 0), stop head, flow head, aggregator,
+ * VAE fc1, and the VAE frames of latent n-2 on a second stream. *pcm_count = samples per request
+ * this step emits into MT_BUF_PCM (0 before step 2). Returns after enqueueing (no host sync). */
+mt_status mt_engine_step(mt_engine* engine, void* stream, int* pcm_count);
+/* After the last step: decodes one remaining latent per call (Engine.swift:360-367);
+ * *pcm_count = 0 once everything is decoded. */
+mt_status mt_engine_flush(mt_engine* engine, void* stream, int* pcm_count);
+mt_status mt_engine_buffer(const mt_engine* engine, int which, const float** ptr, long long* request_stride);
+/* Steps enqueued so far in this generation. */
+int mt_engine_steps_done(const mt_engine* engine);
+/* Kernels the last mt_engine_step enqueued (all streams). */
+int mt_engine_step_kernels(const mt_engine* engine);
+/* End to end from host memory: copies embeds (or ids) and noise in, runs prefill, `steps` steps
+ * and the flush, and copies every PCM chunk and stop probability out. pcm_host is [R, pcm_stride];
+ * pcm_count receives the samples written per request (the same for all). The stop head is
+ * evaluated every step; generation runs all `steps` (stop not obeyed). */
+mt_status mt_engine_generate(mt_engine* engine, void* stream, int requests, int prompt_rows, const float* embeds_host,
+                             const int32_t* ids_host, const float* noise_host, int steps, float cfg, float* pcm_host,
+                             long long pcm_stride, long long* pcm_count, float* stop_prob_host);
 
 /* ---------------------------------------------------------------------------------------------
  * Synthetic data (seeded random-init weights and noise)

@@ -5,8 +5,8 @@ mirrors its structs. Torch tensors are accepted wherever the ABI takes a device 
 current torch stream is passed as the CUDA stream. There is no CPU fallback: every compute call
 goes to the CUDA library, and importing fails loudly if the library has not been built.
 
-The directory is named ``ming-tts_b200``; import it with ``load_package()`` from ``_loader.py`` or
-register it under the module name ``mingtts_b200``.
+The directory is named ``ming-tts_b200``; tests/conftest.py, bench.py and __graft_entry__.py import it
+under the module name ``mingtts_b200`` with importlib.
 """
 from __future__ import annotations
 
@@ -81,6 +81,20 @@ class ModelWeights(ctypes.Structure):
                 ("embed_tokens", c_void_p)]
 
 
+class TensorInfo(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 96), ("offset", c_size_t), ("numel", c_size_t), ("dtype", c_int),
+                ("init", c_int), ("std", c_float), ("seed", c_uint64)]
+
+
+class EngineOptions(ctypes.Structure):
+    _fields_ = [("max_requests", c_int), ("max_prompt", c_int), ("max_steps", c_int), ("vae_ring", c_int),
+                ("use_graphs", c_int)]
+
+
+MT_DTYPE_BF16, MT_DTYPE_F32 = 0, 1
+BUF_Z, BUF_STOP_LOGITS, BUF_LATENTS, BUF_AGG_OUT, BUF_VELOCITY0, BUF_VAE_HIDDEN, BUF_PCM = range(7)
+
+
 # ------------------------------------------------------------------------------------------------
 # Library loading and prototypes
 # ------------------------------------------------------------------------------------------------
@@ -94,6 +108,8 @@ PROTOTYPES = {
     "mt_ctx_check": (c_int, [_P, _P]),
     "mt_linear_route": (c_int, [c_int, c_int, c_int]),
     "mt_linear": (c_int, [_P, _P, _P, c_int, c_int, _P, _P, _P, c_int, c_int, _P, c_int, c_uint32]),
+    "mt_linear_split": (c_int, [_P, _P, _P, _P, c_int, c_int, _P, _P, _P, c_int, c_int, _P, c_int, _P, _P, c_int,
+                                c_uint32]),
     "mt_rmsnorm": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P, _P, c_int, c_float]),
     "mt_copy": (c_int, [_P, _P, _P, c_int, _P]),
     "mt_rope_cache": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, _P, c_int, _P]),
@@ -104,6 +120,26 @@ PROTOTYPES = {
     "mt_upsample4": (c_int, [_P, _P, _P, _P, _P, c_int, _P]),
     "mt_istft_frames": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P, _P, _P, c_int, c_int]),
     "mt_istft_emit": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P]),
+    "mt_model_config_default": (None, [POINTER(ModelConfig)]),
+    "mt_model_tensors": (c_int, [POINTER(ModelConfig), c_uint64, c_int, _P, c_int]),
+    "mt_model_arena_bytes": (c_size_t, [POINTER(ModelConfig), c_int]),
+    "mt_model_create_random": (c_int, [_P, POINTER(ModelConfig), c_uint64, c_int, POINTER(c_void_p)]),
+    "mt_model_create_from_arena": (c_int, [_P, POINTER(ModelConfig), _P, c_int, POINTER(c_void_p)]),
+    "mt_model_get_weights": (_P, [_P]),
+    "mt_model_get_config": (_P, [_P]),
+    "mt_model_arena": (c_int, [_P, POINTER(c_void_p), POINTER(c_size_t)]),
+    "mt_model_destroy": (None, [_P]),
+    "mt_engine_create": (c_int, [_P, _P, POINTER(EngineOptions), POINTER(c_void_p)]),
+    "mt_engine_destroy": (None, [_P]),
+    "mt_engine_begin": (c_int, [_P, _P, c_int, c_int, _P, _P, _P, _P, c_int, c_float]),
+    "mt_engine_prefill": (c_int, [_P, _P]),
+    "mt_engine_step": (c_int, [_P, _P, POINTER(c_int)]),
+    "mt_engine_flush": (c_int, [_P, _P, POINTER(c_int)]),
+    "mt_engine_buffer": (c_int, [_P, c_int, POINTER(c_void_p), POINTER(ctypes.c_longlong)]),
+    "mt_engine_steps_done": (c_int, [_P]),
+    "mt_engine_step_kernels": (c_int, [_P]),
+    "mt_engine_generate": (c_int, [_P, _P, c_int, c_int, _P, _P, _P, c_int, c_float, _P, ctypes.c_longlong,
+                                   POINTER(ctypes.c_longlong), _P]),
     "mt_gaussian_noise_host": (None, [_P, c_size_t, c_uint64]),
     "mt_randn_bf16_host": (None, [_P, c_size_t, c_uint64, c_float]),
     "mt_randn_bf16": (c_int, [_P, _P, _P, c_size_t, c_uint64, c_float]),
@@ -203,3 +239,223 @@ class Context:
 
 def version() -> str:
     return lib().mt_version().decode()
+
+
+# ------------------------------------------------------------------------------------------------
+# Model and engine
+# ------------------------------------------------------------------------------------------------
+def default_config() -> ModelConfig:
+    c = ModelConfig()
+    lib().mt_model_config_default(ctypes.byref(c))
+    return c
+
+
+def small_config() -> ModelConfig:
+    """A reduced model with the same block structure, for fast CPU-oracle parity runs."""
+    c = default_config()
+    c.llm.hidden, c.llm.heads, c.llm.kv_heads, c.llm.intermediate, c.llm.layers = 128, 2, 1, 256, 2
+    c.vae.hidden, c.vae.heads, c.vae.kv_heads, c.vae.intermediate, c.vae.layers = 128, 2, 1, 256, 2
+    c.flow.hidden, c.flow.heads, c.flow.depth, c.flow.ff = 128, 2, 2, 256
+    c.agg.hidden, c.agg.heads, c.agg.depth, c.agg.ff, c.agg.out_dim = 128, 2, 2, 256, 128
+    c.vocab, c.nfft, c.hop = 1000, 256, 64
+    return c
+
+
+def tensor_table(cfg: ModelConfig, seed: int = 0, with_embeddings: bool = True) -> list[TensorInfo]:
+    n = lib().mt_model_tensors(ctypes.byref(cfg), seed, int(with_embeddings), None, 0)
+    arr = (TensorInfo * n)()
+    lib().mt_model_tensors(ctypes.byref(cfg), seed, int(with_embeddings), arr, n)
+    return list(arr)
+
+
+def weights_struct(cfg: ModelConfig, base: int, tensors: list[TensorInfo]):
+    """mt_model_weights over an arena at address `base` (device or host) laid out as `tensors`.
+    Returns (struct, keepalive) -- keep both alive while the struct is in use."""
+    off = {t.name.decode(): t.offset for t in tensors}
+
+    def at(name):
+        return base + off[name] if name in off else None
+
+    keep = []
+
+    def qwen(prefix, qc):
+        layers = (QwenLayer * qc.layers)()
+        for l in range(qc.layers):
+            p = f"{prefix}.layers.{l}"
+            layers[l] = QwenLayer(at(p + ".input_layernorm.weight"), at(p + ".self_attn.qkv_proj.weight"),
+                                  at(p + ".self_attn.qkv_proj.bias"), at(p + ".self_attn.o_proj.weight"),
+                                  at(p + ".post_attention_layernorm.weight"), at(p + ".mlp.gate_proj.weight"),
+                                  at(p + ".mlp.up_proj.weight"), at(p + ".mlp.down_proj.weight"))
+        keep.append(layers)
+        return QwenWeights(qc, ctypes.cast(layers, POINTER(QwenLayer)), at(prefix + ".norm.weight"))
+
+    def dit(prefix, dc):
+        blocks = (DitBlock * dc.depth)()
+        for i in range(dc.depth):
+            p = f"{prefix}.blocks.{i}"
+            blocks[i] = DitBlock(at(p + ".norm1.weight"), at(p + ".attn.to_qkv.weight"), at(p + ".attn.to_qkv.bias"),
+                                 at(p + ".attn.to_out.0.weight"), at(p + ".attn.to_out.0.bias"),
+                                 at(p + ".norm2.weight"), at(p + ".mlp.ff.0.0.weight"), at(p + ".mlp.ff.0.0.bias"),
+                                 at(p + ".mlp.ff.2.weight"), at(p + ".mlp.ff.2.bias"))
+        keep.append(blocks)
+        return DitWeights(dc, ctypes.cast(blocks, POINTER(DitBlock)), at(prefix + ".final_layer.norm_final.weight"),
+                          at(prefix + ".final_layer.linear.weight"), at(prefix + ".final_layer.linear.bias"),
+                          at(prefix + ".rotary_embed.inv_freq"))
+
+    f, a, v = "flowloss.cfm.model", "linear_proj_audio", "audio.decoder"
+    w = ModelWeights()
+    w.llm = qwen("model.model", cfg.llm)
+    w.stop_w, w.stop_b = at("stop_head.weight"), at("stop_head.bias")
+    w.flow_x_w, w.flow_x_b = at(f + ".x_embedder.weight"), at(f + ".x_embedder.bias")
+    w.flow_c_w, w.flow_c_b = at(f + ".c_embedder.cond_embedder.weight"), at(f + ".c_embedder.cond_embedder.bias")
+    w.flow_t1_w, w.flow_t1_b = at(f + ".t_embedder.time_mlp.0.weight"), at(f + ".t_embedder.time_mlp.0.bias")
+    w.flow_t2_w, w.flow_t2_b = at(f + ".t_embedder.time_mlp.2.weight"), at(f + ".t_embedder.time_mlp.2.bias")
+    w.flow = dit(f, cfg.flow)
+    w.agg_x_w, w.agg_x_b, w.agg_cls = at(a + ".x_embedder.weight"), at(a + ".x_embedder.bias"), at(a + ".word_embedder.weight")
+    w.agg = dit(a, cfg.agg)
+    w.vae_fc1_w, w.vae_fc1_b = at(v + ".fc1.weight"), at(v + ".fc1.bias")
+    w.vae = qwen(v + ".decoder", cfg.vae)
+    w.vae_head_w, w.vae_head_b = at(v + ".head.out.weight"), at(v + ".head.out.bias")
+    w.vae_window = at(v + ".head.istft.window")
+    w.embed_tokens = at("model.model.embed_tokens.weight")
+    return w, keep
+
+
+class Model:
+    """An mt_model with a device arena (random-init from `seed`)."""
+
+    def __init__(self, ctx: Context, cfg: ModelConfig | None = None, seed: int = 1, with_embeddings: bool = True):
+        self.ctx = ctx
+        self.cfg = cfg if cfg is not None else default_config()
+        self.seed = seed
+        self.with_embeddings = with_embeddings
+        self._m = c_void_p()
+        ctx._check(lib().mt_model_create_random(ctx.handle, ctypes.byref(self.cfg), seed, int(with_embeddings),
+                                                ctypes.byref(self._m)), "mt_model_create_random")
+
+    @property
+    def handle(self):
+        return self._m
+
+    def arena(self):
+        p, n = c_void_p(), c_size_t()
+        lib().mt_model_arena(self._m, ctypes.byref(p), ctypes.byref(n))
+        return p.value, n.value
+
+    def tensors(self):
+        return tensor_table(self.cfg, self.seed, self.with_embeddings)
+
+    def arena_to_host(self):
+        """Host numpy uint8 copy of the device arena."""
+        import numpy as np
+        p, nbytes = self.arena()
+        return device_to_numpy(p, (nbytes,), np.uint8)
+
+    def close(self):
+        if self._m:
+            lib().mt_model_destroy(self._m)
+            self._m = c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class _DeviceView:
+    """Exposes a raw device pointer through __cuda_array_interface__ (zero-copy view for torch)."""
+
+    def __init__(self, address: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (address, False),
+                                         "version": 3, "strides": None}
+
+
+def device_view(address: int, shape, dtype="float32"):
+    """A torch CUDA tensor viewing library-owned device memory (no copy)."""
+    import numpy as np
+    import torch
+    return torch.as_tensor(_DeviceView(address, shape, np.dtype(dtype).str), device="cuda")
+
+
+def device_to_numpy(address: int, shape, dtype="float32"):
+    """Copies library-owned device memory into a new numpy array."""
+    import torch
+    torch.cuda.synchronize()
+    return device_view(address, shape, dtype).cpu().numpy().copy()
+
+
+class Engine:
+    """mt_engine: the generation loop for R concurrent requests."""
+
+    def __init__(self, ctx: Context, model: Model, max_requests: int, max_prompt: int, max_steps: int,
+                 use_graphs: bool = True, vae_ring: int = 0):
+        self.ctx, self.model = ctx, model
+        self.opt = EngineOptions(max_requests, max_prompt, max_steps, vae_ring, int(use_graphs))
+        self._e = c_void_p()
+        ctx._check(lib().mt_engine_create(ctx.handle, model.handle, ctypes.byref(self.opt), ctypes.byref(self._e)),
+                   "mt_engine_create")
+
+    @property
+    def handle(self):
+        return self._e
+
+    def begin(self, requests, prompt_rows, embeds=None, token_ids=None, noise=None, initial_history=None, steps=1,
+              cfg=2.0, stream=None):
+        self.ctx._check(lib().mt_engine_begin(self._e, stream if stream is not None else current_stream(), requests,
+                                              prompt_rows, ptr(embeds), ptr(token_ids), ptr(noise),
+                                              ptr(initial_history), steps, cfg), "mt_engine_begin")
+
+    def prefill(self, stream=None):
+        self.ctx._check(lib().mt_engine_prefill(self._e, stream if stream is not None else current_stream()),
+                        "mt_engine_prefill")
+
+    def step(self, stream=None) -> int:
+        cnt = c_int()
+        self.ctx._check(lib().mt_engine_step(self._e, stream if stream is not None else current_stream(),
+                                             ctypes.byref(cnt)), "mt_engine_step")
+        return cnt.value
+
+    def flush(self, stream=None) -> int:
+        cnt = c_int()
+        self.ctx._check(lib().mt_engine_flush(self._e, stream if stream is not None else current_stream(),
+                                              ctypes.byref(cnt)), "mt_engine_flush")
+        return cnt.value
+
+    def buffer(self, which: int):
+        p, stride = c_void_p(), ctypes.c_longlong()
+        self.ctx._check(lib().mt_engine_buffer(self._e, which, ctypes.byref(p), ctypes.byref(stride)),
+                        "mt_engine_buffer")
+        return p.value, stride.value
+
+    def read(self, which: int, requests: int, count: int | None = None):
+        """Host copy [requests, count] of an engine buffer (count defaults to the request stride)."""
+        import numpy as np
+        p, stride = self.buffer(which)
+        full = device_to_numpy(p, (requests, stride))
+        return full if count is None else np.ascontiguousarray(full[:, :count])
+
+    def generate(self, requests, prompt_rows, noise_host, steps, cfg=2.0, embeds_host=None, ids_host=None,
+                 stream=None):
+        import numpy as np
+        c = self.model.cfg
+        stride = 4 * c.hop * steps
+        pcm = np.zeros((requests, stride), np.float32)
+        stop = np.zeros((requests, steps), np.float32)
+        cnt = ctypes.c_longlong()
+        self.ctx._check(lib().mt_engine_generate(self._e, stream if stream is not None else current_stream(), requests,
+                                                 prompt_rows, ptr(embeds_host), ptr(ids_host), ptr(noise_host), steps,
+                                                 cfg, ptr(pcm), stride, ctypes.byref(cnt), ptr(stop)),
+                        "mt_engine_generate")
+        return pcm[:, :cnt.value], stop
+
+    def close(self):
+        if self._e:
+            lib().mt_engine_destroy(self._e)
+            self._e = c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,791 @@
+// engine.cu -- the generation loop of Ming-3.0-tts-0.5B for R concurrent requests on one GPU.
+//
+// Restates MingEngine.generate / encodeStep (Sources/MingTTS/Engine/Engine.swift:302-415),
+// QwenForward.dispatches (Qwen.swift:72-97), DiTForward.encode (DiT.swift:35-52), the streaming
+// VAEDecoder (VAEDecoder.swift:64-107) and the temb precompute (Engine.swift:187-198).
+//
+// B200 layout: every request's rows are stacked, so each projection is one GEMM over all requests
+// (LLM R rows, flow DiT 6R, aggregator 2R, VAE 4R, prefill R*T). Row counts <= 8 use the
+// CUDA-core GEMV on fp32 activations; larger ones the tcgen05 GEMM on bf16 hi/lo planes, which
+// the producing kernels (RMSNorm, attention, the gated/GELU epilogues) write directly.
+// Stream A runs LLM token n -> stop head -> flow head -> aggregator -> VAE fc1; stream B decodes
+// the VAE frames of latent n-2 concurrently (the reference pairs the same two stacks on one
+// concurrent encoder, Qwen.swift:103-114). Step-dependent values live in a device step state
+// filled from pinned memory, so steady-state steps replay one captured CUDA graph.
+#include <math.h>
+#include <string.h>
+
+#include <vector>
+
+#include "common.cuh"
+#include "engine_kernels.cuh"
+#include "kernels.cuh"
+
+namespace mt {
+
+static const int kGemvMax = 8;  // rows at or below which linears use the CUDA-core GEMV
+static thread_local int g_kernels = 0;  // kernels enqueued by the current engine call
+
+struct Act {  // activation matrix with fp32 and bf16 hi/lo representations
+    float* f = nullptr;
+    uint16_t* hi = nullptr;
+    uint16_t* lo = nullptr;
+    int ld = 0;
+};
+
+struct Lin {
+    bool tc = false;
+    LinearArgs g{};
+    GemmPlan p{};
+};
+
+struct QwenLayerPlans { Lin qkv, o, gu, down; };
+struct DitBlockPlans { Lin qkv, out, ff1, ff2; };
+
+struct DitBufs {
+    float* x = nullptr;  // residual [rows, hidden]
+    Act norm, attn, ff;
+    float* qkv = nullptr;
+};
+
+struct QwenBufs {
+    float* x = nullptr;  // residual
+    Act norm, attn, mlp;
+    float* qkv = nullptr;
+    float* kv = nullptr;  // [R][layers][2][kv][cap][64]
+    int cap = 0;
+    float* inv_freq = nullptr;  // [32]
+};
+
+}  // namespace mt
+
+using namespace mt;
+
+struct mt_engine {
+    mt_ctx* ctx = nullptr;
+    const mt_model* model = nullptr;
+    mt_model_config cfg{};
+    mt_model_weights w{};
+    mt_engine_options opt{};
+    std::vector<void*> allocs;
+    std::vector<float> timesteps;
+
+    // Buffers.
+    QwenBufs llm, vae;
+    Act z;
+    float* stop = nullptr;
+    float* temb = nullptr;
+    float* cemb = nullptr;
+    float *y = nullptr, *hist = nullptr, *noise = nullptr, *latents = nullptr, *vel0 = nullptr;
+    DitBufs flow, agg;
+    Act agg_norm;
+    float* vae_h = nullptr;
+    Act vae_hidden;
+    float* spec = nullptr;
+    float* fring = nullptr;
+    float* pcm = nullptr;
+    int max_chunk = 0;
+    int* state_dev = nullptr;
+    int* state_host = nullptr;  // pinned
+
+    // Current generation.
+    int R = 0, T = 0, steps = 0;
+    float cfg_scale = 2.0f;
+    int n = 0;          // steps enqueued
+    int latents_fed = 0, decoded = 0, emitted = 0;
+    bool begun = false, prefilled = false;
+
+    // Plans for the current (R, T).
+    int plan_R = -1, plan_T = -1;
+    std::vector<QwenLayerPlans> llm_dec, llm_pre, vae_layers;
+    std::vector<DitBlockPlans> flow_blocks, agg_blocks;
+    Lin cond, agg_final, vae_head, stop_lin;
+
+    cudaStream_t sb = nullptr;  // VAE stream
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    int step_kernels = 0;       // kernels of the last step
+    int graph_kernels = 0;      // kernels in the captured step graph
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+    cudaStream_t graph_stream = nullptr;
+};
+
+namespace {
+
+template <typename T>
+mt_status dalloc(mt_engine* e, T** p, size_t count) {
+    *p = nullptr;
+    if (count == 0) count = 1;
+    cudaError_t err = cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T));
+    if (err != cudaSuccess) return fail(e->ctx, MT_ERR_NOMEM, "engine: cudaMalloc of %zu bytes: %s", count * sizeof(T),
+                                        cudaGetErrorString(err));
+    cudaMemset(*p, 0, count * sizeof(T));
+    e->allocs.push_back(*p);
+    return MT_OK;
+}
+
+mt_status act_alloc(mt_engine* e, Act* a, size_t rows, int cols) {
+    a->ld = cols;
+    mt_status st = dalloc(e, &a->f, rows * cols);
+    if (st == MT_OK) st = dalloc(e, &a->hi, rows * cols);
+    if (st == MT_OK) st = dalloc(e, &a->lo, rows * cols);
+    return st;
+}
+
+#define TRY(expr)                            \
+    do {                                     \
+        mt_status _st = (expr);              \
+        if (_st != MT_OK) return _st;        \
+    } while (0)
+
+mt_status qwen_alloc(mt_engine* e, QwenBufs* q, const mt_qwen_config& c, size_t rows, int requests, int cap) {
+    const int qkvw = (c.heads + 2 * c.kv_heads) * 64;
+    TRY(dalloc(e, &q->x, rows * c.hidden));
+    TRY(act_alloc(e, &q->norm, rows, c.hidden));
+    TRY(act_alloc(e, &q->attn, rows, c.heads * 64));
+    TRY(act_alloc(e, &q->mlp, rows, c.intermediate));
+    TRY(dalloc(e, &q->qkv, rows * qkvw));
+    q->cap = cap;
+    TRY(dalloc(e, &q->kv, (size_t)requests * c.layers * 2 * c.kv_heads * cap * 64));
+    TRY(dalloc(e, &q->inv_freq, 32));
+    float inv[32];
+    for (int i = 0; i < 32; i++) inv[i] = 1.0f / powf(c.rope_theta, (float)(2 * i) / 64.0f);  // Qwen.swift:60
+    cudaMemcpy(q->inv_freq, inv, sizeof(inv), cudaMemcpyHostToDevice);
+    return MT_OK;
+}
+
+mt_status dit_alloc(mt_engine* e, DitBufs* d, const mt_dit_config& c, size_t rows) {
+    TRY(dalloc(e, &d->x, rows * c.hidden));
+    TRY(act_alloc(e, &d->norm, rows, c.hidden));
+    TRY(act_alloc(e, &d->attn, rows, c.hidden));
+    TRY(act_alloc(e, &d->ff, rows, c.ff));
+    TRY(dalloc(e, &d->qkv, rows * 3 * c.hidden));
+    return MT_OK;
+}
+
+// A linear over m rows of x: CUDA-core GEMV (fp32 x.f) for m <= 8, else a tcgen05 plan (x.hi/lo).
+// `y` receives fp32 output; `ys` (optional) receives the activation for a following linear in the
+// representation that linear's route reads.
+mt_status make_lin(mt_engine* e, Lin* L, const Act& x, int m, const mt_bf16* w, const mt_bf16* w2,
+                   const mt_bf16* bias, int n, int k, float* y, int ldy, const Act* ys, uint32_t flags,
+                   int split = 1) {
+    LinearArgs a{};
+    a.m = m; a.n = n; a.k = k; a.w = w; a.w2 = w2; a.bias = bias; a.flags = flags | (bias ? MT_LINEAR_BIAS : 0);
+    a.split_k = 1;
+    L->tc = m > kGemvMax;
+    if (!L->tc) {
+        a.x = x.f; a.ldx = x.ld;
+        a.y = ys ? ys->f : y;
+        a.ldy = ys ? ys->ld : ldy;
+        L->g = a;
+        return MT_OK;
+    }
+    a.x_hi = x.hi; a.x_lo = x.lo; a.ld_split = x.ld;
+    if (ys) {
+        a.y_hi = ys->hi; a.y_lo = ys->lo; a.ld_ysplit = ys->ld;
+    } else {
+        a.y = y; a.ldy = ldy;
+    }
+    a.split_k = split;
+    return make_gemm_plan(e->ctx, a, &L->p);
+}
+
+inline void run(const Lin& L, cudaStream_t s) {
+    g_kernels++;
+    if (L.tc) run_gemm_plan(L.p, s);
+    else launch_gemv(L.g, s);
+}
+
+// RMSNorm of `rows` rows into the representation the consumer route (rows_consumer) reads; fp32
+// also when keep_f32.
+void norm(const float* x, int ldx, int rows, int width, const mt_bf16* w, float eps, const Act& out, int rows_consumer,
+          bool keep_f32, cudaStream_t s) {
+    RmsArgs a{};
+    a.x = x; a.ldx = ldx; a.rows = rows; a.width = width; a.w = w; a.eps = eps;
+    const bool tc = rows_consumer > kGemvMax;
+    if (!tc || keep_f32) { a.y = out.f; a.ldy = out.ld; }
+    if (tc) { a.y_hi = out.hi; a.y_lo = out.lo; a.ld_split = out.ld; }
+    launch_rmsnorm(a, s);
+    g_kernels++;
+}
+
+mt_status plan_qwen(mt_engine* e, std::vector<QwenLayerPlans>& plans, const mt_qwen_weights& W, QwenBufs& b, int rows) {
+    const mt_qwen_config& c = W.cfg;
+    const int qkvw = (c.heads + 2 * c.kv_heads) * 64;
+    plans.resize(c.layers);
+    for (int l = 0; l < c.layers; l++) {
+        const mt_qwen_layer& L = W.layers[l];
+        TRY(make_lin(e, &plans[l].qkv, b.norm, rows, L.qkv_w, nullptr, L.qkv_b, qkvw, c.hidden, b.qkv, qkvw, nullptr, 0));
+        TRY(make_lin(e, &plans[l].o, b.attn, rows, L.o_w, nullptr, nullptr, c.hidden, c.heads * 64, b.x, c.hidden,
+                     nullptr, MT_LINEAR_ACCUM));
+        TRY(make_lin(e, &plans[l].gu, b.norm, rows, L.gate_w, L.up_w, nullptr, c.intermediate, c.hidden, nullptr, 0,
+                     &b.mlp, MT_LINEAR_SILU_GATE));
+        TRY(make_lin(e, &plans[l].down, b.mlp, rows, L.down_w, nullptr, nullptr, c.hidden, c.intermediate, b.x,
+                     c.hidden, nullptr, MT_LINEAR_ACCUM));
+    }
+    return MT_OK;
+}
+
+mt_status plan_dit(mt_engine* e, std::vector<DitBlockPlans>& plans, const mt_dit_weights& W, DitBufs& b, int rows) {
+    const mt_dit_config& c = W.cfg;
+    plans.resize(c.depth);
+    for (int i = 0; i < c.depth; i++) {
+        const mt_dit_block& B = W.blocks[i];
+        TRY(make_lin(e, &plans[i].qkv, b.norm, rows, B.qkv_w, nullptr, B.qkv_b, 3 * c.hidden, c.hidden, b.qkv,
+                     3 * c.hidden, nullptr, 0));
+        TRY(make_lin(e, &plans[i].out, b.attn, rows, B.out_w, nullptr, B.out_b, c.hidden, c.hidden, b.x, c.hidden,
+                     nullptr, MT_LINEAR_ACCUM));
+        TRY(make_lin(e, &plans[i].ff1, b.norm, rows, B.ff1_w, nullptr, B.ff1_b, c.ff, c.hidden, nullptr, 0, &b.ff,
+                     MT_LINEAR_GELU));
+        TRY(make_lin(e, &plans[i].ff2, b.ff, rows, B.ff2_w, nullptr, B.ff2_b, c.hidden, c.ff, b.x, c.hidden, nullptr,
+                     MT_LINEAR_ACCUM));
+    }
+    return MT_OK;
+}
+
+mt_status build_plans(mt_engine* e) {
+    if (e->plan_R == e->R && e->plan_T == e->T) return MT_OK;
+    const int R = e->R, T = e->T;
+    const mt_model_config& c = e->cfg;
+    TRY(plan_qwen(e, e->llm_dec, e->w.llm, e->llm, R));
+    TRY(plan_qwen(e, e->llm_pre, e->w.llm, e->llm, R * T));
+    TRY(make_lin(e, &e->cond, e->z, R, e->w.flow_c_w, nullptr, e->w.flow_c_b, c.flow.hidden, c.llm.hidden, e->cemb,
+                 c.flow.hidden, nullptr, 0));
+    {
+        // The stop head has two outputs: always the GEMV (rows processed in chunks of 8).
+        LinearArgs a{};
+        a.x = e->z.f; a.ldx = e->z.ld; a.m = R; a.n = 2; a.k = c.llm.hidden; a.w = e->w.stop_w; a.bias = e->w.stop_b;
+        a.flags = MT_LINEAR_BIAS; a.y = e->stop; a.ldy = 2;
+        e->stop_lin.tc = false;
+        e->stop_lin.g = a;
+    }
+    TRY(plan_dit(e, e->flow_blocks, e->w.flow, e->flow, 6 * R));
+    TRY(plan_dit(e, e->agg_blocks, e->w.agg, e->agg, 2 * R));
+    TRY(make_lin(e, &e->agg_final, e->agg_norm, R, e->w.agg.final_w, nullptr, e->w.agg.final_b, c.agg.out_dim,
+                 c.agg.hidden, e->llm.x, c.llm.hidden, nullptr, 0));
+    TRY(plan_qwen(e, e->vae_layers, e->w.vae, e->vae, 4 * R));
+    TRY(make_lin(e, &e->vae_head, e->vae_hidden, 4 * R, e->w.vae_head_w, nullptr, e->w.vae_head_b, c.nfft + 2,
+                 c.vae.hidden, e->spec, c.nfft + 2, nullptr, 0));
+    e->plan_R = R;
+    e->plan_T = T;
+    return MT_OK;
+}
+
+// One pass of a Qwen stack (QwenForward.dispatches, Qwen.swift:72-97) over `rows` rows grouped by
+// request (rows_per_req each); positions pos0 + pos_dev[request] + row % rows_per_req.
+void qwen_forward(mt_engine* e, const mt_qwen_weights& W, QwenBufs& b, std::vector<QwenLayerPlans>& plans, int rows,
+                  int rows_per_req, int pos0, const int* pos_dev, int max_keys, cudaStream_t s) {
+    const mt_qwen_config& c = W.cfg;
+    const int qkvw = (c.heads + 2 * c.kv_heads) * 64;
+    const size_t tensor = (size_t)c.kv_heads * b.cap * 64;
+    const long long req_stride = (long long)c.layers * 2 * tensor;
+    const bool tc = rows > kGemvMax;
+    for (int l = 0; l < c.layers; l++) {
+        const mt_qwen_layer& L = W.layers[l];
+        float* kc = b.kv + (size_t)(2 * l) * tensor;
+        float* vc = kc + tensor;
+        norm(b.x, c.hidden, rows, c.hidden, L.norm1, c.eps, b.norm, rows, false, s);
+        run(plans[l].qkv, s);
+        RopeArgs ra{};
+        ra.qkv = b.qkv; ra.ldq = qkvw; ra.rows = rows; ra.rows_per_req = rows_per_req; ra.hq = c.heads;
+        ra.hkv = c.kv_heads; ra.pos0 = pos0; ra.pos_dev = pos_dev; ra.kc = kc; ra.vc = vc; ra.req_stride = req_stride;
+        ra.cap = b.cap; ra.inv_freq = b.inv_freq;
+        launch_rope_cache(ra, s); g_kernels++;
+        AttnArgs aa{};
+        aa.q = b.qkv; aa.ldq = qkvw; aa.rows = rows; aa.rows_per_req = rows_per_req; aa.hq = c.heads; aa.hkv = c.kv_heads;
+        aa.pos0 = pos0; aa.pos_dev = pos_dev; aa.window = c.window; aa.kc = kc; aa.vc = vc; aa.req_stride = req_stride;
+        aa.cap = b.cap; aa.max_keys = max_keys;
+        if (tc) { aa.out_hi = b.attn.hi; aa.out_lo = b.attn.lo; aa.ld_split = b.attn.ld; }
+        else { aa.out = b.attn.f; aa.ldo = b.attn.ld; }
+        launch_attention(aa, s); g_kernels++;
+        run(plans[l].o, s);
+        norm(b.x, c.hidden, rows, c.hidden, L.norm2, c.eps, b.norm, rows, false, s);
+        run(plans[l].gu, s);
+        run(plans[l].down, s);
+    }
+}
+
+// DiTForward.encode blocks (DiT.swift:35-48) over batch sequences of seq rows; the final layer is
+// done by the caller.
+void dit_blocks(mt_engine* e, const mt_dit_weights& W, DitBufs& b, std::vector<DitBlockPlans>& plans, int batch,
+                int seq, cudaStream_t s) {
+    const mt_dit_config& c = W.cfg;
+    const int rows = batch * seq;
+    const bool tc = rows > kGemvMax;
+    for (int i = 0; i < c.depth; i++) {
+        const mt_dit_block& B = W.blocks[i];
+        norm(b.x, c.hidden, rows, c.hidden, B.norm1, c.eps, b.norm, rows, false, s);
+        run(plans[i].qkv, s);
+        DitAttnArgs da{};
+        da.qkv = b.qkv; da.ld = 3 * c.hidden; da.batch = batch; da.seq = seq; da.heads = c.heads;
+        da.inv_freq = W.inv_freq;
+        if (tc) { da.out_hi = b.attn.hi; da.out_lo = b.attn.lo; da.ld_split = b.attn.ld; }
+        else { da.out = b.attn.f; da.ldo = b.attn.ld; }
+        launch_dit_attention(da, s); g_kernels++;
+        run(plans[i].out, s);
+        norm(b.x, c.hidden, rows, c.hidden, B.norm2, c.eps, b.norm, rows, false, s);
+        run(plans[i].ff1, s);
+        run(plans[i].ff2, s);
+    }
+}
+
+// DiT.swift:56-65 schedule and :68-79 sinusoid, in fp32 as the Swift Float code.
+void flow_timesteps(int steps, float* out) {
+    static const int e10[] = {0, 2, 4, 6, 8, 12, 16, 20, 24, 28, 32}, e5[] = {0, 2, 4, 8, 16, 32},
+                     e6[] = {0, 2, 4, 6, 8, 16, 32}, e7[] = {0, 2, 4, 6, 8, 16, 24, 32},
+                     e12[] = {0, 2, 4, 6, 8, 10, 12, 14, 16, 20, 24, 28, 32},
+                     e16[] = {0, 1, 2, 3, 4, 5, 6, 7, 8, 10, 12, 14, 16, 20, 24, 28, 32};
+    const int* tab = steps == 10 ? e10 : steps == 5 ? e5 : steps == 6 ? e6 : steps == 7 ? e7 : steps == 12 ? e12
+                   : steps == 16 ? e16 : nullptr;
+    const float half_pi = 3.14159274101257324f / 2.0f;
+    for (int i = 0; i <= steps; i++) {
+        const float t = tab ? (float)tab[i] / 32.0f : (float)i / (float)steps;
+        out[i] = t - (cosf(half_pi * t) - 1.0f + t);
+    }
+}
+
+void sinusoid(float t, int dim, float* out) {
+    const int half = dim / 2;
+    const float step = (float)(log(10000.0) / (double)(half - 1));
+    for (int i = 0; i < half; i++) {
+        const float freq = expf((float)i * -step);
+        const float arg = (1000.0f * t) * freq;
+        out[i] = (float)sin((double)arg);
+        out[half + i] = (float)cos((double)arg);
+    }
+}
+
+mt_status precompute_temb(mt_engine* e) {
+    const mt_model_config& c = e->cfg;
+    const int FS = c.flow_steps, Df = c.flow.hidden;
+    e->timesteps.resize(FS + 1);
+    flow_timesteps(FS, e->timesteps.data());
+    std::vector<float> sin_host((size_t)FS * c.time_dim);
+    for (int k = 0; k < FS; k++) sinusoid(e->timesteps[k], c.time_dim, sin_host.data() + (size_t)k * c.time_dim);
+    float *sinus = nullptr, *mid = nullptr;
+    TRY(dalloc(e, &sinus, sin_host.size()));
+    TRY(dalloc(e, &mid, (size_t)FS * Df));
+    cudaMemcpy(sinus, sin_host.data(), sin_host.size() * sizeof(float), cudaMemcpyHostToDevice);
+    TRY(mt_linear(e->ctx, nullptr, sinus, c.time_dim, FS, e->w.flow_t1_w, nullptr, e->w.flow_t1_b, Df, c.time_dim, mid,
+                  Df, MT_LINEAR_BIAS | MT_LINEAR_SILU));
+    TRY(mt_linear(e->ctx, nullptr, mid, Df, FS, e->w.flow_t2_w, nullptr, e->w.flow_t2_b, Df, Df, e->temb, Df,
+                  MT_LINEAR_BIAS));
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) return fail(e->ctx, MT_ERR_CUDA, "temb precompute: %s", cudaGetErrorString(err));
+    return MT_OK;
+}
+
+// ---- step pieces ---------------------------------------------------------------------------------
+
+void llm_token(mt_engine* e, cudaStream_t s) {
+    const mt_qwen_config& c = e->cfg.llm;
+    const int R = e->R;
+    qwen_forward(e, e->w.llm, e->llm, e->llm_dec, R, 1, 0, e->state_dev + st_llm_pos(R), e->llm.cap, s);
+    norm(e->llm.x, c.hidden, R, c.hidden, e->w.llm.final_norm, c.eps, e->z, R, true, s);
+}
+
+void flow_agg_fc1(mt_engine* e, cudaStream_t s) {
+    const mt_model_config& c = e->cfg;
+    const int R = e->R, L = c.latent_dim, Df = c.flow.hidden;
+    run(e->stop_lin, s);
+    run(e->cond, s);
+    launch_flow_begin(e->y, e->hist, e->noise, L, e->opt.max_steps, e->state_dev, R, s); g_kernels++;
+    for (int k = 0; k < c.flow_steps; k++) {
+        launch_flow_assemble_batched(e->y, e->hist, e->cemb, e->w.flow_c_b, e->temb + (size_t)k * Df, e->w.flow_x_w,
+                                     e->w.flow_x_b, Df, L, e->flow.x, R, s);
+        g_kernels++;
+        dit_blocks(e, e->w.flow, e->flow, e->flow_blocks, 2 * R, 3, s);
+        FlowFinalArgs fa{};
+        fa.X = e->flow.x; fa.hidden = Df; fa.norm_w = e->w.flow.final_norm; fa.eps = c.flow.eps;
+        fa.final_w = e->w.flow.final_w; fa.final_b = e->w.flow.final_b; fa.latent = L; fa.y = e->y;
+        fa.cfg = e->cfg_scale; fa.dt = e->timesteps[k + 1] - e->timesteps[k]; fa.vel0 = e->vel0;
+        fa.flow_steps = c.flow_steps; fa.k = k; fa.latents = e->latents; fa.steps_cap = e->opt.max_steps;
+        fa.state = e->state_dev;
+        launch_flow_final(fa, R, s); g_kernels++;
+    }
+    // Aggregator (Engine.swift:406-410): [cls, x_emb(latent)] -> DiT -> final layer of row 0 -> LLM input.
+    const int Da = c.agg.hidden;
+    launch_agg_assemble(e->y, e->w.agg_cls, e->w.agg_x_w, e->w.agg_x_b, Da, L, e->agg.x, R, s); g_kernels++;
+    dit_blocks(e, e->w.agg, e->agg, e->agg_blocks, R, 2, s);
+    norm(e->agg.x, 2 * Da, R, Da, e->w.agg.final_norm, c.agg.eps, e->agg_norm, R, false, s);
+    run(e->agg_final, s);
+}
+
+void vae_fc1(mt_engine* e, cudaStream_t s) {
+    const mt_model_config& c = e->cfg;
+    launch_vae_fc1(e->y, e->w.vae_fc1_w, e->w.vae_fc1_b, c.vae.hidden, c.latent_dim, e->vae_h, e->state_dev, e->R, s);
+    g_kernels++;
+}
+
+// VAEDecoder.decodeDispatches (VAEDecoder.swift:86-107) for latent d of every request.
+void vae_decode(mt_engine* e, cudaStream_t s) {
+    const mt_model_config& c = e->cfg;
+    const int R = e->R, Hv = c.vae.hidden;
+    launch_vae_upsample(e->vae_h, Hv, e->state_dev, e->vae.x, R, s); g_kernels++;
+    const int max_keys = c.vae.window > 0 ? c.vae.window : e->vae.cap;
+    qwen_forward(e, e->w.vae, e->vae, e->vae_layers, 4 * R, 4, 0, e->state_dev + st_vae_pos(R), max_keys, s);
+    norm(e->vae.x, Hv, 4 * R, Hv, e->w.vae.final_norm, c.vae.eps, e->vae_hidden, 4 * R, true, s);
+    run(e->vae_head, s);
+    IstftArgs ia{};
+    ia.spec = e->spec; ia.ld_spec = c.nfft + 2; ia.count = 4 * R; ia.nfft = c.nfft; ia.window = e->w.vae_window;
+    ia.frames = e->fring; ia.req_stride = 8LL * c.nfft; ia.frames_per_req = 4; ia.frame0 = 0;
+    ia.frame0_dev = e->state_dev + st_vae_pos(R); ia.ring = 8;
+    launch_istft_frames(ia, s); g_kernels++;
+    EmitArgs ea{};
+    ea.frames = e->fring; ea.req_stride = 8LL * c.nfft; ea.window = e->w.vae_window; ea.nfft = c.nfft; ea.hop = c.hop;
+    ea.s0 = 0; ea.s0_dev = e->state_dev + st_emit_s0(R); ea.count = 0; ea.count_dev = e->state_dev + st_emit_count(R);
+    ea.last_frame = 0; ea.last_dev = e->state_dev + st_emit_last(R); ea.ring = 8; ea.out = e->pcm; ea.ld_out = e->max_chunk;
+    launch_istft_emit(ea, e->max_chunk, R, s); g_kernels++;
+}
+
+// Host-side bookkeeping of one VAE decode (VAEDecoder.swift:96-106); fills the state header and
+// per-request emission fields, returns the sample count.
+int plan_decode(mt_engine* e, int d, bool has_next) {
+    const int hop = e->cfg.hop, pad = (e->cfg.nfft - hop) / 2, R = e->R;
+    const int frame_count = 4 * (d + 1);
+    const int final_end = has_next ? frame_count * hop - pad : frame_count * hop;
+    const int count = final_end - e->emitted;
+    int* st = e->state_host;
+    st[ST_D] = d;
+    st[ST_HAS_NEXT] = has_next ? 1 : 0;
+    for (int r = 0; r < R; r++) {
+        st[st_vae_pos(R) + r] = 4 * d;
+        st[st_emit_s0(R) + r] = e->emitted;
+        st[st_emit_count(R) + r] = count;
+        st[st_emit_last(R) + r] = frame_count - 1;
+    }
+    e->emitted = final_end;
+    e->decoded = d + 1;
+    return count;
+}
+
+void upload_state(mt_engine* e, cudaStream_t s) {
+    cudaMemcpyAsync(e->state_dev, e->state_host, st_size(e->opt.max_requests) * sizeof(int), cudaMemcpyHostToDevice, s);
+}
+
+// Enqueues the device work of a step whose state is already uploaded. with_llm: n > 0;
+// with_decode: a VAE decode is due.
+void enqueue_step(mt_engine* e, cudaStream_t s, bool with_llm, bool with_decode) {
+    if (with_decode) {
+        cudaEventRecord(e->ev_fork, s);
+        cudaStreamWaitEvent(e->sb, e->ev_fork, 0);
+        vae_decode(e, e->sb);
+        cudaEventRecord(e->ev_join, e->sb);
+    }
+    if (with_llm) llm_token(e, s);
+    flow_agg_fc1(e, s);
+    if (with_decode) cudaStreamWaitEvent(s, e->ev_join, 0);
+    vae_fc1(e, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_options* opt, mt_engine** out) {
+    MT_REQUIRE(ctx, ctx && model && opt && out, MT_ERR_ARG, "mt_engine_create: null argument");
+    *out = nullptr;
+    const mt_model_config* cfgp = mt_model_get_config(model);
+    const mt_model_config& c = *cfgp;
+    MT_REQUIRE(ctx, opt->max_requests >= 1 && opt->max_prompt >= 1 && opt->max_steps >= 1 &&
+                        opt->max_prompt + opt->max_steps <= c.llm_capacity,
+               MT_ERR_CAPACITY, "mt_engine_create: requests %d prompt %d steps %d (prompt + steps <= %d)",
+               opt->max_requests, opt->max_prompt, opt->max_steps, c.llm_capacity);
+    const int ring = opt->vae_ring > 0 ? opt->vae_ring : 128;
+    MT_REQUIRE(ctx, c.vae.window > 0 && ring >= c.vae.window + 3, MT_ERR_CAPACITY,
+               "mt_engine_create: VAE ring %d must hold window %d + 3 positions", ring, c.vae.window);
+    mt_engine* e = new mt_engine();
+    e->ctx = ctx;
+    e->model = model;
+    e->cfg = c;
+    e->w = *mt_model_get_weights(model);
+    e->opt = *opt;
+    e->opt.vae_ring = ring;
+    const int R = opt->max_requests, T = opt->max_prompt, S = opt->max_steps;
+    auto cleanup = [&](mt_status st) {
+        mt_engine_destroy(e);
+        return st;
+    };
+#define ETRY(expr)                                    \
+    do {                                              \
+        mt_status _s = (expr);                        \
+        if (_s != MT_OK) return cleanup(_s);          \
+    } while (0)
+    ETRY(qwen_alloc(e, &e->llm, c.llm, (size_t)R * T, R, c.llm_capacity));
+    ETRY(act_alloc(e, &e->z, R, c.llm.hidden));
+    ETRY(dalloc(e, &e->stop, (size_t)R * 2));
+    ETRY(dalloc(e, &e->temb, (size_t)c.flow_steps * c.flow.hidden));
+    ETRY(dalloc(e, &e->cemb, (size_t)R * c.flow.hidden));
+    ETRY(dalloc(e, &e->y, (size_t)R * c.latent_dim));
+    ETRY(dalloc(e, &e->hist, (size_t)R * c.latent_dim));
+    ETRY(dalloc(e, &e->noise, (size_t)R * S * c.latent_dim));
+    ETRY(dalloc(e, &e->latents, (size_t)R * S * c.latent_dim));
+    ETRY(dalloc(e, &e->vel0, (size_t)R * c.flow_steps * 2 * c.latent_dim));
+    ETRY(dit_alloc(e, &e->flow, c.flow, (size_t)6 * R));
+    ETRY(dit_alloc(e, &e->agg, c.agg, (size_t)2 * R));
+    ETRY(act_alloc(e, &e->agg_norm, R, c.agg.hidden));
+    ETRY(dalloc(e, &e->vae_h, (size_t)R * VAE_H_RING * c.vae.hidden));
+    ETRY(qwen_alloc(e, &e->vae, c.vae, (size_t)4 * R, R, ring));
+    ETRY(act_alloc(e, &e->vae_hidden, (size_t)4 * R, c.vae.hidden));
+    ETRY(dalloc(e, &e->spec, (size_t)4 * R * (c.nfft + 2)));
+    ETRY(dalloc(e, &e->fring, (size_t)R * 8 * c.nfft));
+    e->max_chunk = 4 * c.hop + (c.nfft - c.hop) / 2;
+    ETRY(dalloc(e, &e->pcm, (size_t)R * e->max_chunk));
+    ETRY(dalloc(e, &e->state_dev, (size_t)st_size(R)));
+    if (cudaMallocHost(&e->state_host, st_size(R) * sizeof(int)) != cudaSuccess)
+        return cleanup(fail(ctx, MT_ERR_NOMEM, "engine: pinned step state"));
+    memset(e->state_host, 0, st_size(R) * sizeof(int));
+    if (cudaStreamCreateWithFlags(&e->sb, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->ev_join, cudaEventDisableTiming) != cudaSuccess)
+        return cleanup(fail(ctx, MT_ERR_CUDA, "engine: stream/event creation"));
+    ETRY(precompute_temb(e));
+#undef ETRY
+    *out = e;
+    return MT_OK;
+}
+
+void mt_engine_destroy(mt_engine* e) {
+    if (!e) return;
+    if (e->graph_exec) cudaGraphExecDestroy(e->graph_exec);
+    if (e->graph) cudaGraphDestroy(e->graph);
+    if (e->sb) cudaStreamDestroy(e->sb);
+    if (e->ev_fork) cudaEventDestroy(e->ev_fork);
+    if (e->ev_join) cudaEventDestroy(e->ev_join);
+    if (e->state_host) cudaFreeHost(e->state_host);
+    for (void* p : e->allocs) cudaFree(p);
+    delete e;
+}
+
+mt_status mt_engine_begin(mt_engine* e, void* stream, int requests, int prompt_rows, const float* embeds,
+                          const int32_t* token_ids, const float* noise, const float* initial_history, int steps,
+                          float cfg) {
+    if (!e) return MT_ERR_ARG;
+    mt_ctx* ctx = e->ctx;
+    const mt_model_config& c = e->cfg;
+    MT_REQUIRE(ctx, (embeds || token_ids) && noise, MT_ERR_ARG, "mt_engine_begin: need embeds or token ids, and noise");
+    MT_REQUIRE(ctx, !token_ids || e->w.embed_tokens, MT_ERR_ARG, "mt_engine_begin: model has no embedding table");
+    MT_REQUIRE(ctx, requests >= 1 && requests <= e->opt.max_requests && prompt_rows >= 1 &&
+                        prompt_rows <= e->opt.max_prompt && steps >= 1 && steps <= e->opt.max_steps &&
+                        prompt_rows + steps <= c.llm_capacity,
+               MT_ERR_CAPACITY, "mt_engine_begin: requests %d prompt %d steps %d exceed the engine's capacity",
+               requests, prompt_rows, steps);
+    cudaStream_t s = as_stream(stream);
+    e->R = requests;
+    e->T = prompt_rows;
+    e->steps = steps;
+    e->cfg_scale = cfg;
+    e->n = 0;
+    e->latents_fed = e->decoded = e->emitted = 0;
+    e->prefilled = false;
+    if (e->plan_R != requests && e->graph_exec) {
+        cudaGraphExecDestroy(e->graph_exec);
+        cudaGraphDestroy(e->graph);
+        e->graph_exec = nullptr;
+        e->graph = nullptr;
+    }
+    TRY(build_plans(e));
+    const int H = c.llm.hidden, L = c.latent_dim, S = e->opt.max_steps;
+    if (embeds) {
+        cudaMemcpyAsync(e->llm.x, embeds, sizeof(float) * (size_t)requests * prompt_rows * H, cudaMemcpyDeviceToDevice, s);
+    } else {
+        launch_embed_gather(token_ids, requests * prompt_rows, e->w.embed_tokens, H, c.vocab, e->llm.x, ctx->d_status, s);
+    }
+    cudaMemcpy2DAsync(e->noise, (size_t)S * L * sizeof(float), noise, (size_t)steps * L * sizeof(float),
+                      (size_t)steps * L * sizeof(float), requests, cudaMemcpyDeviceToDevice, s);
+    if (initial_history)
+        cudaMemcpyAsync(e->hist, initial_history, sizeof(float) * (size_t)requests * L, cudaMemcpyDeviceToDevice, s);
+    else
+        cudaMemsetAsync(e->hist, 0, sizeof(float) * (size_t)requests * L, s);
+    cudaMemsetAsync(e->y, 0, sizeof(float) * (size_t)requests * L, s);
+    // KV caches need no reset: every position is written before it is read.
+    e->begun = true;
+    return check_launch(ctx, "mt_engine_begin");
+}
+
+mt_status mt_engine_prefill(mt_engine* e, void* stream) {
+    if (!e) return MT_ERR_ARG;
+    MT_REQUIRE(e->ctx, e->begun && !e->prefilled, MT_ERR_STATE, "mt_engine_prefill: call after mt_engine_begin, once");
+    cudaStream_t s = as_stream(stream);
+    const mt_qwen_config& c = e->cfg.llm;
+    const int R = e->R, T = e->T;
+    qwen_forward(e, e->w.llm, e->llm, e->llm_pre, R * T, T, 0, nullptr, T, s);
+    // Final norm of each request's last row -> z (normRows 1, Engine.swift:329).
+    norm(e->llm.x + (size_t)(T - 1) * c.hidden, T * c.hidden, R, c.hidden, e->w.llm.final_norm, c.eps, e->z, R, true, s);
+    e->prefilled = true;
+    return check_launch(e->ctx, "mt_engine_prefill");
+}
+
+mt_status mt_engine_step(mt_engine* e, void* stream, int* pcm_count) {
+    if (!e) return MT_ERR_ARG;
+    mt_ctx* ctx = e->ctx;
+    MT_REQUIRE(ctx, e->prefilled, MT_ERR_STATE, "mt_engine_step: prefill first");
+    MT_REQUIRE(ctx, e->n < e->steps, MT_ERR_STATE, "mt_engine_step: all %d steps done", e->steps);
+    cudaStream_t s = as_stream(stream);
+    const int R = e->R, n = e->n;
+    int* st = e->state_host;
+    // The previous step's upload may still be pending on the device: wait before rewriting.
+    cudaStreamSynchronize(s);
+    st[ST_N] = n;
+    for (int r = 0; r < R; r++) st[st_llm_pos(R) + r] = e->T + n - 1;
+    // Deferred decode (VAEDecoder.deferredDecode, :73-76): latent n-2 once latent n-1 exists.
+    const bool with_decode = e->decoded + 1 < e->latents_fed;
+    int count = 0;
+    if (with_decode) count = plan_decode(e, e->decoded, true);
+    else st[ST_D] = -1;
+    const bool with_llm = n > 0;
+    const bool steady = with_llm && with_decode;
+    if (steady && e->opt.use_graphs) {
+        if (!e->graph_exec || e->graph_stream != s) {
+            if (e->graph_exec) {
+                cudaGraphExecDestroy(e->graph_exec);
+                cudaGraphDestroy(e->graph);
+                e->graph_exec = nullptr;
+            }
+            cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+            upload_state(e, s);
+            g_kernels = 0;
+            enqueue_step(e, s, true, true);
+            e->graph_kernels = g_kernels;
+            cudaError_t err = cudaStreamEndCapture(s, &e->graph);
+            if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph capture: %s", cudaGetErrorString(err));
+            err = cudaGraphInstantiate(&e->graph_exec, e->graph, 0);
+            if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph instantiate: %s", cudaGetErrorString(err));
+            e->graph_stream = s;
+        }
+        cudaGraphLaunch(e->graph_exec, s);
+        e->step_kernels = e->graph_kernels;
+    } else {
+        upload_state(e, s);
+        g_kernels = 0;
+        enqueue_step(e, s, with_llm, with_decode);
+        e->step_kernels = g_kernels;
+    }
+    e->latents_fed++;
+    e->n++;
+    if (pcm_count) *pcm_count = count;
+    return check_launch(ctx, "mt_engine_step");
+}
+
+mt_status mt_engine_flush(mt_engine* e, void* stream, int* pcm_count) {
+    if (!e) return MT_ERR_ARG;
+    MT_REQUIRE(e->ctx, e->prefilled, MT_ERR_STATE, "mt_engine_flush: nothing generated");
+    cudaStream_t s = as_stream(stream);
+    if (pcm_count) *pcm_count = 0;
+    if (e->decoded >= e->latents_fed) return MT_OK;
+    cudaStreamSynchronize(s);
+    const int d = e->decoded;
+    const int count = plan_decode(e, d, d + 1 < e->latents_fed);
+    upload_state(e, s);
+    vae_decode(e, s);
+    if (pcm_count) *pcm_count = count;
+    return check_launch(e->ctx, "mt_engine_flush");
+}
+
+mt_status mt_engine_buffer(const mt_engine* e, int which, const float** ptr, long long* stride) {
+    if (!e || !ptr || !stride) return MT_ERR_ARG;
+    const mt_model_config& c = e->cfg;
+    switch (which) {
+        case MT_BUF_Z: *ptr = e->z.f; *stride = c.llm.hidden; break;
+        case MT_BUF_STOP_LOGITS: *ptr = e->stop; *stride = 2; break;
+        case MT_BUF_LATENTS: *ptr = e->latents; *stride = (long long)e->opt.max_steps * c.latent_dim; break;
+        case MT_BUF_AGG_OUT: *ptr = e->llm.x; *stride = c.llm.hidden; break;
+        case MT_BUF_VELOCITY0: *ptr = e->vel0; *stride = (long long)c.flow_steps * 2 * c.latent_dim; break;
+        case MT_BUF_VAE_HIDDEN: *ptr = e->vae_hidden.f; *stride = 4LL * c.vae.hidden; break;
+        case MT_BUF_PCM: *ptr = e->pcm; *stride = e->max_chunk; break;
+        default: return MT_ERR_ARG;
+    }
+    return MT_OK;
+}
+
+int mt_engine_steps_done(const mt_engine* e) { return e ? e->n : -1; }
+
+int mt_engine_step_kernels(const mt_engine* e) { return e ? e->step_kernels : -1; }
+
+mt_status mt_engine_generate(mt_engine* e, void* stream, int requests, int prompt_rows, const float* embeds_host,
+                             const int32_t* ids_host, const float* noise_host, int steps, float cfg, float* pcm_host,
+                             long long pcm_stride, long long* pcm_count, float* stop_prob_host) {
+    if (!e) return MT_ERR_ARG;
+    mt_ctx* ctx = e->ctx;
+    MT_REQUIRE(ctx, (embeds_host || ids_host) && noise_host && pcm_host && pcm_count, MT_ERR_ARG,
+               "mt_engine_generate: null argument");
+    const mt_model_config& c = e->cfg;
+    MT_REQUIRE(ctx, pcm_stride >= 4LL * c.hop * steps, MT_ERR_CAPACITY,
+               "mt_engine_generate: pcm_stride %lld < %lld samples", pcm_stride, 4LL * c.hop * steps);
+    MT_REQUIRE(ctx, requests >= 1 && requests <= e->opt.max_requests && prompt_rows >= 1 &&
+                        prompt_rows <= e->opt.max_prompt && steps >= 1 && steps <= e->opt.max_steps,
+               MT_ERR_CAPACITY, "mt_engine_generate: requests %d prompt %d steps %d exceed the engine", requests,
+               prompt_rows, steps);
+    cudaStream_t s = as_stream(stream);
+    const size_t in_rows = (size_t)requests * prompt_rows;
+    const size_t emb_bytes = embeds_host ? in_rows * c.llm.hidden * sizeof(float) : in_rows * sizeof(int32_t);
+    const size_t noise_bytes = (size_t)requests * steps * c.latent_dim * sizeof(float);
+    // Staging: device copies of the inputs, pinned host buffers for every chunk and stop logit.
+    void* d_in = nullptr;
+    float* d_noise = nullptr;
+    float* h_pcm = nullptr;
+    float* h_stop = nullptr;
+    const size_t chunk_floats = (size_t)requests * e->max_chunk;
+    const int emissions = steps + 2;
+    bool ok = cudaMalloc(&d_in, emb_bytes) == cudaSuccess && cudaMalloc(&d_noise, noise_bytes) == cudaSuccess &&
+              cudaMallocHost(&h_pcm, chunk_floats * emissions * sizeof(float)) == cudaSuccess &&
+              cudaMallocHost(&h_stop, (size_t)steps * requests * 2 * sizeof(float)) == cudaSuccess;
+    std::vector<int> counts;
+    mt_status st = MT_OK;
+    if (!ok) st = fail(ctx, MT_ERR_NOMEM, "mt_engine_generate: staging buffers");
+    if (st == MT_OK) {
+        cudaMemcpyAsync(d_in, embeds_host ? (const void*)embeds_host : (const void*)ids_host, emb_bytes,
+                        cudaMemcpyHostToDevice, s);
+        cudaMemcpyAsync(d_noise, noise_host, noise_bytes, cudaMemcpyHostToDevice, s);
+        st = mt_engine_begin(e, stream, requests, prompt_rows, embeds_host ? (const float*)d_in : nullptr,
+                             embeds_host ? nullptr : (const int32_t*)d_in, d_noise, nullptr, steps, cfg);
+    }
+    if (st == MT_OK) st = mt_engine_prefill(e, stream);
+    for (int n = 0; st == MT_OK && n < steps; n++) {
+        int count = 0;
+        st = mt_engine_step(e, stream, &count);
+        if (st != MT_OK) break;
+        cudaMemcpyAsync(h_stop + (size_t)n * requests * 2, e->stop, (size_t)requests * 2 * sizeof(float),
+                        cudaMemcpyDeviceToHost, s);
+        if (count > 0) {
+            cudaMemcpyAsync(h_pcm + counts.size() * chunk_floats, e->pcm, chunk_floats * sizeof(float),
+                            cudaMemcpyDeviceToHost, s);
+            counts.push_back(count);
+        }
+    }
+    while (st == MT_OK) {
+        int count = 0;
+        st = mt_engine_flush(e, stream, &count);
+        if (st != MT_OK || count == 0) break;
+        cudaMemcpyAsync(h_pcm + counts.size() * chunk_floats, e->pcm, chunk_floats * sizeof(float),
+                        cudaMemcpyDeviceToHost, s);
+        counts.push_back(count);
+    }
+    if (st == MT_OK) {
+        cudaError_t err = cudaStreamSynchronize(s);
+        if (err != cudaSuccess) st = fail(ctx, MT_ERR_CUDA, "mt_engine_generate: %s", cudaGetErrorString(err));
+    }
+    if (st == MT_OK) {
+        long long total = 0;
+        for (size_t i = 0; i < counts.size(); i++) {
+            for (int r = 0; r < requests; r++)
+                memcpy(pcm_host + r * pcm_stride + total, h_pcm + i * chunk_floats + (size_t)r * e->max_chunk,
+                       counts[i] * sizeof(float));
+            total += counts[i];
+        }
+        *pcm_count = total;
+        if (stop_prob_host)
+            for (int n = 0; n < steps; n++)
+                for (int r = 0; r < requests; r++) {
+                    const float* l = h_stop + ((size_t)n * requests + r) * 2;
+                    stop_prob_host[(size_t)r * steps + n] = 1.0f / (1.0f + expf(l[0] - l[1]));  // Engine.swift:349
+                }
+    }
+    if (d_in) cudaFree(d_in);
+    if (d_noise) cudaFree(d_noise);
+    if (h_pcm) cudaFreeHost(h_pcm);
+    if (h_stop) cudaFreeHost(h_stop);
+    return st;
+}
+
+}  // extern "C"

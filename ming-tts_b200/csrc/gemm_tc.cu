@@ -27,20 +27,9 @@ namespace mt {
 constexpr int TC_THREADS = 128;
 constexpr int TC_BM = 128;  // weight rows per tile (MMA M)
 constexpr int TC_BK = 64;   // bf16 K per stage = one 128-byte swizzle span
-constexpr uint32_t WAIT_LIMIT = 1u << 24;
+constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait
 
-struct TcEpi {
-    int m, n, k;
-    int bn;            // activation rows per tile (MMA N), multiple of 16, <= 256
-    int stages;
-    int kb_per_split;  // k blocks per blockIdx.z
-    const uint16_t* bias;
-    float* y; int ldy;
-    uint16_t* y_hi; uint16_t* y_lo; int ld_ysplit;
-    uint32_t flags;
-    int split;         // > 1: red.add fp32 partials into y (no activation allowed)
-    unsigned int* status;
-};
+
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -55,11 +44,18 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                  : "memory");
 }
 
-// Bounded wait on the phase with the given parity. Returns false (and records the site) when the
-// iteration limit runs out.
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait on the phase with the given parity: gives up after WAIT_NS of wall time (checked
+// every 256 polls), records the site in the status word and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status, unsigned site) {
     const uint32_t addr = smem_u32(bar);
-    for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; i++) {
         uint32_t ok;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -69,6 +65,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
             : "r"(addr), "r"(parity)
             : "memory");
         if (ok) return true;
+        if ((i & 255u) == 0) {
+            const uint64_t now = global_ns();
+            if (t0 == 0) t0 = now;
+            else if (now - t0 > WAIT_NS) break;
+        }
     }
     report_status(status, DEV_TIMEOUT, site, blockIdx.x | (blockIdx.y << 16));
     return false;
@@ -296,18 +297,23 @@ static bool make_map(CUtensorMap* map, const void* ptr, int rows, int cols, int 
 
 static int round16(int v) { return (v + 15) & ~15; }
 
-mt_status launch_gemm_tc(mt_ctx* ctx, const LinearArgs& a, cudaStream_t s) {
+mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     const bool gated = (a.flags & MT_LINEAR_SILU_GATE) != 0;
-    MT_REQUIRE(ctx, a.k % 8 == 0 && a.ld_split % 8 == 0, MT_ERR_SHAPE, "gemm_tc: k %d ld %d need multiples of 8",
-               a.k, a.ld_split);
+    MT_REQUIRE(ctx, a.m > 0 && a.n > 0 && a.k > 0, MT_ERR_SHAPE, "gemm_tc: empty shape m %d n %d k %d", a.m, a.n, a.k);
+    MT_REQUIRE(ctx, a.k % 8 == 0 && a.ld_split % 8 == 0 && a.ld_split >= a.k, MT_ERR_SHAPE,
+               "gemm_tc: k %d ld %d need multiples of 8", a.k, a.ld_split);
     MT_REQUIRE(ctx, ((uintptr_t)a.w & 15u) == 0 && ((uintptr_t)a.x_hi & 15u) == 0 && ((uintptr_t)a.x_lo & 15u) == 0 &&
                         (!gated || ((uintptr_t)a.w2 & 15u) == 0),
                MT_ERR_ARG, "gemm_tc: operands need 16-byte alignment");
     MT_REQUIRE(ctx, a.y || a.y_hi, MT_ERR_ARG, "gemm_tc: no output");
-    TcEpi e{};
+    MT_REQUIRE(ctx, !(a.flags & MT_LINEAR_BIAS) || a.bias, MT_ERR_ARG, "gemm_tc: BIAS needs bias");
+    MT_REQUIRE(ctx, !(a.flags & MT_LINEAR_ACCUM) || a.y, MT_ERR_ARG, "gemm_tc: ACCUM needs fp32 y");
+    TcEpi& e = plan->e;
+    e = TcEpi{};
     e.m = a.m; e.n = a.n; e.k = a.k;
-    e.bn = a.m <= 256 ? round16(a.m) : 128;
+    e.bn = a.bn_override > 0 ? a.bn_override : (a.m <= 256 ? round16(a.m) : 128);
     if (e.bn < 16) e.bn = 16;
+    MT_REQUIRE(ctx, e.bn % 16 == 0 && e.bn <= 256, MT_ERR_SHAPE, "gemm_tc: tile rows %d", e.bn);
     const uint32_t stage_bytes = TC_BM * 128 * (gated ? 2 : 1) + 2u * e.bn * 128;
     const uint32_t budget = 200 * 1024;
     e.stages = (int)(budget / stage_bytes);
@@ -324,22 +330,35 @@ mt_status launch_gemm_tc(mt_ctx* ctx, const LinearArgs& a, cudaStream_t s) {
     e.bias = a.bias; e.y = a.y; e.ldy = a.ldy; e.y_hi = a.y_hi; e.y_lo = a.y_lo; e.ld_ysplit = a.ld_ysplit;
     e.flags = a.flags; e.status = ctx->d_status;
 
-    CUtensorMap tw, tw2, th, tl;
-    bool ok = make_map(&tw, a.w, a.n, a.k, a.k, TC_BM);
-    ok = ok && make_map(&tw2, gated ? a.w2 : a.w, a.n, a.k, a.k, TC_BM);
-    ok = ok && make_map(&th, a.x_hi, a.m, a.k, a.ld_split, e.bn);
-    ok = ok && make_map(&tl, a.x_lo, a.m, a.k, a.ld_split, e.bn);
+    bool ok = make_map(&plan->tw, a.w, a.n, a.k, a.k, TC_BM);
+    ok = ok && make_map(&plan->tw2, gated ? a.w2 : a.w, a.n, a.k, a.k, TC_BM);
+    ok = ok && make_map(&plan->th, a.x_hi, a.m, a.k, a.ld_split, e.bn);
+    ok = ok && make_map(&plan->tl, a.x_lo, a.m, a.k, a.ld_split, e.bn);
     MT_REQUIRE(ctx, ok, MT_ERR_CUDA, "gemm_tc: cuTensorMapEncodeTiled failed (m %d n %d k %d)", a.m, a.n, a.k);
-
-    const size_t smem = (size_t)e.stages * stage_bytes + 1024;
-    dim3 grid((a.n + TC_BM - 1) / TC_BM, (a.m + e.bn - 1) / e.bn, split);
-    if (gated) {
-        cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        gemm_tc_kernel<true><<<grid, TC_THREADS, smem, s>>>(tw, tw2, th, tl, e);
-    } else {
-        cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        gemm_tc_kernel<false><<<grid, TC_THREADS, smem, s>>>(tw, tw2, th, tl, e);
+    plan->gated = gated;
+    plan->smem = (size_t)e.stages * stage_bytes + 1024;
+    plan->grid = dim3((a.n + TC_BM - 1) / TC_BM, (a.m + e.bn - 1) / e.bn, split);
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+        cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+        attr_set = true;
     }
+    return MT_OK;
+}
+
+void run_gemm_plan(const GemmPlan& p, cudaStream_t s) {
+    if (p.gated)
+        gemm_tc_kernel<true><<<p.grid, TC_THREADS, p.smem, s>>>(p.tw, p.tw2, p.th, p.tl, p.e);
+    else
+        gemm_tc_kernel<false><<<p.grid, TC_THREADS, p.smem, s>>>(p.tw, p.tw2, p.th, p.tl, p.e);
+}
+
+mt_status launch_gemm_tc(mt_ctx* ctx, const LinearArgs& a, cudaStream_t s) {
+    GemmPlan plan;
+    mt_status st = make_gemm_plan(ctx, a, &plan);
+    if (st != MT_OK) return st;
+    run_gemm_plan(plan, s);
     return check_launch(ctx, "gemm_tc");
 }
 

@@ -1,6 +1,8 @@
 // kernels.cuh -- argument blocks and launchers of the device kernels (internal to libmingcuda.so).
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace mt {
@@ -79,8 +81,34 @@ struct LinearArgs {
     uint16_t* y_hi; uint16_t* y_lo; int ld_ysplit;  // bf16 hi/lo output planes (optional)
     uint32_t flags;
     int split_k;                               // tensor-core route: >1 = atomically reduced K splits
+    int bn_override;                           // tensor-core route: activation rows per tile (0 = auto)
 };
 void launch_gemv(const LinearArgs& a, cudaStream_t s);
 mt_status launch_gemm_tc(mt_ctx* ctx, const LinearArgs& a, cudaStream_t s);
+
+// Epilogue/launch parameters of the tensor-core GEMM (gemm_tc.cu).
+struct TcEpi {
+    int m, n, k;
+    int bn;            // activation rows per tile (MMA N), multiple of 16, <= 256
+    int stages;
+    int kb_per_split;  // k blocks per blockIdx.z
+    const uint16_t* bias;
+    float* y; int ldy;
+    uint16_t* y_hi; uint16_t* y_lo; int ld_ysplit;
+    uint32_t flags;
+    int split;         // > 1: red.add fp32 partials into y (no activation allowed)
+    unsigned int* status;
+};
+
+// A tensor-core GEMM with its tensor maps encoded once; run_gemm_plan only launches.
+struct GemmPlan {
+    CUtensorMap tw, tw2, th, tl;
+    TcEpi e;
+    dim3 grid;
+    size_t smem;
+    bool gated;
+};
+mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan);
+void run_gemm_plan(const GemmPlan& p, cudaStream_t s);
 
 }  // namespace mt

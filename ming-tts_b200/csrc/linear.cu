@@ -229,4 +229,20 @@ mt_status mt_linear(mt_ctx* ctx, void* stream, const float* x, int ldx, int m, c
     return launch_gemm_tc(ctx, a, s);
 }
 
+mt_status mt_linear_split(mt_ctx* ctx, void* stream, const mt_bf16* x_hi, const mt_bf16* x_lo, int ld_x, int m,
+                          const mt_bf16* w, const mt_bf16* w2, const mt_bf16* bias, int n, int k, float* y, int ldy,
+                          mt_bf16* y_hi, mt_bf16* y_lo, int ld_ysplit, uint32_t flags) {
+    MT_REQUIRE(ctx, ctx && x_hi && x_lo && w && (y || (y_hi && y_lo)), MT_ERR_ARG, "mt_linear_split: null argument");
+    MT_REQUIRE(ctx, (flags & ~31u) == 0, MT_ERR_ARG, "mt_linear_split: unknown flag bits 0x%x", flags);
+    MT_REQUIRE(ctx, !(flags & MT_LINEAR_SILU_GATE) || w2, MT_ERR_ARG, "mt_linear_split: SILU_GATE needs w2");
+    MT_REQUIRE(ctx, m >= 0 && n > 0 && k > 0 && k % 8 == 0 && ld_x >= k && (!y || ldy >= n) &&
+                        (!y_hi || ld_ysplit >= n),
+               MT_ERR_SHAPE, "mt_linear_split: m %d n %d k %d ld_x %d", m, n, k, ld_x);
+    if (m == 0) return MT_OK;
+    LinearArgs a{};
+    a.x_hi = x_hi; a.x_lo = x_lo; a.ld_split = ld_x; a.m = m; a.n = n; a.k = k; a.w = w; a.w2 = w2; a.bias = bias;
+    a.y = y; a.ldy = ldy; a.y_hi = y_hi; a.y_lo = y_lo; a.ld_ysplit = ld_ysplit; a.flags = flags; a.split_k = 1;
+    return launch_gemm_tc(ctx, a, as_stream(stream));
+}
+
 }  // extern "C"

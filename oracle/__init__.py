@@ -25,7 +25,7 @@ class GenerateIO(ctypes.Structure):
                 ("noise", _P), ("initial_history", _P),
                 ("stop_logits", _P), ("llm_hidden", _P), ("latents", _P), ("agg_out", _P), ("velocity0", _P),
                 ("vae_hidden", _P), ("layer0_prefill", _P), ("layer_last_prefill", _P), ("pcm", _P),
-                ("pcm_cap", c_long), ("chunk_counts", _P),
+                ("pcm_cap", c_long), ("chunk_counts", _P), ("step_seconds", _P),
                 ("steps_run", c_int), ("stopped", c_int), ("pcm_count", c_long), ("chunks", c_int)]
 
 

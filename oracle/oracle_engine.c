@@ -10,6 +10,7 @@
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #include "oracle.h"
 #include "oracle_engine.h"
@@ -246,6 +247,11 @@ int or_generate(const mt_model_config* cfg, const mt_model_weights* w, or_genera
             chunks++;
             if (io->pcm && pcm_count + chunk <= io->pcm_cap) memcpy(io->pcm + pcm_count, vae.pcm, sizeof(float) * chunk);
             pcm_count += chunk;
+        }
+        if (io->step_seconds) {
+            struct timespec ts_now;
+            clock_gettime(CLOCK_MONOTONIC, &ts_now);
+            io->step_seconds[n] = (double)ts_now.tv_sec + 1e-9 * (double)ts_now.tv_nsec;
         }
         const float stop_prob = 1.0f / (1.0f + expf(logits[0] - logits[1]));
         if (io->obey_stop && stop_prob > 0.5f && n > 3) {

@@ -31,6 +31,7 @@ typedef struct {
     float* pcm;                   /* all emitted samples in order */
     long pcm_cap;
     int* chunk_counts;            /* [steps + 2] samples per emission */
+    double* step_seconds;         /* [steps] monotonic seconds at the end of each step (CPU timing) */
     /* results */
     int steps_run;
     int stopped;

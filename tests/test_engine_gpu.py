@@ -1,0 +1,174 @@
+"""GPU parity of the batched generation engine against the CPU oracle's reference loop.
+
+The engine runs R requests at once (stacked rows, tensor cores above 8 rows, two streams, CUDA
+graphs); the oracle restates MingEngine.generate (Engine.swift:302-415) for one request at a time on
+the same weights (a host copy of the engine's arena). Per request and step: LLM output z, stop
+logits, aggregator output, step-0 velocities, every latent, and the streamed waveform.
+Bar (north star): latents and waveform cosine >= 0.999 for the same noise; here also
+max|latent error| <= 1e-3 * max|latent| and per-step stop logits within 1e-3.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import cosine, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def oracle_generate(oracle, cfg, w_host, embeds, noise, steps, cfg_scale=2.0):
+    L, H, Hv = cfg.latent_dim, cfg.llm.hidden, cfg.vae.hidden
+    T = embeds.shape[0]
+    out = dict(stop=np.zeros((steps, 2), np.float32), z=np.zeros((steps, H), np.float32),
+               latents=np.zeros((steps, L), np.float32), agg=np.zeros((steps, H), np.float32),
+               vel0=np.zeros((cfg.flow_steps, 2, L), np.float32), vae_hidden=np.zeros((steps, 4, Hv), np.float32),
+               pcm=np.zeros(4 * cfg.hop * (steps + 1), np.float32), chunks=np.zeros(steps + 2, np.int32))
+    io = oracle.GenerateIO()
+    io.prompt_rows, io.embeds, io.steps, io.cfg, io.obey_stop = T, embeds.ctypes.data, steps, cfg_scale, 0
+    io.noise = noise.ctypes.data
+    io.stop_logits, io.llm_hidden, io.latents = out["stop"].ctypes.data, out["z"].ctypes.data, out["latents"].ctypes.data
+    io.agg_out, io.velocity0, io.vae_hidden = out["agg"].ctypes.data, out["vel0"].ctypes.data, out["vae_hidden"].ctypes.data
+    io.pcm, io.pcm_cap, io.chunk_counts = out["pcm"].ctypes.data, out["pcm"].size, out["chunks"].ctypes.data
+    assert oracle.lib().or_generate(ctypes.addressof(cfg), ctypes.addressof(w_host), ctypes.byref(io)) == 0
+    out["pcm"] = out["pcm"][:io.pcm_count]
+    out["chunks"] = out["chunks"][:io.chunks]
+    return out
+
+
+def engine_generate(mt, eng, cfg, embeds=None, ids=None, noise=None, steps=1, cfg_scale=2.0):
+    import torch
+    R, T = (embeds.shape[0], embeds.shape[1]) if embeds is not None else ids.shape
+    H, L = cfg.llm.hidden, cfg.latent_dim
+    eng.begin(R, T, embeds=dev(embeds) if embeds is not None else None,
+              token_ids=dev(ids) if ids is not None else None, noise=dev(noise), steps=steps, cfg=cfg_scale)
+    eng.prefill()
+    res = dict(stop=[], z=[], agg=[], pcm=[[] for _ in range(R)], chunks=[], vae_hidden=[])
+    for n in range(steps):
+        count = eng.step()
+        torch.cuda.synchronize()
+        res["stop"].append(eng.read(mt.BUF_STOP_LOGITS, R))
+        res["z"].append(eng.read(mt.BUF_Z, R))
+        res["agg"].append(eng.read(mt.BUF_AGG_OUT, R))
+        if count:
+            res["chunks"].append(count)
+            res["vae_hidden"].append(eng.read(mt.BUF_VAE_HIDDEN, R))
+            pcm = eng.read(mt.BUF_PCM, R, count)
+            for r in range(R):
+                res["pcm"][r].append(pcm[r])
+    while True:
+        count = eng.flush()
+        if not count:
+            break
+        torch.cuda.synchronize()
+        res["chunks"].append(count)
+        res["vae_hidden"].append(eng.read(mt.BUF_VAE_HIDDEN, R))
+        pcm = eng.read(mt.BUF_PCM, R, count)
+        for r in range(R):
+            res["pcm"][r].append(pcm[r])
+    res["latents"] = eng.read(mt.BUF_LATENTS, R).reshape(R, -1, L)[:, :steps]
+    res["vel0"] = eng.read(mt.BUF_VELOCITY0, R).reshape(R, cfg.flow_steps, 2, L)
+    res["stop"] = np.stack(res["stop"], 1)
+    res["z"] = np.stack(res["z"], 1)
+    res["agg"] = np.stack(res["agg"], 1)
+    res["pcm"] = [np.concatenate(p) for p in res["pcm"]]
+    res["vae_hidden"] = np.stack(res["vae_hidden"], 1).reshape(R, -1, 4, cfg.vae.hidden)
+    return res
+
+
+def compare(mt, oracle, ctx, cfg, R, T, steps, seed, use_graphs=True, use_ids=False, lat_rel=1e-3):
+    model = mt.Model(ctx, cfg, seed=seed)
+    host = model.arena_to_host()
+    tensors = model.tensors()
+    w_host, keep = mt.weights_struct(cfg, host.ctypes.data, tensors)
+    H, L = cfg.llm.hidden, cfg.latent_dim
+    rs = np.random.default_rng(seed)
+    noise = np.stack([oracle.gaussian_noise(steps * L, 1000 + r).reshape(steps, L) for r in range(R)])
+    if use_ids:
+        ids = rs.integers(0, cfg.vocab, size=(R, T), dtype=np.int32)
+        off = {t.name.decode(): t.offset for t in tensors}["model.model.embed_tokens.weight"]
+        table = host[off:off + cfg.vocab * H * 2].view(np.uint16).reshape(cfg.vocab, H)
+        embeds = oracle.bf16_to_f32(table[ids]).astype(np.float32)
+    else:
+        ids = None
+        embeds = (0.5 * rs.standard_normal((R, T, H))).astype(np.float32)
+    eng = mt.Engine(ctx, model, R, T, steps, use_graphs=use_graphs)
+    got = engine_generate(mt, eng, cfg, embeds=None if use_ids else embeds, ids=ids, noise=noise, steps=steps)
+    for r in range(R):
+        want = oracle_generate(oracle, cfg, w_host, np.ascontiguousarray(embeds[r]), np.ascontiguousarray(noise[r]), steps)
+        tag = f"R{R} request {r}"
+        assert list(got["chunks"]) == list(want["chunks"]), f"{tag}: emission counts"
+        assert rel_err(got["z"][r], want["z"]) < 1e-3, f"{tag}: llm hidden rel {rel_err(got['z'][r], want['z'])}"
+        assert np.abs(got["stop"][r] - want["stop"]).max() < 1e-3, f"{tag}: stop logits"
+        assert rel_err(got["vel0"][r], want["vel0"]) < 1e-3, f"{tag}: step-0 velocity"
+        assert rel_err(got["agg"][r], want["agg"]) < 1e-3, f"{tag}: aggregator out"
+        lat_c = cosine(got["latents"][r], want["latents"])
+        lat_e = rel_err(got["latents"][r], want["latents"])
+        assert lat_c >= 0.9999 and lat_e <= lat_rel, f"{tag}: latents cosine {lat_c} rel {lat_e}"
+        vh = got["vae_hidden"][r]
+        assert rel_err(vh, want["vae_hidden"][:vh.shape[0]]) < 2e-3, f"{tag}: vae hidden"
+        pc = cosine(got["pcm"][r], want["pcm"])
+        assert got["pcm"][r].shape == want["pcm"].shape and pc >= 0.999, f"{tag}: waveform cosine {pc}"
+    eng.close()
+    model.close()
+    return got
+
+
+def test_small_model_mixed_routes(ctx, mt, oracle):
+    # R = 3: LLM and aggregator rows on the GEMV, flow (18) and VAE (12) rows on the tensor cores.
+    compare(mt, oracle, ctx, mt.small_config(), R=3, T=5, steps=7, seed=3)
+
+
+def test_small_model_all_tensor_core(ctx, mt, oracle):
+    compare(mt, oracle, ctx, mt.small_config(), R=12, T=6, steps=6, seed=4, use_ids=True)
+
+
+def test_graph_replay_matches_eager(ctx, mt, oracle):
+    cfg = mt.small_config()
+    model = mt.Model(ctx, cfg, seed=5)
+    R, T, steps = 9, 4, 6
+    rs = np.random.default_rng(5)
+    embeds = (0.5 * rs.standard_normal((R, T, cfg.llm.hidden))).astype(np.float32)
+    noise = rs.standard_normal((R, steps, cfg.latent_dim)).astype(np.float32)
+    outs = []
+    for graphs in (False, True):
+        eng = mt.Engine(ctx, model, R, T, steps, use_graphs=graphs)
+        outs.append(engine_generate(mt, eng, cfg, embeds=embeds, noise=noise, steps=steps))
+        eng.close()
+    np.testing.assert_array_equal(outs[0]["latents"], outs[1]["latents"])
+    for a, b in zip(outs[0]["pcm"], outs[1]["pcm"]):
+        np.testing.assert_array_equal(a, b)
+
+
+def test_generate_host_api_matches_steps(ctx, mt, oracle):
+    cfg = mt.small_config()
+    model = mt.Model(ctx, cfg, seed=6)
+    R, T, steps = 4, 5, 5
+    rs = np.random.default_rng(6)
+    embeds = (0.5 * rs.standard_normal((R, T, cfg.llm.hidden))).astype(np.float32)
+    noise = rs.standard_normal((R, steps, cfg.latent_dim)).astype(np.float32)
+    eng = mt.Engine(ctx, model, R, T, steps)
+    pcm, stop = eng.generate(R, T, noise, steps, embeds_host=embeds)
+    ref = engine_generate(mt, eng, cfg, embeds=embeds, noise=noise, steps=steps)
+    assert pcm.shape == (R, 4 * cfg.hop * steps)
+    for r in range(R):
+        np.testing.assert_allclose(pcm[r], ref["pcm"][r], rtol=0, atol=1e-6)
+        p = 1.0 / (1.0 + np.exp(ref["stop"][r][:, 0] - ref["stop"][r][:, 1]))
+        np.testing.assert_allclose(stop[r], p, atol=1e-6)
+
+
+def test_full_model_parity(ctx, mt, oracle):
+    # Reference dimensions (Ming-3.0-tts-0.5B), two requests, four steps and the flush.
+    compare(mt, oracle, ctx, mt.default_config(), R=2, T=8, steps=4, seed=1, use_ids=True)
+
+
+def test_full_model_batched_parity(ctx, mt, oracle):
+    # Enough requests that every stack (LLM 12 rows, flow 72, aggregator 24, VAE 48) is on the tensor cores.
+    compare(mt, oracle, ctx, mt.default_config(), R=12, T=4, steps=3, seed=2, use_ids=True)

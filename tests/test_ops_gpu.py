@@ -183,7 +183,7 @@ def test_istft_matches_direct_overlap_add(ctx, oracle):
     c = ctx.call
     c("istft_frames", specd, 2 * bins, 4, nfft, None, wd, frd, 0, ring)
     c("istft_emit", frd, wd, nfft, hop, 0, 4 * hop - pad, 3, ring, outd)
-    c("istft_frames", specd[4 * 2 * bins:], 2 * bins, 4, nfft, None, wd, frd, 4, ring)
+    c("istft_frames", specd[4:], 2 * bins, 4, nfft, None, wd, frd, 4, ring)
     c("istft_emit", frd, wd, nfft, hop, 4 * hop - pad, 4 * hop, 7, ring, outd[4 * hop - pad:])
     c("istft_emit", frd, wd, nfft, hop, 8 * hop - pad, pad, 7, ring, outd[8 * hop - pad:])
     ctx.check()

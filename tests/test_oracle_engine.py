@@ -1,0 +1,68 @@
+"""CPU checks of the oracle's generation loop and of the model tensor table (no GPU)."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from test_engine_gpu import oracle_generate
+
+
+def host_arena(mt, oracle, cfg, seed):
+    """Builds the model arena on the host from the tensor table, with the oracle's generator."""
+    tensors = mt.tensor_table(cfg, seed)
+    nbytes = mt.lib().mt_model_arena_bytes(ctypes.byref(cfg), 1)
+    arena = np.zeros(nbytes, np.uint8)
+    for t in tensors:
+        if t.dtype == mt.MT_DTYPE_BF16:
+            view = arena[t.offset:t.offset + 2 * t.numel].view(np.uint16)
+            view[:] = 0x3F80 if t.init == 1 else oracle.randn_bf16(t.numel, t.seed, t.std)
+        else:
+            view = arena[t.offset:t.offset + 4 * t.numel].view(np.float32)
+            if t.init == 0:
+                view[:] = oracle.bf16_to_f32(oracle.randn_bf16(t.numel, t.seed, t.std))
+            elif t.init == 2:
+                view[:] = (1.0 / np.power(10000.0, 2 * np.arange(t.numel) / 64.0)).astype(np.float32)
+            elif t.init == 3:
+                view[:] = (0.5 - 0.5 * np.cos(2 * np.pi * np.arange(t.numel) / t.numel)).astype(np.float32)
+    return arena, tensors
+
+
+def test_tensor_table_layout(mt):
+    cfg = mt.default_config()
+    t = mt.tensor_table(cfg)
+    names = [x.name.decode() for x in t]
+    assert len(names) == len(set(names))
+    assert all(x.offset % 256 == 0 for x in t)
+    assert all(a.offset + a.numel * (2 if a.dtype == 0 else 4) <= b.offset for a, b in zip(t, t[1:]))
+    # The per-step weights of Ming-3.0-tts-0.5B (LLM + flow + aggregator + VAE decoder): ~0.92 B parameters.
+    per_step = sum(x.numel for x in t if not x.name.startswith(b"model.model.embed_tokens"))
+    assert 0.90e9 < per_step < 0.95e9
+    qkv = next(x for x in t if x.name == b"model.model.layers.0.self_attn.qkv_proj.weight")
+    assert qkv.numel == (14 + 2 * 2) * 64 * 896
+
+
+def test_oracle_generation_bookkeeping(mt, oracle):
+    cfg = mt.small_config()
+    arena, tensors = host_arena(mt, oracle, cfg, seed=3)
+    w, keep = mt.weights_struct(cfg, arena.ctypes.data, tensors)
+    steps, T = 5, 4
+    rs = np.random.default_rng(0)
+    embeds = (0.5 * rs.standard_normal((T, cfg.llm.hidden))).astype(np.float32)
+    noise = oracle.gaussian_noise(steps * cfg.latent_dim, 7).reshape(steps, cfg.latent_dim)
+    a = oracle_generate(oracle, cfg, w, embeds, noise, steps)
+    b = oracle_generate(oracle, cfg, w, embeds, noise, steps)
+    hop, pad = cfg.hop, (cfg.nfft - cfg.hop) // 2
+    # Emissions: latent 0 at step 2 (4 hops minus the pad), then 4 hops each, the last adds the pad
+    # (VAEDecoder.swift:93-99); total = 4 hops per latent.
+    assert list(a["chunks"]) == [4 * hop - pad] + [4 * hop] * (steps - 2) + [4 * hop + pad]
+    assert a["pcm"].size == 4 * hop * steps
+    np.testing.assert_array_equal(a["pcm"], b["pcm"])
+    np.testing.assert_array_equal(a["latents"], b["latents"])
+    assert np.isfinite(a["pcm"]).all() and np.abs(a["pcm"]).max() > 0
+    # The latent history feeds the next step: different noise at step 1 changes latent 1 only from there on.
+    noise2 = noise.copy()
+    noise2[1] += 1.0
+    c = oracle_generate(oracle, cfg, w, embeds, noise2, steps)
+    np.testing.assert_array_equal(a["latents"][0], c["latents"][0])
+    assert not np.allclose(a["latents"][1], c["latents"][1])
