@@ -149,8 +149,9 @@ def request_inputs(mt, cfg, requests, prompt, steps, first_request):
 # ------------------------------------------------------------------------------------------------
 # Kernel-level measurements
 # ------------------------------------------------------------------------------------------------
-def time_gemm(mt, ctx, m, n, k, flags, iters=200):
-    """Average duration of the tcgen05 GEMM at one shape (CUDA events, launches back to back)."""
+def time_gemm(mt, ctx, m, n, k, flags, iters=100, rounds=3):
+    """Average duration of the tcgen05 GEMM at one shape: `iters` launches replayed from a CUDA
+    graph (so host launch cost is not measured), CUDA events, best of `rounds`."""
     import torch
     g = torch.Generator(device="cuda").manual_seed(0)
     xh = (torch.randn(m, k, device="cuda", generator=g)).to(torch.bfloat16)
@@ -160,17 +161,28 @@ def time_gemm(mt, ctx, m, n, k, flags, iters=200):
     yh = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
     yl = torch.empty_like(yh)
     args = (xh, xl, k, m, w, None, b, n, k, None, 0, yh, yl, n, flags | mt.BIAS)
-    for _ in range(5):
-        ctx.call("linear_split", *args)
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(iters):
-        ctx.call("linear_split", *args)
-    e.record()
-    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            ctx.call("linear_split", *args)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(iters):
+                ctx.call("linear_split", *args)
+        graph.replay()
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(rounds):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            graph.replay()
+            e.record(stream)
+            e.synchronize()
+            t = s.elapsed_time(e) * 1e-3 / iters
+            best = t if best is None else min(best, t)
     ctx.check()
-    return s.elapsed_time(e) / iters * 1e-3
+    return best
 
 
 def time_gemv_pool(mt, ctx, n, k, m=2, pool_bytes=1 << 30, rounds=3):
@@ -299,9 +311,22 @@ def main():
     ap.add_argument("--cpu-prompt", type=int, default=16)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--gemm", type=str, default="",
+                    help="M,N,K[,flags]: time one tensor-core GEMM shape alone and exit (for focused profiling)")
+    ap.add_argument("--profile", action="store_true",
+                    help="prefill, warm-up and timed steps only (for a profiler's launch list); prints ms/step")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
     rank, world, local = dist_setup(args)
+    if args.gemm:
+        mt = load_package()
+        ctx = mt.Context(local)
+        f = [int(v) for v in args.gemm.split(",")]
+        m, n, k, flags = f[0], f[1], f[2], (f[3] if len(f) > 3 else 0)
+        t = time_gemm(mt, ctx, m, n, k, flags, iters=20, rounds=1)
+        print(json.dumps({"gemm": [m, n, k, flags], "us": round(t * 1e6, 2),
+                          "tflops": round(2.0 * m * n * k / t / 1e12, 1)}), flush=True)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         barrier(world)
@@ -329,6 +354,8 @@ def main():
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     kernels = 0
+    if args.profile:
+        torch.cuda.cudart().cudaProfilerStart()  # a profiler started with --profile-from-start off sees only these steps
     with ClockSampler(local) as clocks:
         start.record(stream)
         for _ in range(args.steps):
@@ -336,10 +363,17 @@ def main():
             kernels += mt.lib().mt_engine_step_kernels(eng.handle)
         end.record(stream)
         end.synchronize()
+    if args.profile:
+        torch.cuda.cudart().cudaProfilerStop()
     ctx.check()
     t_local = start.elapsed_time(end) * 1e-3
     t_max = dist_max(t_local, world)
     value = world * R * args.steps * AUDIO_PER_STEP / t_max
+    if args.profile:
+        if rank == 0:
+            print(json.dumps({"profile": True, "ms_per_step": round(t_max / args.steps * 1e3, 3),
+                              "kernels_per_step": kernels // max(args.steps, 1)}), flush=True)
+        return
 
     # ---- end to end through the host API ----
     E = args.e2e_steps

@@ -53,7 +53,15 @@ __device__ __forceinline__ uint16_t f32_to_bf16_rne(float x) {
     return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
-// Two-term bf16 split of an fp32 value: x ~= hi + lo with |x - hi - lo| <= 2^-16 |x|.
+// Hardware round-to-nearest-even fp32 -> bf16 (same result as f32_to_bf16_rne for finite values).
+__device__ __forceinline__ uint16_t cvt_bf16_rn(float x) {
+    uint16_t r;
+    asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(x));
+    return r;
+}
+
+// Two-term bf16 split of an fp32 value: x ~= hi + lo with |x - hi - lo| <= 2^-17 |x|. Integer
+// rounding (the integer pipe has four times the throughput of the conversion unit).
 __device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) {
     hi = f32_to_bf16_rne(x);
     lo = f32_to_bf16_rne(x - bf16f(hi));
@@ -70,14 +78,17 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// GELU (tanh form) with the reference's +-15 clamp (Shaders.swift:23-27).
+// GELU (tanh form) with the reference's +-15 clamp (Shaders.swift:23-27), evaluated through the
+// identity 0.5 (1 + tanh(u)) = 1 / (1 + exp(-2u)): one exponential, no cancellation for negative x,
+// relative error a few fp32 ulps.
 __device__ __forceinline__ float gelu_tanh(float x) {
     const float k = 0.7978845608028654f;
     float u = k * (x + 0.044715f * x * x * x);
     u = fminf(fmaxf(u, -15.0f), 15.0f);
-    return 0.5f * x * (1.0f + tanhf(u));
+    return __fdividef(x, 1.0f + __expf(-2.0f * u));
 }
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+// x * sigmoid(x); __fdividef returns 0 for denominators above 2^126, the right limit for x << 0.
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // Streaming 16-byte weight load: read once, do not pollute L1.
 __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {

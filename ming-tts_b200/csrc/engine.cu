@@ -15,6 +15,7 @@
 #include <math.h>
 #include <string.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "common.cuh"
@@ -87,6 +88,9 @@ struct mt_engine {
     int max_chunk = 0;
     int* state_dev = nullptr;
     int* state_host = nullptr;  // pinned
+    float* ws_a = nullptr;      // split-K workspace of the main stream (LLM, flow, aggregator)
+    float* ws_b = nullptr;      // split-K workspace of the VAE stream
+    size_t ws_a_floats = 0, ws_b_floats = 0;
 
     // Current generation.
     int R = 0, T = 0, steps = 0;
@@ -101,13 +105,13 @@ struct mt_engine {
     std::vector<DitBlockPlans> flow_blocks, agg_blocks;
     Lin cond, agg_final, vae_head, stop_lin;
 
+    cudaStream_t sa = nullptr;  // step stream (owned, capturable; joined to the caller's stream)
     cudaStream_t sb = nullptr;  // VAE stream
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_in = nullptr, ev_out = nullptr;
     int step_kernels = 0;       // kernels of the last step
     int graph_kernels = 0;      // kernels in the captured step graph
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
-    cudaStream_t graph_stream = nullptr;
 };
 
 namespace {
@@ -166,9 +170,11 @@ mt_status dit_alloc(mt_engine* e, DitBufs* d, const mt_dit_config& c, size_t row
 // A linear over m rows of x: CUDA-core GEMV (fp32 x.f) for m <= 8, else a tcgen05 plan (x.hi/lo).
 // `y` receives fp32 output; `ys` (optional) receives the activation for a following linear in the
 // representation that linear's route reads.
+// Tensor-core linears split K automatically to fill the SMs; a nonlinear epilogue then reduces
+// through the stream's fp32 workspace (ws, ws_floats) when it is large enough.
 mt_status make_lin(mt_engine* e, Lin* L, const Act& x, int m, const mt_bf16* w, const mt_bf16* w2,
                    const mt_bf16* bias, int n, int k, float* y, int ldy, const Act* ys, uint32_t flags,
-                   int split = 1) {
+                   float* ws = nullptr, size_t ws_floats = 0) {
     LinearArgs a{};
     a.m = m; a.n = n; a.k = k; a.w = w; a.w2 = w2; a.bias = bias; a.flags = flags | (bias ? MT_LINEAR_BIAS : 0);
     a.split_k = 1;
@@ -186,7 +192,8 @@ mt_status make_lin(mt_engine* e, Lin* L, const Act& x, int m, const mt_bf16* w, 
     } else {
         a.y = y; a.ldy = ldy;
     }
-    a.split_k = split;
+    a.split_k = 0;
+    a.ws = ws && (size_t)m * 2 * n <= ws_floats ? ws : nullptr;
     return make_gemm_plan(e->ctx, a, &L->p);
 }
 
@@ -209,7 +216,8 @@ void norm(const float* x, int ldx, int rows, int width, const mt_bf16* w, float 
     g_kernels++;
 }
 
-mt_status plan_qwen(mt_engine* e, std::vector<QwenLayerPlans>& plans, const mt_qwen_weights& W, QwenBufs& b, int rows) {
+mt_status plan_qwen(mt_engine* e, std::vector<QwenLayerPlans>& plans, const mt_qwen_weights& W, QwenBufs& b, int rows,
+                    float* ws, size_t ws_floats) {
     const mt_qwen_config& c = W.cfg;
     const int qkvw = (c.heads + 2 * c.kv_heads) * 64;
     plans.resize(c.layers);
@@ -219,14 +227,15 @@ mt_status plan_qwen(mt_engine* e, std::vector<QwenLayerPlans>& plans, const mt_q
         TRY(make_lin(e, &plans[l].o, b.attn, rows, L.o_w, nullptr, nullptr, c.hidden, c.heads * 64, b.x, c.hidden,
                      nullptr, MT_LINEAR_ACCUM));
         TRY(make_lin(e, &plans[l].gu, b.norm, rows, L.gate_w, L.up_w, nullptr, c.intermediate, c.hidden, nullptr, 0,
-                     &b.mlp, MT_LINEAR_SILU_GATE));
+                     &b.mlp, MT_LINEAR_SILU_GATE, ws, ws_floats));
         TRY(make_lin(e, &plans[l].down, b.mlp, rows, L.down_w, nullptr, nullptr, c.hidden, c.intermediate, b.x,
                      c.hidden, nullptr, MT_LINEAR_ACCUM));
     }
     return MT_OK;
 }
 
-mt_status plan_dit(mt_engine* e, std::vector<DitBlockPlans>& plans, const mt_dit_weights& W, DitBufs& b, int rows) {
+mt_status plan_dit(mt_engine* e, std::vector<DitBlockPlans>& plans, const mt_dit_weights& W, DitBufs& b, int rows,
+                   float* ws, size_t ws_floats) {
     const mt_dit_config& c = W.cfg;
     plans.resize(c.depth);
     for (int i = 0; i < c.depth; i++) {
@@ -236,7 +245,7 @@ mt_status plan_dit(mt_engine* e, std::vector<DitBlockPlans>& plans, const mt_dit
         TRY(make_lin(e, &plans[i].out, b.attn, rows, B.out_w, nullptr, B.out_b, c.hidden, c.hidden, b.x, c.hidden,
                      nullptr, MT_LINEAR_ACCUM));
         TRY(make_lin(e, &plans[i].ff1, b.norm, rows, B.ff1_w, nullptr, B.ff1_b, c.ff, c.hidden, nullptr, 0, &b.ff,
-                     MT_LINEAR_GELU));
+                     MT_LINEAR_GELU, ws, ws_floats));
         TRY(make_lin(e, &plans[i].ff2, b.ff, rows, B.ff2_w, nullptr, B.ff2_b, c.hidden, c.ff, b.x, c.hidden, nullptr,
                      MT_LINEAR_ACCUM));
     }
@@ -247,8 +256,8 @@ mt_status build_plans(mt_engine* e) {
     if (e->plan_R == e->R && e->plan_T == e->T) return MT_OK;
     const int R = e->R, T = e->T;
     const mt_model_config& c = e->cfg;
-    TRY(plan_qwen(e, e->llm_dec, e->w.llm, e->llm, R));
-    TRY(plan_qwen(e, e->llm_pre, e->w.llm, e->llm, R * T));
+    TRY(plan_qwen(e, e->llm_dec, e->w.llm, e->llm, R, e->ws_a, e->ws_a_floats));
+    TRY(plan_qwen(e, e->llm_pre, e->w.llm, e->llm, R * T, e->ws_a, e->ws_a_floats));
     TRY(make_lin(e, &e->cond, e->z, R, e->w.flow_c_w, nullptr, e->w.flow_c_b, c.flow.hidden, c.llm.hidden, e->cemb,
                  c.flow.hidden, nullptr, 0));
     {
@@ -259,11 +268,11 @@ mt_status build_plans(mt_engine* e) {
         e->stop_lin.tc = false;
         e->stop_lin.g = a;
     }
-    TRY(plan_dit(e, e->flow_blocks, e->w.flow, e->flow, 6 * R));
-    TRY(plan_dit(e, e->agg_blocks, e->w.agg, e->agg, 2 * R));
+    TRY(plan_dit(e, e->flow_blocks, e->w.flow, e->flow, 6 * R, e->ws_a, e->ws_a_floats));
+    TRY(plan_dit(e, e->agg_blocks, e->w.agg, e->agg, 2 * R, e->ws_a, e->ws_a_floats));
     TRY(make_lin(e, &e->agg_final, e->agg_norm, R, e->w.agg.final_w, nullptr, e->w.agg.final_b, c.agg.out_dim,
                  c.agg.hidden, e->llm.x, c.llm.hidden, nullptr, 0));
-    TRY(plan_qwen(e, e->vae_layers, e->w.vae, e->vae, 4 * R));
+    TRY(plan_qwen(e, e->vae_layers, e->w.vae, e->vae, 4 * R, e->ws_b, e->ws_b_floats));
     TRY(make_lin(e, &e->vae_head, e->vae_hidden, 4 * R, e->w.vae_head_w, nullptr, e->w.vae_head_b, c.nfft + 2,
                  c.vae.hidden, e->spec, c.nfft + 2, nullptr, 0));
     e->plan_R = R;
@@ -532,12 +541,20 @@ mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_o
     e->max_chunk = 4 * c.hop + (c.nfft - c.hop) / 2;
     ETRY(dalloc(e, &e->pcm, (size_t)R * e->max_chunk));
     ETRY(dalloc(e, &e->state_dev, (size_t)st_size(R)));
+    e->ws_a_floats = std::max({(size_t)R * 2 * c.llm.intermediate, (size_t)6 * R * 2 * c.flow.ff,
+                               (size_t)2 * R * 2 * c.agg.ff});
+    e->ws_b_floats = (size_t)4 * R * 2 * c.vae.intermediate;
+    ETRY(dalloc(e, &e->ws_a, e->ws_a_floats));
+    ETRY(dalloc(e, &e->ws_b, e->ws_b_floats));
     if (cudaMallocHost(&e->state_host, st_size(R) * sizeof(int)) != cudaSuccess)
         return cleanup(fail(ctx, MT_ERR_NOMEM, "engine: pinned step state"));
     memset(e->state_host, 0, st_size(R) * sizeof(int));
-    if (cudaStreamCreateWithFlags(&e->sb, cudaStreamNonBlocking) != cudaSuccess ||
+    if (cudaStreamCreateWithFlags(&e->sa, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&e->sb, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&e->ev_join, cudaEventDisableTiming) != cudaSuccess)
+        cudaEventCreateWithFlags(&e->ev_join, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->ev_out, cudaEventDisableTiming) != cudaSuccess)
         return cleanup(fail(ctx, MT_ERR_CUDA, "engine: stream/event creation"));
     ETRY(precompute_temb(e));
 #undef ETRY
@@ -549,9 +566,12 @@ void mt_engine_destroy(mt_engine* e) {
     if (!e) return;
     if (e->graph_exec) cudaGraphExecDestroy(e->graph_exec);
     if (e->graph) cudaGraphDestroy(e->graph);
+    if (e->sa) cudaStreamDestroy(e->sa);
     if (e->sb) cudaStreamDestroy(e->sb);
     if (e->ev_fork) cudaEventDestroy(e->ev_fork);
     if (e->ev_join) cudaEventDestroy(e->ev_join);
+    if (e->ev_in) cudaEventDestroy(e->ev_in);
+    if (e->ev_out) cudaEventDestroy(e->ev_out);
     if (e->state_host) cudaFreeHost(e->state_host);
     for (void* p : e->allocs) cudaFree(p);
     delete e;
@@ -621,10 +641,11 @@ mt_status mt_engine_step(mt_engine* e, void* stream, int* pcm_count) {
     mt_ctx* ctx = e->ctx;
     MT_REQUIRE(ctx, e->prefilled, MT_ERR_STATE, "mt_engine_step: prefill first");
     MT_REQUIRE(ctx, e->n < e->steps, MT_ERR_STATE, "mt_engine_step: all %d steps done", e->steps);
-    cudaStream_t s = as_stream(stream);
+    cudaStream_t caller = as_stream(stream);
+    cudaStream_t s = e->sa;
     const int R = e->R, n = e->n;
     int* st = e->state_host;
-    // The previous step's upload may still be pending on the device: wait before rewriting.
+    // The previous step's state upload may still be pending on the device: wait before rewriting.
     cudaStreamSynchronize(s);
     st[ST_N] = n;
     for (int r = 0; r < R; r++) st[st_llm_pos(R) + r] = e->T + n - 1;
@@ -635,23 +656,21 @@ mt_status mt_engine_step(mt_engine* e, void* stream, int* pcm_count) {
     else st[ST_D] = -1;
     const bool with_llm = n > 0;
     const bool steady = with_llm && with_decode;
+    // The step runs on the engine's own stream, ordered after the caller's work and joined back.
+    cudaEventRecord(e->ev_in, caller);
+    cudaStreamWaitEvent(s, e->ev_in, 0);
     if (steady && e->opt.use_graphs) {
-        if (!e->graph_exec || e->graph_stream != s) {
-            if (e->graph_exec) {
-                cudaGraphExecDestroy(e->graph_exec);
-                cudaGraphDestroy(e->graph);
-                e->graph_exec = nullptr;
-            }
-            cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+        if (!e->graph_exec) {
+            cudaError_t err = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+            if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph capture: %s", cudaGetErrorString(err));
             upload_state(e, s);
             g_kernels = 0;
             enqueue_step(e, s, true, true);
             e->graph_kernels = g_kernels;
-            cudaError_t err = cudaStreamEndCapture(s, &e->graph);
+            err = cudaStreamEndCapture(s, &e->graph);
             if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph capture: %s", cudaGetErrorString(err));
             err = cudaGraphInstantiate(&e->graph_exec, e->graph, 0);
             if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph instantiate: %s", cudaGetErrorString(err));
-            e->graph_stream = s;
         }
         cudaGraphLaunch(e->graph_exec, s);
         e->step_kernels = e->graph_kernels;
@@ -661,6 +680,8 @@ mt_status mt_engine_step(mt_engine* e, void* stream, int* pcm_count) {
         enqueue_step(e, s, with_llm, with_decode);
         e->step_kernels = g_kernels;
     }
+    cudaEventRecord(e->ev_out, s);
+    cudaStreamWaitEvent(caller, e->ev_out, 0);
     e->latents_fed++;
     e->n++;
     if (pcm_count) *pcm_count = count;

@@ -3,19 +3,22 @@
 //
 // Reference semantics: the tiled GEMM and gemm8 kernels (Shaders.swift:191-277, 304-408) -- fp32
 // activations times bf16 weights with fp32 accumulation and the linear epilogue. Tensor cores
-// take bf16 operands, so the activations enter as x = hi + lo (both bf16, |x - hi - lo| <= 2^-17|x|)
-// and every K step issues two MMAs (W.hi, W.lo) into the same fp32 TMEM accumulator; the
-// weights are exact in bf16. The result matches fp32 FMA accumulation to ~1e-5 relative.
+// take bf16 operands, so the activations enter as x = hi + lo (both bf16, |x - hi - lo| <= 2^-17|x|);
+// the two planes sit next to each other in shared memory, so one MMA of N = 2 bn computes W.hi and
+// W.lo side by side in TMEM and the epilogue adds them. The weights are exact in bf16. The result
+// matches fp32 FMA accumulation to ~1e-5 relative.
 //
-// Layout ("swap AB"): the MMA's M side is 128 weight rows (output columns n), its N side is up to
-// 256 activation rows (m), so small row counts still use full 128-lane MMAs. The accumulator is
-// D[n_local][m_local] in TMEM (lane = weight row, column = activation row); the epilogue warp w
-// owns TMEM lanes 32w..32w+31 and writes Y rows coalesced along n.
+// Layout ("swap AB"): the MMA's M side is 128 weight rows (output columns n), its N side is
+// 2 x bn activation rows (m), so small row counts still use full 128-lane MMAs. The accumulator is
+// D[n_local][m_local] in TMEM (lane = weight row, column = activation row).
 //
-// Pipeline: warp 0 lane 0 issues TMA loads (128B swizzle, no multicast) into a ring of stages;
-// warp 1 lane 0 issues tcgen05.mma and frees each stage with tcgen05.commit; all four warps run the
-// epilogue once the final commit lands. Every mbarrier wait is bounded: a wait that gives up
-// writes the context status word and the block skips the rest of its work.
+// Persistent schedule: one CTA per SM walks its share of the (n tile, m tile, k split) space.
+// Warp 0 lane 0 issues TMA loads (128B swizzle, no multicast) into a ring of stages shared by all
+// of the CTA's tiles; warp 1 lane 0 issues tcgen05.mma into one of two TMEM accumulators and frees
+// stages with tcgen05.commit; warps 2-9 (two per TMEM lane quadrant) drain the other accumulator
+// through the epilogue, so the epilogue of tile t overlaps the loads and MMAs of tile t + 1.
+// Every mbarrier wait is bounded: a wait that gives up writes the context status word, raises the
+// CTA's abort flag (all other waits then return at once) and the CTA stops issuing work.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -24,7 +27,8 @@
 
 namespace mt {
 
-constexpr int TC_THREADS = 128;
+constexpr int TC_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (warp 2 owns TMEM)
+constexpr int TC_EPI_WARPS = 8;
 constexpr int TC_BM = 128;  // weight rows per tile (MMA M)
 constexpr int TC_BK = 64;   // bf16 K per stage = one 128-byte swizzle span
 constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait
@@ -51,8 +55,10 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 // Bounded wait on the phase with the given parity: gives up after WAIT_NS of wall time (checked
-// every 256 polls), records the site in the status word and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status, unsigned site) {
+// every 256 polls) or as soon as another thread of the CTA has raised *abort; a wait that times out
+// records the site in the status word, raises *abort and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status, unsigned site,
+                                          volatile int* abort) {
     const uint32_t addr = smem_u32(bar);
     uint64_t t0 = 0;
     for (uint32_t i = 0;; i++) {
@@ -65,14 +71,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
             : "r"(addr), "r"(parity)
             : "memory");
         if (ok) return true;
-        if ((i & 255u) == 0) {
+        if ((i & 255u) == 255u) {
+            if (*abort) return false;
             const uint64_t now = global_ns();
             if (t0 == 0) t0 = now;
             else if (now - t0 > WAIT_NS) break;
         }
     }
-    report_status(status, DEV_TIMEOUT, site, blockIdx.x | (blockIdx.y << 16));
+    report_status(status, DEV_TIMEOUT, site, blockIdx.x);
+    *abort = 1;
     return false;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
@@ -115,16 +127,114 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
+// 16 consecutive accumulator columns of this thread's TMEM lane; pair with tmem_wait() before use.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Tile t of the plan: k split z = t / (tiles_m * tiles_n); inside a split, consecutive tiles walk
+// the m tiles of one n tile (CTAs running together share weight tiles in L2).
+struct TileCoord { int n0, m0, kb_begin, kb_end; };
+__device__ __forceinline__ TileCoord tile_coord(const TcEpi& e, int t) {
+    const int per_split = e.tiles_m * e.tiles_n;
+    const int z = t / per_split, r = t % per_split;
+    TileCoord c;
+    c.m0 = (r % e.tiles_m) * e.bn;
+    c.n0 = (r / e.tiles_m) * TC_BM;
+    const int kb_total = (e.k + TC_BK - 1) / TC_BK;
+    c.kb_begin = z * e.kb_per_split;
+    c.kb_end = min(kb_total, c.kb_begin + e.kb_per_split);
+    return c;
+}
+
+// Epilogue of one tile for one warp: 16-column chunks `part`, `part + 2`, ... of TMEM lane quadrant
+// `quad` (weight rows n0 + 32 quad + lane).
+template <bool GATED>
+__device__ __forceinline__ void epilogue_tile(const TcEpi& e, const TileCoord& tc, uint32_t acc, int quad, int part,
+                                              int lane, bool first_split) {
+    const int n = tc.n0 + quad * 32 + lane;
+    const bool live_n = n < e.n;
+    const bool add_bias = (e.flags & MT_LINEAR_BIAS) && live_n && (e.mode == 0 || (e.mode == 1 && first_split));
+    const float bval = add_bias ? bf16f(e.bias[n]) : 0.f;
+    const uint32_t lane_base = acc + ((uint32_t)(quad * 32) << 16);
+    for (int c0 = part * 16; c0 < e.bn; c0 += 32) {
+        uint32_t rh[16], rl[16], r2h[16], r2l[16];
+        tmem_ld16(lane_base + c0, rh);
+        tmem_ld16(lane_base + e.bn + c0, rl);
+        if (GATED) {
+            tmem_ld16(lane_base + 2 * e.bn + c0, r2h);
+            tmem_ld16(lane_base + 3 * e.bn + c0, r2l);
+        }
+        tmem_wait();
+        if (!live_n) continue;
+        const int valid = min(16, e.m - (tc.m0 + c0));  // activation rows of this chunk inside M
+        if (valid <= 0) continue;
+        float val[16], val2[16];
 #pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+        for (int j = 0; j < 16; j++) {
+            val[j] = __uint_as_float(rh[j]) + __uint_as_float(rl[j]);
+            val2[j] = GATED ? __uint_as_float(r2h[j]) + __uint_as_float(r2l[j]) : 0.f;
+        }
+        const size_t row0 = (size_t)(tc.m0 + c0);
+        if (e.mode == 1) {  // split-K, linear epilogue: reduce into y (zeroed or the residual)
+            float* __restrict__ yp = e.y + row0 * e.ldy + n;
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+                if (j < valid) atomicAdd(yp + (size_t)j * e.ldy, val[j] + bval);
+            continue;
+        }
+        if (e.mode == 2) {  // split-K, nonlinear epilogue: raw sums into the workspace
+            float* __restrict__ wp = e.ws + row0 * e.ldws + n;
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                if (j < valid) {
+                    atomicAdd(wp + (size_t)j * e.ldws, val[j]);
+                    if (GATED) atomicAdd(wp + (size_t)j * e.ldws + e.n, val2[j]);
+                }
+            }
+            continue;
+        }
+        const bool accum = (e.flags & MT_LINEAR_ACCUM) && e.y;
+        float old[16];
+        if (accum) {
+            const float* __restrict__ yp = e.y + row0 * e.ldy + n;
+#pragma unroll
+            for (int j = 0; j < 16; j++) old[j] = j < valid ? yp[(size_t)j * e.ldy] : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            float v = val[j] + bval;
+            if (GATED) v = silu(v) * val2[j];
+            if (e.flags & MT_LINEAR_GELU) v = gelu_tanh(v);
+            if (e.flags & MT_LINEAR_SILU) v = silu(v);
+            if (accum) v += old[j];
+            val[j] = v;
+        }
+        if (e.y) {
+            float* __restrict__ yp = e.y + row0 * e.ldy + n;
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+                if (j < valid) yp[(size_t)j * e.ldy] = val[j];
+        }
+        if (e.y_hi) {
+            uint16_t* __restrict__ hp = e.y_hi + row0 * e.ld_ysplit + n;
+            uint16_t* __restrict__ lp = e.y_lo + row0 * e.ld_ysplit + n;
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                uint16_t h, l;
+                split_bf16(val[j], h, l);
+                if (j < valid) {
+                    hp[(size_t)j * e.ld_ysplit] = h;
+                    lp[(size_t)j * e.ld_ysplit] = l;
+                }
+            }
+        }
+    }
 }
 
 template <bool GATED>
@@ -132,30 +242,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
                    const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo, TcEpi e) {
     extern __shared__ __align__(1024) uint8_t dsmem[];
-    __shared__ uint64_t full_bar[8], empty_bar[8], done_bar;
+    __shared__ uint64_t full_bar[8], empty_bar[8], acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_holder;
     __shared__ int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * TC_BM, m0 = blockIdx.y * e.bn;
-    const int kb_total = (e.k + TC_BK - 1) / TC_BK;
-    const int kb_begin = blockIdx.z * e.kb_per_split;
-    const int kb_end = min(kb_total, kb_begin + e.kb_per_split);
     const int S = e.stages;
+    const int tiles_total = e.tiles_m * e.tiles_n * e.split;
 
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
     const uint32_t w_bytes = TC_BM * 128, x_bytes = (uint32_t)e.bn * 128;
     const uint32_t stage_bytes = w_bytes * (GATED ? 2 : 1) + 2 * x_bytes;
-    const uint32_t ncols_acc = (uint32_t)e.bn * (GATED ? 2 : 1);
+    // One accumulator = [W.x_hi | W.x_lo] per weight matrix (2 bn columns each); two of them.
+    const uint32_t acc_cols = (uint32_t)e.bn * (GATED ? 4 : 2);
     uint32_t ncols = 32;
-    while (ncols < ncols_acc) ncols <<= 1;
+    while (ncols < 2 * acc_cols) ncols <<= 1;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
-        mbar_init(&done_bar, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], TC_EPI_WARPS);
+        }
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -169,100 +280,104 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_holder;
+    volatile int* abort = &abort_flag;
 
-    if (warp == 0 && lane == 0) {
-        // TMA producer.
-        for (int kb = kb_begin, i = 0; kb < kb_end; kb++, i++) {
-            const int s = i % S;
-            if (!mbar_wait(&empty_bar[s], ((i / S) & 1) ^ 1, e.status, 1)) { abort_flag = 1; break; }
-            if (*(volatile int*)&abort_flag) break;
-            uint8_t* st = base + (size_t)s * stage_bytes;
-            mbar_expect_tx(&full_bar[s], stage_bytes);
-            const int kc = kb * TC_BK;
-            tma_load_2d(st, &tm_w, &full_bar[s], kc, n0);
-            if (GATED) tma_load_2d(st + w_bytes, &tm_w2, &full_bar[s], kc, n0);
-            uint8_t* xs = st + w_bytes * (GATED ? 2 : 1);
-            tma_load_2d(xs, &tm_xhi, &full_bar[s], kc, m0);
-            tma_load_2d(xs + x_bytes, &tm_xlo, &full_bar[s], kc, m0);
-        }
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer.
-        const uint32_t idesc = idesc_bf16(TC_BM, e.bn);
-        bool ok = true;
-        for (int kb = kb_begin, i = 0; kb < kb_end; kb++, i++) {
-            const int s = i % S;
-            if (!mbar_wait(&full_bar[s], (i / S) & 1, e.status, 2)) { ok = false; abort_flag = 1; break; }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            uint8_t* st = base + (size_t)s * stage_bytes;
-            const uint32_t wa = smem_u32(st);
-            const uint32_t w2a = wa + w_bytes;
-            const uint32_t xa = wa + w_bytes * (GATED ? 2 : 1);
-            const uint32_t xla = xa + x_bytes;
-#pragma unroll
-            for (int kk = 0; kk < TC_BK / 16; kk++) {
-                const uint32_t off = kk * 32;  // 16 bf16 along K inside the swizzle span
-                const uint64_t ad = sw128_desc(wa + off);
-                const uint64_t bh = sw128_desc(xa + off), bl = sw128_desc(xla + off);
-                const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                mma_bf16(tmem, ad, bh, idesc, acc);
-                mma_bf16(tmem, ad, bl, idesc, 1u);
-                if (GATED) {
-                    const uint64_t ad2 = sw128_desc(w2a + off);
-                    mma_bf16(tmem + e.bn, ad2, bh, idesc, acc);
-                    mma_bf16(tmem + e.bn, ad2, bl, idesc, 1u);
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer: one ring of stages across all of this CTA's tiles
+            int g = 0;
+            for (int t = blockIdx.x; t < tiles_total && !*abort; t += gridDim.x) {
+                const TileCoord tc = tile_coord(e, t);
+                for (int kb = tc.kb_begin; kb < tc.kb_end; kb++, g++) {
+                    const int s = g % S;
+                    if (!mbar_wait(&empty_bar[s], ((g / S) & 1) ^ 1, e.status, 1, abort)) break;
+                    uint8_t* st = base + (size_t)s * stage_bytes;
+                    mbar_expect_tx(&full_bar[s], stage_bytes);
+                    const int kc = kb * TC_BK;
+                    tma_load_2d(st, &tm_w, &full_bar[s], kc, tc.n0);
+                    if (GATED) tma_load_2d(st + w_bytes, &tm_w2, &full_bar[s], kc, tc.n0);
+                    uint8_t* xs = st + w_bytes * (GATED ? 2 : 1);
+                    tma_load_2d(xs, &tm_xhi, &full_bar[s], kc, tc.m0);
+                    tma_load_2d(xs + x_bytes, &tm_xlo, &full_bar[s], kc, tc.m0);
                 }
             }
-            mma_commit(&empty_bar[s]);
         }
-        if (ok) mma_commit(&done_bar);
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer: one MMA of N = 2 bn per 16-wide K step per weight matrix
+            const uint32_t idesc = idesc_bf16(TC_BM, 2 * e.bn);
+            int g = 0, tl = 0;
+            for (int t = blockIdx.x; t < tiles_total && !*abort; t += gridDim.x, tl++) {
+                const TileCoord tc = tile_coord(e, t);
+                const int b = tl & 1;
+                if (!mbar_wait(&acc_empty[b], ((tl >> 1) & 1) ^ 1, e.status, 2, abort)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t acc = tmem + b * acc_cols;
+                bool ok = true;
+                for (int kb = tc.kb_begin, i = 0; kb < tc.kb_end; kb++, i++, g++) {
+                    const int s = g % S;
+                    if (!mbar_wait(&full_bar[s], (g / S) & 1, e.status, 3, abort)) { ok = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t wa = smem_u32(base + (size_t)s * stage_bytes);
+                    const uint32_t xa = wa + w_bytes * (GATED ? 2 : 1);
+#pragma unroll
+                    for (int kk = 0; kk < TC_BK / 16; kk++) {
+                        const uint32_t off = kk * 32;  // 16 bf16 along K inside the swizzle span
+                        const uint64_t bx = sw128_desc(xa + off);
+                        const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
+                        mma_bf16(acc, sw128_desc(wa + off), bx, idesc, accum);
+                        if (GATED) mma_bf16(acc + 2 * e.bn, sw128_desc(wa + w_bytes + off), bx, idesc, accum);
+                    }
+                    mma_commit(&empty_bar[s]);
+                }
+                if (!ok) break;
+                mma_commit(&acc_full[b]);
+            }
+        }
+    } else {  // epilogue warps 2..9: quadrant = warp % 4, the two warps of a quadrant alternate chunks
+        const int quad = warp & 3, part = (warp - 2) >> 2;
+        int tl = 0;
+        for (int t = blockIdx.x; t < tiles_total; t += gridDim.x, tl++) {
+            const int b = tl & 1;
+            if (!mbar_wait(&acc_full[b], (tl >> 1) & 1, e.status, 4, abort)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const TileCoord tc = tile_coord(e, t);
+            epilogue_tile<GATED>(e, tc, tmem + b * acc_cols, quad, part, lane,
+                                 t < e.tiles_m * e.tiles_n);
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
     }
     __syncwarp();
-
-    // Epilogue: all four warps; warp w owns accumulator lanes (weight rows) 32w..32w+31.
-    const bool have = mbar_wait(&done_bar, 0, e.status, 3);
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (have) {
-        const int n = n0 + warp * 32 + lane;
-        const bool live_n = n < e.n;
-        const bool first_split = blockIdx.z == 0;
-        const float bval = ((e.flags & MT_LINEAR_BIAS) && live_n && first_split) ? bf16f(e.bias[n]) : 0.f;
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-        for (int c0 = 0; c0 < e.bn; c0 += 16) {
-            float v[16], v2[16];
-            tmem_ld16(lane_base + c0, v);
-            if (GATED) tmem_ld16(lane_base + e.bn + c0, v2);
-            if (!live_n) continue;
-#pragma unroll
-            for (int j = 0; j < 16; j++) {
-                const int m = m0 + c0 + j;
-                if (m >= e.m) break;
-                float val = v[j] + bval;
-                if (e.split > 1) {
-                    atomicAdd(e.y + (size_t)m * e.ldy + n, val);
-                    continue;
-                }
-                if (GATED) val = silu(val) * v2[j];
-                if (e.flags & MT_LINEAR_GELU) val = gelu_tanh(val);
-                if (e.flags & MT_LINEAR_SILU) val = silu(val);
-                if (e.y) {
-                    float* yp = e.y + (size_t)m * e.ldy + n;
-                    if (e.flags & MT_LINEAR_ACCUM) val += *yp;
-                    *yp = val;
-                }
-                if (e.y_hi) {
-                    uint16_t h, l;
-                    split_bf16(val, h, l);
-                    e.y_hi[(size_t)m * e.ld_ysplit + n] = h;
-                    e.y_lo[(size_t)m * e.ld_ysplit + n] = l;
-                }
-            }
-        }
-    }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 2) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+    }
+}
+
+// Finishes a split-K GEMM whose epilogue is nonlinear: y = epi(ws (+ bias)) from the fp32 sums.
+__global__ void split_epilogue_kernel(TcEpi e) {
+    const long long total = (long long)e.m * e.n;
+    const bool gated = (e.flags & MT_LINEAR_SILU_GATE) != 0;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int m = (int)(i / e.n), n = (int)(i % e.n);
+        float val = e.ws[(size_t)m * e.ldws + n];
+        if (e.flags & MT_LINEAR_BIAS) val += bf16f(e.bias[n]);
+        if (gated) val = silu(val) * e.ws[(size_t)m * e.ldws + e.n + n];
+        if (e.flags & MT_LINEAR_GELU) val = gelu_tanh(val);
+        if (e.flags & MT_LINEAR_SILU) val = silu(val);
+        if (e.y) {
+            float* yp = e.y + (size_t)m * e.ldy + n;
+            if (e.flags & MT_LINEAR_ACCUM) val += *yp;
+            *yp = val;
+        }
+        if (e.y_hi) {
+            uint16_t h, l;
+            split_bf16(val, h, l);
+            e.y_hi[(size_t)m * e.ld_ysplit + n] = h;
+            e.y_lo[(size_t)m * e.ld_ysplit + n] = l;
+        }
     }
 }
 
@@ -311,23 +426,42 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     TcEpi& e = plan->e;
     e = TcEpi{};
     e.m = a.m; e.n = a.n; e.k = a.k;
-    e.bn = a.bn_override > 0 ? a.bn_override : (a.m <= 256 ? round16(a.m) : 128);
+    const int sms = ctx->sm_count > 0 ? ctx->sm_count : 148;
+    const int tiles_n = (a.n + TC_BM - 1) / TC_BM;
+    if (a.bn_override > 0) e.bn = a.bn_override;
+    else if (a.m <= 64) e.bn = round16(a.m);                                     // one row tile (decode)
+    else if (a.m > 256 && tiles_n * ((a.m + 127) / 128) >= 2 * sms) e.bn = 128;  // large M: fewer W re-reads
+    else e.bn = 64;
     if (e.bn < 16) e.bn = 16;
-    MT_REQUIRE(ctx, e.bn % 16 == 0 && e.bn <= 256, MT_ERR_SHAPE, "gemm_tc: tile rows %d", e.bn);
+    if (gated && e.bn > 64 && a.bn_override <= 0) e.bn = 64;  // two gated accumulators x 2 buffers fit 512 columns
+    MT_REQUIRE(ctx, e.bn % 16 == 0 && e.bn <= (gated ? 64 : 128), MT_ERR_SHAPE, "gemm_tc: tile rows %d (16..%d)", e.bn,
+               gated ? 64 : 128);
     const uint32_t stage_bytes = TC_BM * 128 * (gated ? 2 : 1) + 2u * e.bn * 128;
-    const uint32_t budget = 200 * 1024;
-    e.stages = (int)(budget / stage_bytes);
+    const int tiles = tiles_n * ((a.m + e.bn - 1) / e.bn);
+    e.stages = (int)((200 * 1024) / stage_bytes);
     if (e.stages > 8) e.stages = 8;
-    MT_REQUIRE(ctx, e.stages >= 2, MT_ERR_SHAPE, "gemm_tc: tile too large");
+    if (e.stages < 2) e.stages = 2;
+    MT_REQUIRE(ctx, (size_t)e.stages * stage_bytes + 1024 <= 201 * 1024, MT_ERR_SHAPE, "gemm_tc: tile too large");
     const int kb_total = (a.k + TC_BK - 1) / TC_BK;
-    int split = a.split_k < 1 ? 1 : a.split_k;
+    const bool linear = !(a.flags & (MT_LINEAR_GELU | MT_LINEAR_SILU | MT_LINEAR_SILU_GATE)) && a.y && !a.y_hi;
+    int split = a.split_k;
+    if (split <= 0) {  // automatic: fill the SMs, at least two k blocks per split
+        split = (sms + tiles - 1) / tiles;
+        if (split > kb_total / 2) split = kb_total / 2;
+        if (!linear && !a.ws) split = 1;
+    }
+    if (split < 1) split = 1;
     if (split > kb_total) split = kb_total;
     e.kb_per_split = (kb_total + split - 1) / split;
     split = (kb_total + e.kb_per_split - 1) / e.kb_per_split;
-    MT_REQUIRE(ctx, split == 1 || (!gated && !(a.flags & (MT_LINEAR_GELU | MT_LINEAR_SILU)) && a.y && !a.y_hi),
-               MT_ERR_ARG, "gemm_tc: split-K needs a linear epilogue into fp32 y");
+    MT_REQUIRE(ctx, split == 1 || linear || a.ws, MT_ERR_ARG,
+               "gemm_tc: split-K with a nonlinear epilogue needs a workspace");
     e.split = split;
+    e.mode = split == 1 ? 0 : (linear ? 1 : 2);
+    e.tiles_n = tiles_n;
+    e.tiles_m = (a.m + e.bn - 1) / e.bn;
     e.bias = a.bias; e.y = a.y; e.ldy = a.ldy; e.y_hi = a.y_hi; e.y_lo = a.y_lo; e.ld_ysplit = a.ld_ysplit;
+    e.ws = a.ws; e.ldws = gated ? 2 * a.n : a.n;
     e.flags = a.flags; e.status = ctx->d_status;
 
     bool ok = make_map(&plan->tw, a.w, a.n, a.k, a.k, TC_BM);
@@ -337,7 +471,8 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     MT_REQUIRE(ctx, ok, MT_ERR_CUDA, "gemm_tc: cuTensorMapEncodeTiled failed (m %d n %d k %d)", a.m, a.n, a.k);
     plan->gated = gated;
     plan->smem = (size_t)e.stages * stage_bytes + 1024;
-    plan->grid = dim3((a.n + TC_BM - 1) / TC_BM, (a.m + e.bn - 1) / e.bn, split);
+    const int work = e.tiles_n * e.tiles_m * split;
+    plan->grid = dim3(work < sms ? work : sms, 1, 1);
     static bool attr_set = false;
     if (!attr_set) {
         cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
@@ -348,10 +483,20 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
 }
 
 void run_gemm_plan(const GemmPlan& p, cudaStream_t s) {
+    const TcEpi& e = p.e;
+    if (e.mode == 1 && !(e.flags & MT_LINEAR_ACCUM))
+        cudaMemset2DAsync(e.y, (size_t)e.ldy * sizeof(float), 0, (size_t)e.n * sizeof(float), e.m, s);
+    if (e.mode == 2) cudaMemsetAsync(e.ws, 0, (size_t)e.m * e.ldws * sizeof(float), s);
     if (p.gated)
         gemm_tc_kernel<true><<<p.grid, TC_THREADS, p.smem, s>>>(p.tw, p.tw2, p.th, p.tl, p.e);
     else
         gemm_tc_kernel<false><<<p.grid, TC_THREADS, p.smem, s>>>(p.tw, p.tw2, p.th, p.tl, p.e);
+    if (e.mode == 2) {
+        const long long total = (long long)e.m * e.n;
+        long long blocks = (total + 255) / 256;
+        if (blocks > 148 * 8) blocks = 148 * 8;
+        split_epilogue_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
+    }
 }
 
 mt_status launch_gemm_tc(mt_ctx* ctx, const LinearArgs& a, cudaStream_t s) {

@@ -80,8 +80,10 @@ struct LinearArgs {
     float* y; int ldy;                         // fp32 output (optional on the tensor-core route)
     uint16_t* y_hi; uint16_t* y_lo; int ld_ysplit;  // bf16 hi/lo output planes (optional)
     uint32_t flags;
-    int split_k;                               // tensor-core route: >1 = atomically reduced K splits
+    int split_k;                               // tensor-core route: K splits (1 = none, 0 = automatic)
     int bn_override;                           // tensor-core route: activation rows per tile (0 = auto)
+    float* ws;                                 // tensor-core route: fp32 [m, 2n] workspace for split-K
+                                               //   with a nonlinear epilogue (optional)
 };
 void launch_gemv(const LinearArgs& a, cudaStream_t s);
 mt_status launch_gemm_tc(mt_ctx* ctx, const LinearArgs& a, cudaStream_t s);
@@ -96,7 +98,10 @@ struct TcEpi {
     float* y; int ldy;
     uint16_t* y_hi; uint16_t* y_lo; int ld_ysplit;
     uint32_t flags;
-    int split;         // > 1: red.add fp32 partials into y (no activation allowed)
+    int split;         // K splits
+    int tiles_m, tiles_n;  // activation-row tiles (bn rows) and weight-row tiles (128 rows)
+    int mode;          // 0: epilogue in the kernel; 1: split-K reduced into y; 2: split-K sums into ws
+    float* ws; int ldws;
     unsigned int* status;
 };
 

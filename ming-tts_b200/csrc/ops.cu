@@ -10,49 +10,59 @@
 namespace mt {
 
 // ------------------------------------------------------------------------------------------------
-// RMSNorm: one warp per row, fp32 sum of squares, optional fp32 and/or bf16 hi/lo outputs.
+// RMSNorm: one block per row; each thread keeps its float4s of the row in registers, so the row
+// is read once; optional fp32 and/or bf16 hi/lo outputs.
 // ------------------------------------------------------------------------------------------------
-__global__ void rmsnorm_kernel(RmsArgs a) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * (blockDim.x >> 5) + warp;
-    if (row >= a.rows) return;
-    const float4* x = reinterpret_cast<const float4*>(a.x + (size_t)row * a.ldx);
+constexpr int RMS_THREADS = 128;
+constexpr int RMS_MAXV = 8;  // float4 per thread: width <= 4096
+
+__global__ void __launch_bounds__(RMS_THREADS) rmsnorm_kernel(RmsArgs a) {
+    __shared__ float part[RMS_THREADS / 32];
+    const int row = blockIdx.x;
     const int n4 = a.width >> 2;
+    const float4* x = reinterpret_cast<const float4*>(a.x + (size_t)row * a.ldx);
+    float4 v[RMS_MAXV];
     float ss = 0.f;
-    for (int i = lane; i < n4; i += 32) {
-        const float4 v = x[i];
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+#pragma unroll
+    for (int i = 0; i < RMS_MAXV; i++) {
+        const int c = threadIdx.x + i * RMS_THREADS;
+        v[i] = c < n4 ? x[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
     }
     ss = warp_sum(ss);
-    const float scale = rsqrtf(ss / (float)a.width + a.eps);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < RMS_THREADS / 32; w++) tot += part[w];
+    const float scale = rsqrtf(tot / (float)a.width + a.eps);
     const uint2* w = reinterpret_cast<const uint2*>(a.w);
-    for (int i = lane; i < n4; i += 32) {
-        const float4 v = x[i];
-        const uint2 wv = w[i];
+#pragma unroll
+    for (int i = 0; i < RMS_MAXV; i++) {
+        const int c = threadIdx.x + i * RMS_THREADS;
+        if (c >= n4) break;
+        const uint2 wv = w[c];
         float4 o;
-        o.x = v.x * scale * bf16_lo(wv.x);
-        o.y = v.y * scale * bf16_hi(wv.x);
-        o.z = v.z * scale * bf16_lo(wv.y);
-        o.w = v.w * scale * bf16_hi(wv.y);
-        if (a.y) reinterpret_cast<float4*>(a.y + (size_t)row * a.ldy)[i] = o;
+        o.x = v[i].x * scale * bf16_lo(wv.x);
+        o.y = v[i].y * scale * bf16_hi(wv.x);
+        o.z = v[i].z * scale * bf16_lo(wv.y);
+        o.w = v[i].w * scale * bf16_hi(wv.y);
+        if (a.y) reinterpret_cast<float4*>(a.y + (size_t)row * a.ldy)[c] = o;
         if (a.y_hi) {
             uint16_t h[4], l[4];
             split_bf16(o.x, h[0], l[0]);
             split_bf16(o.y, h[1], l[1]);
             split_bf16(o.z, h[2], l[2]);
             split_bf16(o.w, h[3], l[3]);
-            uint2 hv = make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
-            uint2 lv = make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
-            reinterpret_cast<uint2*>(a.y_hi + (size_t)row * a.ld_split)[i] = hv;
-            reinterpret_cast<uint2*>(a.y_lo + (size_t)row * a.ld_split)[i] = lv;
+            reinterpret_cast<uint2*>(a.y_hi + (size_t)row * a.ld_split)[c] =
+                make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
+            reinterpret_cast<uint2*>(a.y_lo + (size_t)row * a.ld_split)[c] =
+                make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
         }
     }
 }
 
-void launch_rmsnorm(const RmsArgs& a, cudaStream_t s) {
-    const int warps = 4;
-    rmsnorm_kernel<<<(a.rows + warps - 1) / warps, warps * 32, 0, s>>>(a);
-}
+void launch_rmsnorm(const RmsArgs& a, cudaStream_t s) { rmsnorm_kernel<<<a.rows, RMS_THREADS, 0, s>>>(a); }
 
 // fp32 [rows, cols] (row stride ldx) -> bf16 hi/lo planes [rows, cols] (row stride ld_split).
 __global__ void split_kernel(const float* __restrict__ x, int ldx, int rows, int cols,
@@ -150,14 +160,14 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(AttnArgs a) {
     const float* vc = a.vc + (size_t)req * a.req_stride + (size_t)kvh * a.cap * 64;
 
     float* qs = smem;                       // [G][64]
-    float* ks = qs + G * 64;                // [ATT_CHUNK][65]
-    float* sc = ks + ATT_CHUNK * 65;        // [G][nKeys]
-    float* red = sc + (size_t)G * a.max_keys;  // [G][2]
+    float* ks = qs + G * 64;                // [ATT_CHUNK][65]  K chunk, then V chunk [ATT_CHUNK][64]
+    float* sc = ks + ATT_CHUNK * 65;        // [G][max_keys]
+    float* red = sc + (size_t)G * a.max_keys;  // [G]
     const int tid = threadIdx.x;
     for (int i = tid; i < G * 64; i += ATT_THREADS)
         qs[i] = a.q[(size_t)m * a.ldq + (kvh * G + i / 64) * 64 + (i % 64)];
 
-    // Scores.
+    // Scores, 64 keys at a time: K rows staged coalesced, one (key, head) dot per thread.
     for (int c0 = 0; c0 < nKeys; c0 += ATT_CHUNK) {
         const int cn = min(ATT_CHUNK, nKeys - c0);
         __syncthreads();
@@ -180,7 +190,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(AttnArgs a) {
         }
     }
     __syncthreads();
-    // Softmax per head: warp g handles head g (G <= 8 warps).
+    // Softmax per head: warp g handles head g (G <= 8 warps); scores become unnormalised weights.
     const int warp = tid >> 5, lane = tid & 31;
     for (int g = warp; g < G; g += ATT_THREADS / 32) {
         float* sg = sc + (size_t)g * a.max_keys;
@@ -196,19 +206,41 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(AttnArgs a) {
         sum = warp_sum(sum);
         if (lane == 0) red[g] = 1.0f / sum;
     }
-    __syncthreads();
-    // P.V: thread (g, d); V rows read straight from the cache (coalesced over d).
-    for (int i = tid; i < G * 64; i += ATT_THREADS) {
-        const int g = i / 64, d = i % 64;
-        const float* sg = sc + (size_t)g * a.max_keys;
-        float acc = 0.f;
-        for (int j = 0; j < nKeys; j++) acc += sg[j] * vc[(size_t)((jStart + j) % a.cap) * 64 + d];
-        const float o = acc * red[g];
+    // P.V, 64 keys at a time: V rows staged coalesced in shared memory; thread (g, d) keeps its
+    // output(s) in registers across chunks.
+    const int outs = G * 64;
+    float acc0 = 0.f, acc1 = 0.f;
+    const int o0 = tid, o1 = tid + ATT_THREADS;
+    for (int c0 = 0; c0 < nKeys; c0 += ATT_CHUNK) {
+        const int cn = min(ATT_CHUNK, nKeys - c0);
+        __syncthreads();
+        for (int i = tid; i < cn * 16; i += ATT_THREADS) {
+            const int kk = i >> 4, d4 = i & 15;
+            const int slot = (jStart + c0 + kk) % a.cap;
+            reinterpret_cast<float4*>(ks + kk * 64)[d4] = reinterpret_cast<const float4*>(vc + (size_t)slot * 64)[d4];
+        }
+        __syncthreads();
+        if (o0 < outs) {
+            const float* sg = sc + (size_t)(o0 / 64) * a.max_keys + c0;
+            const int d = o0 % 64;
+            for (int kk = 0; kk < cn; kk++) acc0 += sg[kk] * ks[kk * 64 + d];
+        }
+        if (o1 < outs) {
+            const float* sg = sc + (size_t)(o1 / 64) * a.max_keys + c0;
+            const int d = o1 % 64;
+            for (int kk = 0; kk < cn; kk++) acc1 += sg[kk] * ks[kk * 64 + d];
+        }
+    }
+    for (int t = 0; t < 2; t++) {
+        const int o = t == 0 ? o0 : o1;
+        if (o >= outs) continue;
+        const int g = o / 64, d = o % 64;
+        const float val = (t == 0 ? acc0 : acc1) * red[g];
         const size_t off = (size_t)m * a.ldo + (kvh * G + g) * 64 + d;
-        if (a.out) a.out[off] = o;
+        if (a.out) a.out[off] = val;
         if (a.out_hi) {
             uint16_t h, l;
-            split_bf16(o, h, l);
+            split_bf16(val, h, l);
             const size_t so = (size_t)m * a.ld_split + (kvh * G + g) * 64 + d;
             a.out_hi[so] = h;
             a.out_lo[so] = l;
@@ -217,13 +249,13 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(AttnArgs a) {
 }
 
 size_t attention_smem(int G, int max_keys) {
-    return sizeof(float) * ((size_t)G * 64 + ATT_CHUNK * 65 + (size_t)G * max_keys + (size_t)G * 2);
+    return sizeof(float) * ((size_t)G * 64 + ATT_CHUNK * 65 + (size_t)G * max_keys + (size_t)G);
 }
 
 void launch_attention(const AttnArgs& a, cudaStream_t s) {
     const int G = a.hq / a.hkv;
     const size_t smem = attention_smem(G, a.max_keys);
-    static bool configured = false;
+    static bool configured = false;  // set once, before any graph capture (the first call is eager)
     if (!configured) {
         cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         configured = true;
@@ -354,9 +386,9 @@ extern "C" {
 mt_status mt_rmsnorm(mt_ctx* ctx, void* stream, const float* x, int ldx, int rows, int width,
                      const mt_bf16* w, float* y, int ldy, float eps) {
     MT_REQUIRE(ctx, ctx && x && w && y, MT_ERR_ARG, "mt_rmsnorm: null argument");
-    MT_REQUIRE(ctx, rows >= 0 && width > 0 && width % 4 == 0 && ldx % 4 == 0 && ldy % 4 == 0 &&
+    MT_REQUIRE(ctx, rows >= 0 && width > 0 && width % 4 == 0 && width <= 4096 && ldx % 4 == 0 && ldy % 4 == 0 &&
                         ldx >= width && ldy >= width,
-               MT_ERR_SHAPE, "mt_rmsnorm: width %d ldx %d ldy %d (need width %% 4 == 0, ld >= width, ld %% 4 == 0)",
+               MT_ERR_SHAPE, "mt_rmsnorm: width %d ldx %d ldy %d (need width %% 4 == 0, width <= 4096, ld >= width, ld %% 4 == 0)",
                width, ldx, ldy);
     MT_REQUIRE(ctx, aligned16(x) && aligned16(y) && ((uintptr_t)w & 7u) == 0, MT_ERR_ARG,
                "mt_rmsnorm: x/y need 16-byte, w 8-byte alignment");
