@@ -375,6 +375,19 @@ def main():
                               "kernels_per_step": kernels // max(args.steps, 1)}), flush=True)
         return
 
+    # ---- per-stage split of one eager step (reference StepRecorder semantics) ----
+    eng.stage_timing(True)
+    eng.begin(R, T, token_ids=ids_d, noise=noise_d, steps=min(total_steps, 8))
+    eng.prefill()
+    stage_samples = []
+    for n in range(min(total_steps, 8)):
+        eng.step()
+        if n >= 3:
+            torch.cuda.synchronize()
+            stage_samples.append(eng.stage_ms())
+    eng.stage_timing(False)
+    stage_ms = [round(statistics.median(x[i] for x in stage_samples), 3) for i in range(4)]
+
     # ---- end to end through the host API ----
     E = args.e2e_steps
     ids_h = torch.from_numpy(ids).pin_memory().numpy()
@@ -429,6 +442,8 @@ def main():
                          "down_proj_gbs": round(gv_down_bytes / t_gv_down / 1e9, 1),
                          "pool": f"{copies} distinct weight copies (>= 1 GiB), graph replay",
                          "peak_gbs": hbm_peak, "peak_kind": peak_kind},
+                "stages_ms": {"llm": stage_ms[0], "flow": stage_ms[1], "agg": stage_ms[2], "vae_concurrent": stage_ms[3],
+                              "note": "one eager step, events per stage; the VAE decode runs on a second stream"},
                 "gpu_launches": kernels, "clocks": clocks.summary()}
         if cpu:
             line["cpu_baseline"] = cpu

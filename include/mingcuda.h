@@ -331,6 +331,12 @@ mt_status mt_engine_buffer(const mt_engine* engine, int which, const float** ptr
 int mt_engine_steps_done(const mt_engine* engine);
 /* Kernels the last mt_engine_step enqueued (all streams). */
 int mt_engine_step_kernels(const mt_engine* engine);
+/* Per-stage GPU timing, as the reference's split StepRecorder (Engine.swift:31-86): when on, steps
+ * with both an LLM token and a VAE decode run eagerly (no graph replay) with events around each
+ * stage, and mt_engine_stage_ms returns [llm, flow, agg, vae] milliseconds of the last such step
+ * (the VAE decode runs concurrently on its own stream). */
+mt_status mt_engine_set_stage_timing(mt_engine* engine, int on);
+mt_status mt_engine_stage_ms(mt_engine* engine, float* ms4);
 /* End to end from host memory: copies embeds (or ids) and noise in, runs prefill, `steps` steps
  * and the flush, and copies every PCM chunk and stop probability out. pcm_host is [R, pcm_stride];
  * pcm_count receives the samples written per request (the same for all). The stop head is

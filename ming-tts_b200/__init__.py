@@ -138,6 +138,8 @@ PROTOTYPES = {
     "mt_engine_buffer": (c_int, [_P, c_int, POINTER(c_void_p), POINTER(ctypes.c_longlong)]),
     "mt_engine_steps_done": (c_int, [_P]),
     "mt_engine_step_kernels": (c_int, [_P]),
+    "mt_engine_set_stage_timing": (c_int, [_P, c_int]),
+    "mt_engine_stage_ms": (c_int, [_P, _P]),
     "mt_engine_generate": (c_int, [_P, _P, c_int, c_int, _P, _P, _P, c_int, c_float, _P, ctypes.c_longlong,
                                    POINTER(ctypes.c_longlong), _P]),
     "mt_gaussian_noise_host": (None, [_P, c_size_t, c_uint64]),
@@ -421,6 +423,15 @@ class Engine:
         self.ctx._check(lib().mt_engine_flush(self._e, stream if stream is not None else current_stream(),
                                               ctypes.byref(cnt)), "mt_engine_flush")
         return cnt.value
+
+    def stage_timing(self, on: bool = True):
+        self.ctx._check(lib().mt_engine_set_stage_timing(self._e, int(on)), "mt_engine_set_stage_timing")
+
+    def stage_ms(self):
+        """[llm, flow, agg, vae] GPU milliseconds of the last timed step."""
+        out = (c_float * 4)()
+        self.ctx._check(lib().mt_engine_stage_ms(self._e, out), "mt_engine_stage_ms")
+        return list(out)
 
     def buffer(self, which: int):
         p, stride = c_void_p(), ctypes.c_longlong()

@@ -99,6 +99,30 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
     return r;
 }
 
+// Programmatic dependent launch. Every kernel of the library calls pdl_wait() before it touches
+// global memory (it returns once the preceding kernel on the stream has completed and its writes
+// are visible; a no-op without the launch attribute) and pdl_launch() to let the next kernel's
+// CTAs be scheduled while this one drains.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launches `kernel` with the programmatic-stream-serialization attribute (see pdl_wait).
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Records a device-side failure in the context status word (first writer wins).
 __device__ __forceinline__ void report_status(unsigned int* status, unsigned int code,
                                               unsigned int site, unsigned int detail) {

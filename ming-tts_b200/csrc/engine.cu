@@ -109,6 +109,9 @@ struct mt_engine {
     cudaStream_t sb = nullptr;  // VAE stream
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_in = nullptr, ev_out = nullptr;
     int step_kernels = 0;       // kernels of the last step
+    bool time_stages = false;   // record per-stage events (eager steps only)
+    cudaEvent_t stage_ev[6] = {};  // A: start, after llm, after flow, after agg; B: decode start, end
+    bool stage_valid = false;
     int graph_kernels = 0;      // kernels in the captured step graph
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
@@ -393,7 +396,7 @@ void llm_token(mt_engine* e, cudaStream_t s) {
     norm(e->llm.x, c.hidden, R, c.hidden, e->w.llm.final_norm, c.eps, e->z, R, true, s);
 }
 
-void flow_agg_fc1(mt_engine* e, cudaStream_t s) {
+void flow_stage(mt_engine* e, cudaStream_t s) {
     const mt_model_config& c = e->cfg;
     const int R = e->R, L = c.latent_dim, Df = c.flow.hidden;
     run(e->stop_lin, s);
@@ -412,7 +415,12 @@ void flow_agg_fc1(mt_engine* e, cudaStream_t s) {
         fa.state = e->state_dev;
         launch_flow_final(fa, R, s); g_kernels++;
     }
-    // Aggregator (Engine.swift:406-410): [cls, x_emb(latent)] -> DiT -> final layer of row 0 -> LLM input.
+}
+
+// Aggregator (Engine.swift:406-410): [cls, x_emb(latent)] -> DiT -> final layer of row 0 -> LLM input.
+void agg_stage(mt_engine* e, cudaStream_t s) {
+    const mt_model_config& c = e->cfg;
+    const int R = e->R, L = c.latent_dim;
     const int Da = c.agg.hidden;
     launch_agg_assemble(e->y, e->w.agg_cls, e->w.agg_x_w, e->w.agg_x_b, Da, L, e->agg.x, R, s); g_kernels++;
     dit_blocks(e, e->w.agg, e->agg, e->agg_blocks, R, 2, s);
@@ -474,15 +482,23 @@ void upload_state(mt_engine* e, cudaStream_t s) {
 
 // Enqueues the device work of a step whose state is already uploaded. with_llm: n > 0;
 // with_decode: a VAE decode is due.
-void enqueue_step(mt_engine* e, cudaStream_t s, bool with_llm, bool with_decode) {
+void enqueue_step(mt_engine* e, cudaStream_t s, bool with_llm, bool with_decode, bool timed) {
+    cudaEvent_t* ev = e->stage_ev;
+    if (timed) cudaEventRecord(ev[0], s);
     if (with_decode) {
         cudaEventRecord(e->ev_fork, s);
         cudaStreamWaitEvent(e->sb, e->ev_fork, 0);
+        if (timed) cudaEventRecord(ev[4], e->sb);
         vae_decode(e, e->sb);
+        if (timed) cudaEventRecord(ev[5], e->sb);
         cudaEventRecord(e->ev_join, e->sb);
     }
     if (with_llm) llm_token(e, s);
-    flow_agg_fc1(e, s);
+    if (timed) cudaEventRecord(ev[1], s);
+    flow_stage(e, s);
+    if (timed) cudaEventRecord(ev[2], s);
+    agg_stage(e, s);
+    if (timed) cudaEventRecord(ev[3], s);
     if (with_decode) cudaStreamWaitEvent(s, e->ev_join, 0);
     vae_fc1(e, s);
 }
@@ -549,6 +565,8 @@ mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_o
     if (cudaMallocHost(&e->state_host, st_size(R) * sizeof(int)) != cudaSuccess)
         return cleanup(fail(ctx, MT_ERR_NOMEM, "engine: pinned step state"));
     memset(e->state_host, 0, st_size(R) * sizeof(int));
+    for (int i = 0; i < 6; i++)
+        if (cudaEventCreate(&e->stage_ev[i]) != cudaSuccess) return cleanup(fail(ctx, MT_ERR_CUDA, "engine: events"));
     if (cudaStreamCreateWithFlags(&e->sa, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&e->sb, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
@@ -571,6 +589,8 @@ void mt_engine_destroy(mt_engine* e) {
     if (e->ev_fork) cudaEventDestroy(e->ev_fork);
     if (e->ev_join) cudaEventDestroy(e->ev_join);
     if (e->ev_in) cudaEventDestroy(e->ev_in);
+    for (int i = 0; i < 6; i++)
+        if (e->stage_ev[i]) cudaEventDestroy(e->stage_ev[i]);
     if (e->ev_out) cudaEventDestroy(e->ev_out);
     if (e->state_host) cudaFreeHost(e->state_host);
     for (void* p : e->allocs) cudaFree(p);
@@ -659,13 +679,14 @@ mt_status mt_engine_step(mt_engine* e, void* stream, int* pcm_count) {
     // The step runs on the engine's own stream, ordered after the caller's work and joined back.
     cudaEventRecord(e->ev_in, caller);
     cudaStreamWaitEvent(s, e->ev_in, 0);
-    if (steady && e->opt.use_graphs) {
+    e->stage_valid = false;
+    if (steady && e->opt.use_graphs && !e->time_stages) {
         if (!e->graph_exec) {
             cudaError_t err = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
             if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph capture: %s", cudaGetErrorString(err));
             upload_state(e, s);
             g_kernels = 0;
-            enqueue_step(e, s, true, true);
+            enqueue_step(e, s, true, true, false);
             e->graph_kernels = g_kernels;
             err = cudaStreamEndCapture(s, &e->graph);
             if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph capture: %s", cudaGetErrorString(err));
@@ -677,7 +698,9 @@ mt_status mt_engine_step(mt_engine* e, void* stream, int* pcm_count) {
     } else {
         upload_state(e, s);
         g_kernels = 0;
-        enqueue_step(e, s, with_llm, with_decode);
+        const bool timed = e->time_stages && with_llm && with_decode;
+        enqueue_step(e, s, with_llm, with_decode, timed);
+        e->stage_valid = timed;
         e->step_kernels = g_kernels;
     }
     cudaEventRecord(e->ev_out, s);
@@ -722,6 +745,25 @@ mt_status mt_engine_buffer(const mt_engine* e, int which, const float** ptr, lon
 int mt_engine_steps_done(const mt_engine* e) { return e ? e->n : -1; }
 
 int mt_engine_step_kernels(const mt_engine* e) { return e ? e->step_kernels : -1; }
+
+mt_status mt_engine_set_stage_timing(mt_engine* e, int on) {
+    if (!e) return MT_ERR_ARG;
+    e->time_stages = on != 0;
+    return MT_OK;
+}
+
+mt_status mt_engine_stage_ms(mt_engine* e, float* ms4) {
+    if (!e || !ms4) return MT_ERR_ARG;
+    MT_REQUIRE(e->ctx, e->stage_valid, MT_ERR_STATE, "mt_engine_stage_ms: last step was not timed");
+    cudaEvent_t* ev = e->stage_ev;
+    cudaEventSynchronize(ev[3]);
+    cudaEventSynchronize(ev[5]);
+    cudaEventElapsedTime(&ms4[0], ev[0], ev[1]);
+    cudaEventElapsedTime(&ms4[1], ev[1], ev[2]);
+    cudaEventElapsedTime(&ms4[2], ev[2], ev[3]);
+    cudaEventElapsedTime(&ms4[3], ev[4], ev[5]);
+    return MT_OK;
+}
 
 mt_status mt_engine_generate(mt_engine* e, void* stream, int requests, int prompt_rows, const float* embeds_host,
                              const int32_t* ids_host, const float* noise_host, int steps, float cfg, float* pcm_host,

@@ -12,6 +12,8 @@ namespace mt {
 // batch is table[ids[i]] widened to fp32.
 __global__ void embed_gather_kernel(const int32_t* __restrict__ ids, int rows, const uint16_t* __restrict__ table,
                                     int hidden, int vocab, float* __restrict__ x, unsigned int* status) {
+    pdl_wait();
+    pdl_launch();
     const int row = blockIdx.x;
     if (row >= rows) return;
     int id = ids[row];
@@ -25,12 +27,14 @@ __global__ void embed_gather_kernel(const int32_t* __restrict__ ids, int rows, c
 
 void launch_embed_gather(const int32_t* ids, int rows, const uint16_t* table, int hidden, int vocab, float* x,
                          unsigned int* status, cudaStream_t s) {
-    embed_gather_kernel<<<rows, 256, 0, s>>>(ids, rows, table, hidden, vocab, x, status);
+    launch_k(embed_gather_kernel, rows, 256, 0, s, ids, rows, table, hidden, vocab, x, status);
 }
 
 // history <- y (n > 0), y <- noise[n] (Engine.swift:389-393).
 __global__ void flow_begin_kernel(float* __restrict__ y, float* __restrict__ hist, const float* __restrict__ noise,
                                   int latent, int steps_cap, const int* __restrict__ state) {
+    pdl_wait();
+    pdl_launch();
     const int r = blockIdx.x, d = threadIdx.x;
     if (d >= latent) return;
     const int n = state[ST_N];
@@ -40,7 +44,7 @@ __global__ void flow_begin_kernel(float* __restrict__ y, float* __restrict__ his
 
 void launch_flow_begin(float* y, float* hist, const float* noise, int latent, int steps_cap, const int* state,
                        int requests, cudaStream_t s) {
-    flow_begin_kernel<<<requests, latent, 0, s>>>(y, hist, noise, latent, steps_cap, state);
+    launch_k(flow_begin_kernel, requests, latent, 0, s, y, hist, noise, latent, steps_cap, state);
 }
 
 // The six DiT input rows of every request (flow_assemble, Shaders.swift:654-677): thread c computes
@@ -50,6 +54,8 @@ __global__ void flow_assemble_batched_kernel(const float* __restrict__ y, const 
                                              const float* __restrict__ temb, const uint16_t* __restrict__ xw,
                                              const uint16_t* __restrict__ xb, int hidden, int latent,
                                              float* __restrict__ X) {
+    pdl_wait();
+    pdl_launch();
     extern __shared__ float sv[];  // [2][latent]
     const int r = blockIdx.y;
     for (int d = threadIdx.x; d < latent; d += blockDim.x) {
@@ -81,7 +87,7 @@ __global__ void flow_assemble_batched_kernel(const float* __restrict__ y, const 
 void launch_flow_assemble_batched(const float* y, const float* hist, const float* cemb, const uint16_t* cbias,
                                   const float* temb, const uint16_t* xw, const uint16_t* xb, int hidden, int latent,
                                   float* X, int requests, cudaStream_t s) {
-    flow_assemble_batched_kernel<<<dim3((hidden + 127) / 128, requests), 128, 2 * latent * sizeof(float), s>>>(
+    launch_k(flow_assemble_batched_kernel, dim3((hidden + 127) / 128, requests), 128, 2 * latent * sizeof(float), s, 
         y, hist, cemb, cbias, temb, xw, xb, hidden, latent, X);
 }
 
@@ -92,6 +98,8 @@ void launch_flow_assemble_batched(const float* y, const float* hist, const float
 // rows 2 and 5; the other four never reach an output. Optional captures: the step-0 predictions
 // and, after the last Euler step, the latent.
 __global__ void __launch_bounds__(256) flow_final_kernel(FlowFinalArgs a) {
+    pdl_wait();
+    pdl_launch();
     extern __shared__ float sm[];
     float* xc = sm;                 // [hidden]
     float* xu = sm + a.hidden;      // [hidden]
@@ -160,13 +168,15 @@ __global__ void __launch_bounds__(256) flow_final_kernel(FlowFinalArgs a) {
 }
 
 void launch_flow_final(const FlowFinalArgs& a, int requests, cudaStream_t s) {
-    flow_final_kernel<<<requests, 256, 2 * a.hidden * sizeof(float), s>>>(a);
+    launch_k(flow_final_kernel, requests, 256, 2 * a.hidden * sizeof(float), s, a);
 }
 
 // Aggregator input rows (Engine.swift:407-409): row 2r = cls, row 2r+1 = x_emb(latent of request r).
 __global__ void agg_assemble_kernel(const float* __restrict__ y, const float* __restrict__ cls,
                                     const uint16_t* __restrict__ xw, const uint16_t* __restrict__ xb, int hidden,
                                     int latent, float* __restrict__ X) {
+    pdl_wait();
+    pdl_launch();
     extern __shared__ float sv[];
     const int r = blockIdx.y;
     for (int d = threadIdx.x; d < latent; d += blockDim.x) sv[d] = y[r * latent + d];
@@ -185,7 +195,7 @@ __global__ void agg_assemble_kernel(const float* __restrict__ y, const float* __
 
 void launch_agg_assemble(const float* y, const float* cls, const uint16_t* xw, const uint16_t* xb, int hidden,
                          int latent, float* X, int requests, cudaStream_t s) {
-    agg_assemble_kernel<<<dim3((hidden + 127) / 128, requests), 128, latent * sizeof(float), s>>>(y, cls, xw, xb,
+    launch_k(agg_assemble_kernel, dim3((hidden + 127) / 128, requests), 128, latent * sizeof(float), s, y, cls, xw, xb,
                                                                                                 hidden, latent, X);
 }
 
@@ -194,6 +204,8 @@ void launch_agg_assemble(const float* y, const float* cls, const uint16_t* xw, c
 __global__ void vae_fc1_kernel(const float* __restrict__ y, const uint16_t* __restrict__ w,
                                const uint16_t* __restrict__ b, int hidden, int latent, float* __restrict__ h,
                                const int* __restrict__ state) {
+    pdl_wait();
+    pdl_launch();
     extern __shared__ float sv[];
     const int r = blockIdx.y;
     for (int d = threadIdx.x; d < latent; d += blockDim.x) sv[d] = y[r * latent + d];
@@ -212,7 +224,7 @@ __global__ void vae_fc1_kernel(const float* __restrict__ y, const uint16_t* __re
 
 void launch_vae_fc1(const float* y, const uint16_t* w, const uint16_t* b, int hidden, int latent, float* h,
                     const int* state, int requests, cudaStream_t s) {
-    vae_fc1_kernel<<<dim3((hidden + 127) / 128, requests), 128, latent * sizeof(float), s>>>(y, w, b, hidden, latent,
+    launch_k(vae_fc1_kernel, dim3((hidden + 127) / 128, requests), 128, latent * sizeof(float), s, y, w, b, hidden, latent,
                                                                                            h, state);
 }
 
@@ -220,6 +232,8 @@ void launch_vae_fc1(const float* y, const uint16_t* w, const uint16_t* b, int hi
 // (upsample4, Shaders.swift:704-719; neighbours clamp to h[d] when absent).
 __global__ void vae_upsample_kernel(const float* __restrict__ h, int hidden, const int* __restrict__ state,
                                     float* __restrict__ frames) {
+    pdl_wait();
+    pdl_launch();
     const int r = blockIdx.y;
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= hidden) return;
@@ -237,7 +251,7 @@ __global__ void vae_upsample_kernel(const float* __restrict__ h, int hidden, con
 }
 
 void launch_vae_upsample(const float* h, int hidden, const int* state, float* frames, int requests, cudaStream_t s) {
-    vae_upsample_kernel<<<dim3((hidden + 127) / 128, requests), 128, 0, s>>>(h, hidden, state, frames);
+    launch_k(vae_upsample_kernel, dim3((hidden + 127) / 128, requests), 128, 0, s, h, hidden, state, frames);
 }
 
 }  // namespace mt

@@ -281,6 +281,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_holder;
     volatile int* abort = &abort_flag;
+    // Barrier init and TMEM allocation above overlap the previous kernel's tail; global memory is
+    // touched only from here on.
+    pdl_wait();
+    pdl_launch();
 
     if (warp == 0) {
         if (lane == 0) {  // TMA producer: one ring of stages across all of this CTA's tiles
@@ -358,6 +362,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
 // Finishes a split-K GEMM whose epilogue is nonlinear: y = epi(ws (+ bias)) from the fp32 sums.
 __global__ void split_epilogue_kernel(TcEpi e) {
+    pdl_wait();
+    pdl_launch();
     const long long total = (long long)e.m * e.n;
     const bool gated = (e.flags & MT_LINEAR_SILU_GATE) != 0;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -428,10 +434,15 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     e.m = a.m; e.n = a.n; e.k = a.k;
     const int sms = ctx->sm_count > 0 ? ctx->sm_count : 148;
     const int tiles_n = (a.n + TC_BM - 1) / TC_BM;
+    const bool linear = !(a.flags & (MT_LINEAR_GELU | MT_LINEAR_SILU | MT_LINEAR_SILU_GATE)) && a.y && !a.y_hi;
+    // Split-K by default only where partial sums can be reduced into y without zeroing it first
+    // (ACCUM: y holds the residual). Tile rows measured on the engine's shapes: narrow tiles for few
+    // rows (more CTAs), 128 rows once M is large (fewer weight re-reads through L2).
+    const bool splittable = linear && (a.flags & MT_LINEAR_ACCUM);
     if (a.bn_override > 0) e.bn = a.bn_override;
-    else if (a.m <= 64) e.bn = round16(a.m);                                     // one row tile (decode)
-    else if (a.m > 256 && tiles_n * ((a.m + 127) / 128) >= 2 * sms) e.bn = 128;  // large M: fewer W re-reads
-    else e.bn = 64;
+    else if (a.m <= 32) e.bn = round16(a.m);
+    else if (splittable) e.bn = a.m <= 64 ? 32 : a.m <= 128 ? 64 : 128;
+    else e.bn = a.m <= 128 ? 32 : a.m <= 256 ? 64 : 128;
     if (e.bn < 16) e.bn = 16;
     if (gated && e.bn > 64 && a.bn_override <= 0) e.bn = 64;  // two gated accumulators x 2 buffers fit 512 columns
     MT_REQUIRE(ctx, e.bn % 16 == 0 && e.bn <= (gated ? 64 : 128), MT_ERR_SHAPE, "gemm_tc: tile rows %d (16..%d)", e.bn,
@@ -443,12 +454,11 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     if (e.stages < 2) e.stages = 2;
     MT_REQUIRE(ctx, (size_t)e.stages * stage_bytes + 1024 <= 201 * 1024, MT_ERR_SHAPE, "gemm_tc: tile too large");
     const int kb_total = (a.k + TC_BK - 1) / TC_BK;
-    const bool linear = !(a.flags & (MT_LINEAR_GELU | MT_LINEAR_SILU | MT_LINEAR_SILU_GATE)) && a.y && !a.y_hi;
     int split = a.split_k;
-    if (split <= 0) {  // automatic: fill the SMs, at least two k blocks per split
-        split = (sms + tiles - 1) / tiles;
+    if (split <= 0) {  // automatic: about 160 work units, at least two k blocks each, at most 8 splits
+        split = splittable ? (160 + tiles - 1) / tiles : 1;
+        if (split > 8) split = 8;
         if (split > kb_total / 2) split = kb_total / 2;
-        if (!linear && !a.ws) split = 1;
     }
     if (split < 1) split = 1;
     if (split > kb_total) split = kb_total;
@@ -488,14 +498,14 @@ void run_gemm_plan(const GemmPlan& p, cudaStream_t s) {
         cudaMemset2DAsync(e.y, (size_t)e.ldy * sizeof(float), 0, (size_t)e.n * sizeof(float), e.m, s);
     if (e.mode == 2) cudaMemsetAsync(e.ws, 0, (size_t)e.m * e.ldws * sizeof(float), s);
     if (p.gated)
-        gemm_tc_kernel<true><<<p.grid, TC_THREADS, p.smem, s>>>(p.tw, p.tw2, p.th, p.tl, p.e);
+        launch_k(gemm_tc_kernel<true>, p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
     else
-        gemm_tc_kernel<false><<<p.grid, TC_THREADS, p.smem, s>>>(p.tw, p.tw2, p.th, p.tl, p.e);
+        launch_k(gemm_tc_kernel<false>, p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
     if (e.mode == 2) {
         const long long total = (long long)e.m * e.n;
         long long blocks = (total + 255) / 256;
         if (blocks > 148 * 8) blocks = 148 * 8;
-        split_epilogue_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
+        launch_k(split_epilogue_kernel, (unsigned)blocks, 256, 0, s, e);
     }
 }
 

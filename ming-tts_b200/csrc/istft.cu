@@ -17,6 +17,8 @@ constexpr int ISTFT_THREADS = 256;
 // computed with cospif) sit in shared memory; each thread evaluates one output sample as the
 // direct real inverse DFT, walking the table with index k*t mod N.
 __global__ void __launch_bounds__(ISTFT_THREADS) istft_frames_kernel(IstftArgs a) {
+    pdl_wait();
+    pdl_launch();
     extern __shared__ float sm[];
     const int N = a.nfft, bins = N / 2 + 1;
     float* re = sm;
@@ -119,6 +121,8 @@ __device__ __forceinline__ void fft_stage(const float2* __restrict__ src, float2
 }
 
 __global__ void __launch_bounds__(ISTFT_THREADS) istft_fft_kernel(IstftArgs a, FftPlan p) {
+    pdl_wait();
+    pdl_launch();
     extern __shared__ float2 sm2[];
     const int M = p.M, N = 2 * M;
     float2* xs = sm2;            // X[0..M]
@@ -197,17 +201,19 @@ void launch_istft_frames(const IstftArgs& a, cudaStream_t s) {
     if (fft_plan(M, &p) && fsmem <= 200 * 1024) {
         if (fsmem > 48 * 1024)
             cudaFuncSetAttribute(istft_fft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);
-        istft_fft_kernel<<<a.count, ISTFT_THREADS, fsmem, s>>>(a, p);
+        launch_k(istft_fft_kernel, a.count, ISTFT_THREADS, fsmem, s, a, p);
         return;
     }
     const size_t smem = istft_frames_smem(a.nfft);
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(istft_frames_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    istft_frames_kernel<<<dim3((a.nfft + ISTFT_THREADS - 1) / ISTFT_THREADS, a.count), ISTFT_THREADS, smem, s>>>(a);
+    launch_k(istft_frames_kernel, dim3((a.nfft + ISTFT_THREADS - 1) / ISTFT_THREADS, a.count), ISTFT_THREADS, smem, s, a);
 }
 
 // One thread per output sample; request r = blockIdx.y emits count samples starting at its s0.
 __global__ void istft_emit_kernel(EmitArgs a) {
+    pdl_wait();
+    pdl_launch();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int req = blockIdx.y;
     const int count = a.count_dev ? a.count_dev[req] : a.count;
@@ -232,7 +238,7 @@ __global__ void istft_emit_kernel(EmitArgs a) {
 
 void launch_istft_emit(const EmitArgs& a, int max_count, int requests, cudaStream_t s) {
     if (max_count <= 0 || requests <= 0) return;
-    istft_emit_kernel<<<dim3((max_count + 255) / 256, requests), 256, 0, s>>>(a);
+    launch_k(istft_emit_kernel, dim3((max_count + 255) / 256, requests), 256, 0, s, a);
 }
 
 }  // namespace mt

@@ -18,6 +18,8 @@ constexpr int GEMV_THREADS = 256;
 
 template <int MR, int G, bool GATED>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(LinearArgs a) {
+    pdl_wait();
+    pdl_launch();
     constexpr int C = GEMV_THREADS / G;  // columns per block
     __shared__ float red[GATED ? 2 : 1][GEMV_THREADS / 32][MR];
     const int tid = threadIdx.x;
@@ -142,12 +144,12 @@ static void launch_gemv_g(const LinearArgs& a, int G, cudaStream_t s) {
     const int C = GEMV_THREADS / G;
     dim3 grid((a.n + C - 1) / C, (a.m + MR - 1) / MR);
     switch (G) {
-        case 8: gemv_kernel<MR, 8, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
-        case 16: gemv_kernel<MR, 16, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
-        case 32: gemv_kernel<MR, 32, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
-        case 64: gemv_kernel<MR, 64, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
-        case 128: gemv_kernel<MR, 128, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
-        default: gemv_kernel<MR, 256, GATED><<<grid, GEMV_THREADS, 0, s>>>(a); break;
+        case 8: launch_k(gemv_kernel<MR, 8, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        case 16: launch_k(gemv_kernel<MR, 16, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        case 32: launch_k(gemv_kernel<MR, 32, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        case 64: launch_k(gemv_kernel<MR, 64, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        case 128: launch_k(gemv_kernel<MR, 128, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        default: launch_k(gemv_kernel<MR, 256, GATED>, grid, GEMV_THREADS, 0, s, a); break;
     }
 }
 

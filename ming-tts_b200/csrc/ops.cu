@@ -17,6 +17,8 @@ constexpr int RMS_THREADS = 128;
 constexpr int RMS_MAXV = 8;  // float4 per thread: width <= 4096
 
 __global__ void __launch_bounds__(RMS_THREADS) rmsnorm_kernel(RmsArgs a) {
+    pdl_wait();
+    pdl_launch();
     __shared__ float part[RMS_THREADS / 32];
     const int row = blockIdx.x;
     const int n4 = a.width >> 2;
@@ -62,11 +64,13 @@ __global__ void __launch_bounds__(RMS_THREADS) rmsnorm_kernel(RmsArgs a) {
     }
 }
 
-void launch_rmsnorm(const RmsArgs& a, cudaStream_t s) { rmsnorm_kernel<<<a.rows, RMS_THREADS, 0, s>>>(a); }
+void launch_rmsnorm(const RmsArgs& a, cudaStream_t s) { launch_k(rmsnorm_kernel, a.rows, RMS_THREADS, 0, s, a); }
 
 // fp32 [rows, cols] (row stride ldx) -> bf16 hi/lo planes [rows, cols] (row stride ld_split).
 __global__ void split_kernel(const float* __restrict__ x, int ldx, int rows, int cols,
                              uint16_t* __restrict__ hi, uint16_t* __restrict__ lo, int ld_split) {
+    pdl_wait();
+    pdl_launch();
     const int c4 = cols >> 2;
     const long long total = (long long)rows * c4;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -91,10 +95,12 @@ void launch_split(const float* x, int ldx, int rows, int cols, uint16_t* hi, uin
     long long blocks = (total + 255) / 256;
     if (blocks > sm_count * 8LL) blocks = sm_count * 8LL;
     if (blocks < 1) blocks = 1;
-    split_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, ldx, rows, cols, hi, lo, ld_split);
+    launch_k(split_kernel, (unsigned)blocks, 256, 0, s, x, ldx, rows, cols, hi, lo, ld_split);
 }
 
 __global__ void copy_kernel(const float* __restrict__ x, int count, float* __restrict__ y) {
+    pdl_wait();
+    pdl_launch();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) y[i] = x[i];
 }
 
@@ -104,6 +110,8 @@ __global__ void copy_kernel(const float* __restrict__ x, int count, float* __res
 // start at kc/vc + request * req_stride and whose first position is pos0 (+ pos_dev[request]).
 // ------------------------------------------------------------------------------------------------
 __global__ void rope_cache_kernel(RopeArgs a) {
+    pdl_wait();
+    pdl_launch();
     const int m = blockIdx.x;
     const int slot = threadIdx.x >> 5, i = threadIdx.x & 31;
     if (slot >= a.hq + 2 * a.hkv) return;
@@ -136,7 +144,7 @@ __global__ void rope_cache_kernel(RopeArgs a) {
 }
 
 void launch_rope_cache(const RopeArgs& a, cudaStream_t s) {
-    rope_cache_kernel<<<a.rows, (a.hq + 2 * a.hkv) * 32, 0, s>>>(a);
+    launch_k(rope_cache_kernel, a.rows, (a.hq + 2 * a.hkv) * 32, 0, s, a);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -148,6 +156,8 @@ constexpr int ATT_THREADS = 256;
 constexpr int ATT_CHUNK = 64;
 
 __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(AttnArgs a) {
+    pdl_wait();
+    pdl_launch();
     extern __shared__ float smem[];
     const int m = blockIdx.x, kvh = blockIdx.y;
     const int G = a.hq / a.hkv;
@@ -260,7 +270,7 @@ void launch_attention(const AttnArgs& a, cudaStream_t s) {
         cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         configured = true;
     }
-    attention_kernel<<<dim3(a.rows, a.hkv), ATT_THREADS, smem, s>>>(a);
+    launch_k(attention_kernel, dim3(a.rows, a.hkv), ATT_THREADS, smem, s, a);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -268,6 +278,8 @@ void launch_attention(const AttnArgs& a, cudaStream_t s) {
 // RoPE pair, so q and k rotate with one sincos per position.
 // ------------------------------------------------------------------------------------------------
 __global__ void dit_attention_kernel(DitAttnArgs a) {
+    pdl_wait();
+    pdl_launch();
     const int work = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (work >= a.batch * a.seq * a.heads) return;
@@ -318,7 +330,7 @@ __global__ void dit_attention_kernel(DitAttnArgs a) {
 
 void launch_dit_attention(const DitAttnArgs& a, cudaStream_t s) {
     const int work = a.batch * a.seq * a.heads;
-    dit_attention_kernel<<<(work + 7) / 8, 256, 0, s>>>(a);
+    launch_k(dit_attention_kernel, (work + 7) / 8, 256, 0, s, a);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -329,6 +341,8 @@ __global__ void flow_assemble_kernel(const float* __restrict__ y, const float* _
                                      const float* __restrict__ temb, const uint16_t* __restrict__ xw,
                                      const uint16_t* __restrict__ xb, int hidden, int latent,
                                      float* __restrict__ x) {
+    pdl_wait();
+    pdl_launch();
     const int c = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
     if (c >= hidden) return;
     const int s = r % 3;
@@ -348,6 +362,8 @@ __global__ void flow_assemble_kernel(const float* __restrict__ y, const float* _
 __global__ void flow_euler_kernel(float* __restrict__ y, const float* __restrict__ pred, int ldp,
                                   int pred_row, int null_row, int latent, float cfg, float dt,
                                   float* __restrict__ capture) {
+    pdl_wait();
+    pdl_launch();
     const int d = blockIdx.x * blockDim.x + threadIdx.x;
     if (d >= latent) return;
     const float c = pred[(size_t)pred_row * ldp + d];
@@ -361,6 +377,8 @@ __global__ void flow_euler_kernel(float* __restrict__ y, const float* __restrict
 
 __global__ void upsample4_kernel(const float* __restrict__ prev, const float* __restrict__ cur,
                                  const float* __restrict__ next, int hidden, float* __restrict__ frames) {
+    pdl_wait();
+    pdl_launch();
     const int c = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
     if (c >= hidden) return;
     const float v0 = cur[c];
@@ -405,7 +423,7 @@ mt_status mt_copy(mt_ctx* ctx, void* stream, const float* x, int count, float* y
     if (count == 0) return MT_OK;
     int blocks = (count + 255) / 256;
     if (blocks > 1024) blocks = 1024;
-    copy_kernel<<<blocks, 256, 0, as_stream(stream)>>>(x, count, y);
+    launch_k(copy_kernel, blocks, 256, 0, as_stream(stream), x, count, y);
     return check_launch(ctx, "mt_copy");
 }
 
@@ -466,7 +484,7 @@ mt_status mt_flow_assemble(mt_ctx* ctx, void* stream, const float* y, const floa
     MT_REQUIRE(ctx, ctx && y && history && cemb && cond_bias && temb && x_w && x_b && x, MT_ERR_ARG,
                "mt_flow_assemble: null argument");
     MT_REQUIRE(ctx, hidden > 0 && latent_dim > 0, MT_ERR_SHAPE, "mt_flow_assemble: hidden %d latent %d", hidden, latent_dim);
-    flow_assemble_kernel<<<dim3((hidden + 255) / 256, 6), 256, 0, as_stream(stream)>>>(
+    launch_k(flow_assemble_kernel, dim3((hidden + 255) / 256, 6), 256, 0, as_stream(stream), 
         y, history, cemb, cond_bias, temb, x_w, x_b, hidden, latent_dim, x);
     return check_launch(ctx, "mt_flow_assemble");
 }
@@ -476,7 +494,7 @@ mt_status mt_flow_euler(mt_ctx* ctx, void* stream, float* y, const float* pred, 
     MT_REQUIRE(ctx, ctx && y && pred, MT_ERR_ARG, "mt_flow_euler: null argument");
     MT_REQUIRE(ctx, latent_dim > 0 && pred_row >= 0 && null_row >= 0 && ldp >= latent_dim, MT_ERR_SHAPE,
                "mt_flow_euler: latent %d ldp %d", latent_dim, ldp);
-    flow_euler_kernel<<<(latent_dim + 255) / 256, 256, 0, as_stream(stream)>>>(y, pred, ldp, pred_row, null_row,
+    launch_k(flow_euler_kernel, (latent_dim + 255) / 256, 256, 0, as_stream(stream), y, pred, ldp, pred_row, null_row,
                                                                            latent_dim, cfg, dt, capture);
     return check_launch(ctx, "mt_flow_euler");
 }
@@ -485,7 +503,7 @@ mt_status mt_upsample4(mt_ctx* ctx, void* stream, const float* prev, const float
                        int hidden, float* frames) {
     MT_REQUIRE(ctx, ctx && cur && frames, MT_ERR_ARG, "mt_upsample4: null argument");
     MT_REQUIRE(ctx, hidden > 0, MT_ERR_SHAPE, "mt_upsample4: hidden %d", hidden);
-    upsample4_kernel<<<dim3((hidden + 255) / 256, 4), 256, 0, as_stream(stream)>>>(prev, cur, next, hidden, frames);
+    launch_k(upsample4_kernel, dim3((hidden + 255) / 256, 4), 256, 0, as_stream(stream), prev, cur, next, hidden, frames);
     return check_launch(ctx, "mt_upsample4");
 }
 
