@@ -188,6 +188,20 @@ mt_status mt_linear_split(mt_ctx* ctx, void* stream, const mt_bf16* x_hi, const 
                           const mt_bf16* w, const mt_bf16* w2, const mt_bf16* bias, int n, int k, float* y, int ldy,
                           mt_bf16* y_hi, mt_bf16* y_lo, int ld_ysplit, uint32_t flags);
 
+/* mt_linear_static computes what mt_linear computes, always on the tensor-core route, for callers that
+ * cannot allocate device memory: a host framework that owns every device allocation through its own
+ * pool, or a real-time audio thread that must not block on an allocation. It takes no context and
+ * allocates nothing: the scratch for splitting x into bf16 hi/lo planes is a 4 MiB array compiled
+ * into the library, held on every GPU that loads the library until the process exits. Nothing in it
+ * needs to start at zero (each call writes the planes it then reads). Limit: m * k <= 1,048,576
+ * (larger calls return MT_ERR_CAPACITY). The first call on a device looks up the array's device
+ * address with that device current; make that first call before any stream capture. Every call on
+ * a device uses the same array, so calls that can overlap on the GPU (streams not ordered with each
+ * other) race and corrupt each other's results: order them. Errors are reported by the status only
+ * (there is no context for a message). Has no counterpart in the reference. */
+mt_status mt_linear_static(void* stream, const float* x, int ldx, int m, const mt_bf16* w, const mt_bf16* w2,
+                           const mt_bf16* bias, int n, int k, float* y, int ldy, uint32_t flags);
+
 /* y = x * rsqrt(mean(x^2) + eps) * w per row. Replaces Encoder.rmsnorm (Kernels.swift:163-171),
  * kernel rmsnorm (Shaders.swift:418-441). width % 4 == 0. */
 mt_status mt_rmsnorm(mt_ctx* ctx, void* stream, const float* x, int ldx, int rows, int width,

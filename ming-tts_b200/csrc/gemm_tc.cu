@@ -492,6 +492,48 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     return MT_OK;
 }
 
+// Plan for callers without a context (mt_linear_static): no split-K, no status word, no error
+// strings; returns MT_ERR_CUDA only if a tensor map cannot be encoded. Inputs are validated by
+// the caller.
+mt_status make_gemm_plan_bare(int sm_count, const LinearArgs& a, GemmPlan* plan) {
+    const bool gated = (a.flags & MT_LINEAR_SILU_GATE) != 0;
+    TcEpi& e = plan->e;
+    e = TcEpi{};
+    e.m = a.m; e.n = a.n; e.k = a.k;
+    const int sms = sm_count > 0 ? sm_count : 148;
+    e.tiles_n = (a.n + TC_BM - 1) / TC_BM;
+    e.bn = a.m <= 32 ? round16(a.m) : a.m <= 128 ? 32 : a.m <= 256 ? 64 : 128;
+    if (e.bn < 16) e.bn = 16;
+    if (gated && e.bn > 64) e.bn = 64;
+    e.tiles_m = (a.m + e.bn - 1) / e.bn;
+    const uint32_t stage_bytes = TC_BM * 128 * (gated ? 2 : 1) + 2u * e.bn * 128;
+    e.stages = (int)((200 * 1024) / stage_bytes);
+    if (e.stages > 8) e.stages = 8;
+    const int kb_total = (a.k + TC_BK - 1) / TC_BK;
+    e.kb_per_split = kb_total;
+    e.split = 1;
+    e.mode = 0;
+    e.bias = a.bias; e.y = a.y; e.ldy = a.ldy; e.y_hi = a.y_hi; e.y_lo = a.y_lo; e.ld_ysplit = a.ld_ysplit;
+    e.flags = a.flags;
+    e.status = nullptr;
+    bool ok = make_map(&plan->tw, a.w, a.n, a.k, a.k, TC_BM);
+    ok = ok && make_map(&plan->tw2, gated ? a.w2 : a.w, a.n, a.k, a.k, TC_BM);
+    ok = ok && make_map(&plan->th, a.x_hi, a.m, a.k, a.ld_split, e.bn);
+    ok = ok && make_map(&plan->tl, a.x_lo, a.m, a.k, a.ld_split, e.bn);
+    if (!ok) return MT_ERR_CUDA;
+    plan->gated = gated;
+    plan->smem = (size_t)e.stages * stage_bytes + 1024;
+    const int work = e.tiles_n * e.tiles_m;
+    plan->grid = dim3(work < sms ? work : sms, 1, 1);
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+        cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+        attr_set = true;
+    }
+    return MT_OK;
+}
+
 void run_gemm_plan(const GemmPlan& p, cudaStream_t s) {
     const TcEpi& e = p.e;
     if (e.mode == 1 && !(e.flags & MT_LINEAR_ACCUM))

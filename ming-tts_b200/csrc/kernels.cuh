@@ -114,6 +114,7 @@ struct GemmPlan {
     bool gated;
 };
 mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan);
+mt_status make_gemm_plan_bare(int sm_count, const LinearArgs& a, GemmPlan* plan);
 void run_gemm_plan(const GemmPlan& p, cudaStream_t s);
 
 }  // namespace mt
