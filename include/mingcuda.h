@@ -324,9 +324,11 @@ enum {
 
 mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_options* opt, mt_engine** out);
 void mt_engine_destroy(mt_engine* engine);
-/* Starts a generation of `requests` requests with `prompt_rows` prompt rows each. Inputs are device
- * pointers: embeds [R, T, llm.hidden] fp32, or token_ids [R, T] (int32, gathered from embed_tokens)
- * when embeds is NULL; noise [R, steps, latent]; initial_history [R, latent] or NULL (zeros).
+/* Starts a generation of `requests` requests with `prompt_rows` prompt rows each. Inputs: embeds
+ * [R, T, llm.hidden] fp32, or token_ids [R, T] (int32, gathered from embed_tokens) when embeds is
+ * NULL; noise [R, steps, latent]; initial_history [R, latent] or NULL (zeros). token_ids must be in
+ * device memory; embeds, noise and initial_history may be in host or device memory (copied on the
+ * stream; pageable host memory makes the copy synchronous).
  * Resets the KV caches and VAE counters (Engine.swift:312-317). */
 mt_status mt_engine_begin(mt_engine* engine, void* stream, int requests, int prompt_rows, const float* embeds,
                           const int32_t* token_ids, const float* noise, const float* initial_history, int steps,
@@ -354,7 +356,8 @@ mt_status mt_engine_stage_ms(mt_engine* engine, float* ms4);
 /* End to end from host memory: copies embeds (or ids) and noise in, runs prefill, `steps` steps
  * and the flush, and copies every PCM chunk and stop probability out. pcm_host is [R, pcm_stride];
  * pcm_count receives the samples written per request (the same for all). The stop head is
- * evaluated every step; generation runs all `steps` (stop not obeyed). */
+ * evaluated every step; generation runs all `steps` (stop not obeyed). Uses staging the engine
+ * allocated at creation (no allocation per call); returns when the last sample is in pcm_host. */
 mt_status mt_engine_generate(mt_engine* engine, void* stream, int requests, int prompt_rows, const float* embeds_host,
                              const int32_t* ids_host, const float* noise_host, int steps, float cfg, float* pcm_host,
                              long long pcm_stride, long long* pcm_count, float* stop_prob_host);

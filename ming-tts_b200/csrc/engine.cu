@@ -26,6 +26,7 @@ namespace mt {
 
 static const int kGemvMax = 8;  // rows at or below which linears use the CUDA-core GEMV
 static thread_local int g_kernels = 0;  // kernels enqueued by the current engine call
+static const int kPcmRing = 4;  // pinned PCM slots mt_engine_generate cycles through
 
 struct Act {  // activation matrix with fp32 and bf16 hi/lo representations
     float* f = nullptr;
@@ -115,6 +116,12 @@ struct mt_engine {
     int graph_kernels = 0;      // kernels in the captured step graph
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
+
+    // Host-API staging of mt_engine_generate, allocated once with the engine.
+    int32_t* ids_stage = nullptr;  // device copy of the prompt token ids
+    float* ring_host = nullptr;    // pinned [kPcmRing][R * max_chunk] PCM slots
+    float* stop_host = nullptr;    // pinned [max_steps][R][2] stop logits
+    cudaEvent_t ring_ev[kPcmRing] = {};
 };
 
 namespace {
@@ -562,8 +569,14 @@ mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_o
     e->ws_b_floats = (size_t)4 * R * 2 * c.vae.intermediate;
     ETRY(dalloc(e, &e->ws_a, e->ws_a_floats));
     ETRY(dalloc(e, &e->ws_b, e->ws_b_floats));
-    if (cudaMallocHost(&e->state_host, st_size(R) * sizeof(int)) != cudaSuccess)
-        return cleanup(fail(ctx, MT_ERR_NOMEM, "engine: pinned step state"));
+    ETRY(dalloc(e, &e->ids_stage, (size_t)R * T));
+    if (cudaMallocHost(&e->state_host, st_size(R) * sizeof(int)) != cudaSuccess ||
+        cudaMallocHost(&e->ring_host, (size_t)kPcmRing * R * e->max_chunk * sizeof(float)) != cudaSuccess ||
+        cudaMallocHost(&e->stop_host, (size_t)S * R * 2 * sizeof(float)) != cudaSuccess)
+        return cleanup(fail(ctx, MT_ERR_NOMEM, "engine: pinned host staging"));
+    for (int i = 0; i < kPcmRing; i++)
+        if (cudaEventCreateWithFlags(&e->ring_ev[i], cudaEventDisableTiming) != cudaSuccess)
+            return cleanup(fail(ctx, MT_ERR_CUDA, "engine: events"));
     memset(e->state_host, 0, st_size(R) * sizeof(int));
     for (int i = 0; i < 6; i++)
         if (cudaEventCreate(&e->stage_ev[i]) != cudaSuccess) return cleanup(fail(ctx, MT_ERR_CUDA, "engine: events"));
@@ -593,6 +606,10 @@ void mt_engine_destroy(mt_engine* e) {
         if (e->stage_ev[i]) cudaEventDestroy(e->stage_ev[i]);
     if (e->ev_out) cudaEventDestroy(e->ev_out);
     if (e->state_host) cudaFreeHost(e->state_host);
+    if (e->ring_host) cudaFreeHost(e->ring_host);
+    if (e->stop_host) cudaFreeHost(e->stop_host);
+    for (int i = 0; i < kPcmRing; i++)
+        if (e->ring_ev[i]) cudaEventDestroy(e->ring_ev[i]);
     for (void* p : e->allocs) cudaFree(p);
     delete e;
 }
@@ -627,14 +644,14 @@ mt_status mt_engine_begin(mt_engine* e, void* stream, int requests, int prompt_r
     TRY(build_plans(e));
     const int H = c.llm.hidden, L = c.latent_dim, S = e->opt.max_steps;
     if (embeds) {
-        cudaMemcpyAsync(e->llm.x, embeds, sizeof(float) * (size_t)requests * prompt_rows * H, cudaMemcpyDeviceToDevice, s);
+        cudaMemcpyAsync(e->llm.x, embeds, sizeof(float) * (size_t)requests * prompt_rows * H, cudaMemcpyDefault, s);
     } else {
         launch_embed_gather(token_ids, requests * prompt_rows, e->w.embed_tokens, H, c.vocab, e->llm.x, ctx->d_status, s);
     }
     cudaMemcpy2DAsync(e->noise, (size_t)S * L * sizeof(float), noise, (size_t)steps * L * sizeof(float),
-                      (size_t)steps * L * sizeof(float), requests, cudaMemcpyDeviceToDevice, s);
+                      (size_t)steps * L * sizeof(float), requests, cudaMemcpyDefault, s);
     if (initial_history)
-        cudaMemcpyAsync(e->hist, initial_history, sizeof(float) * (size_t)requests * L, cudaMemcpyDeviceToDevice, s);
+        cudaMemcpyAsync(e->hist, initial_history, sizeof(float) * (size_t)requests * L, cudaMemcpyDefault, s);
     else
         cudaMemsetAsync(e->hist, 0, sizeof(float) * (size_t)requests * L, s);
     cudaMemsetAsync(e->y, 0, sizeof(float) * (size_t)requests * L, s);
@@ -780,74 +797,76 @@ mt_status mt_engine_generate(mt_engine* e, void* stream, int requests, int promp
                MT_ERR_CAPACITY, "mt_engine_generate: requests %d prompt %d steps %d exceed the engine", requests,
                prompt_rows, steps);
     cudaStream_t s = as_stream(stream);
-    const size_t in_rows = (size_t)requests * prompt_rows;
-    const size_t emb_bytes = embeds_host ? in_rows * c.llm.hidden * sizeof(float) : in_rows * sizeof(int32_t);
-    const size_t noise_bytes = (size_t)requests * steps * c.latent_dim * sizeof(float);
-    // Staging: device copies of the inputs, pinned host buffers for every chunk and stop logit.
-    void* d_in = nullptr;
-    float* d_noise = nullptr;
-    float* h_pcm = nullptr;
-    float* h_stop = nullptr;
-    const size_t chunk_floats = (size_t)requests * e->max_chunk;
-    const int emissions = steps + 2;
-    bool ok = cudaMalloc(&d_in, emb_bytes) == cudaSuccess && cudaMalloc(&d_noise, noise_bytes) == cudaSuccess &&
-              cudaMallocHost(&h_pcm, chunk_floats * emissions * sizeof(float)) == cudaSuccess &&
-              cudaMallocHost(&h_stop, (size_t)steps * requests * 2 * sizeof(float)) == cudaSuccess;
-    std::vector<int> counts;
+    // Prompt and noise go straight from the caller's buffers into the engine (begin copies embeds and
+    // noise from host or device memory); token ids go through a device stage for the gather kernel.
     mt_status st = MT_OK;
-    if (!ok) st = fail(ctx, MT_ERR_NOMEM, "mt_engine_generate: staging buffers");
-    if (st == MT_OK) {
-        cudaMemcpyAsync(d_in, embeds_host ? (const void*)embeds_host : (const void*)ids_host, emb_bytes,
-                        cudaMemcpyHostToDevice, s);
-        cudaMemcpyAsync(d_noise, noise_host, noise_bytes, cudaMemcpyHostToDevice, s);
-        st = mt_engine_begin(e, stream, requests, prompt_rows, embeds_host ? (const float*)d_in : nullptr,
-                             embeds_host ? nullptr : (const int32_t*)d_in, d_noise, nullptr, steps, cfg);
+    const int32_t* ids_dev = nullptr;
+    if (!embeds_host) {
+        cudaError_t err = cudaMemcpyAsync(e->ids_stage, ids_host, (size_t)requests * prompt_rows * sizeof(int32_t),
+                                          cudaMemcpyHostToDevice, s);
+        if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "mt_engine_generate: %s", cudaGetErrorString(err));
+        ids_dev = e->ids_stage;
     }
+    st = mt_engine_begin(e, stream, requests, prompt_rows, embeds_host, ids_dev, noise_host, nullptr, steps, cfg);
     if (st == MT_OK) st = mt_engine_prefill(e, stream);
+
+    // Each emission is copied into the next pinned ring slot; the slot's previous emission is unpacked
+    // into pcm_host (after its event) before the copy is enqueued, so the host unpacks emission i - 4
+    // while the GPU runs the steps after it.
+    const size_t chunk_floats = (size_t)requests * e->max_chunk;
+    std::vector<int> counts;
+    std::vector<long long> offsets;
+    long long total = 0;
+    auto unpack = [&](size_t i) {
+        const float* src = e->ring_host + (i % kPcmRing) * chunk_floats;
+        for (int r = 0; r < requests; r++)
+            memcpy(pcm_host + r * pcm_stride + offsets[i], src + (size_t)r * e->max_chunk, counts[i] * sizeof(float));
+    };
+    auto emit = [&](int count) -> mt_status {
+        MT_REQUIRE(ctx, total + count <= pcm_stride, MT_ERR_CAPACITY,
+                   "mt_engine_generate: %lld samples exceed pcm_stride %lld", total + count, pcm_stride);
+        const size_t i = counts.size();
+        const int slot = (int)(i % kPcmRing);
+        if (i >= (size_t)kPcmRing) {
+            cudaError_t err = cudaEventSynchronize(e->ring_ev[slot]);
+            if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "mt_engine_generate: %s", cudaGetErrorString(err));
+            unpack(i - kPcmRing);
+        }
+        cudaMemcpyAsync(e->ring_host + slot * chunk_floats, e->pcm, chunk_floats * sizeof(float),
+                        cudaMemcpyDeviceToHost, s);
+        cudaEventRecord(e->ring_ev[slot], s);
+        offsets.push_back(total);
+        counts.push_back(count);
+        total += count;
+        return MT_OK;
+    };
     for (int n = 0; st == MT_OK && n < steps; n++) {
         int count = 0;
         st = mt_engine_step(e, stream, &count);
         if (st != MT_OK) break;
-        cudaMemcpyAsync(h_stop + (size_t)n * requests * 2, e->stop, (size_t)requests * 2 * sizeof(float),
+        cudaMemcpyAsync(e->stop_host + (size_t)n * requests * 2, e->stop, (size_t)requests * 2 * sizeof(float),
                         cudaMemcpyDeviceToHost, s);
-        if (count > 0) {
-            cudaMemcpyAsync(h_pcm + counts.size() * chunk_floats, e->pcm, chunk_floats * sizeof(float),
-                            cudaMemcpyDeviceToHost, s);
-            counts.push_back(count);
-        }
+        if (count > 0) st = emit(count);
     }
     while (st == MT_OK) {
         int count = 0;
         st = mt_engine_flush(e, stream, &count);
         if (st != MT_OK || count == 0) break;
-        cudaMemcpyAsync(h_pcm + counts.size() * chunk_floats, e->pcm, chunk_floats * sizeof(float),
-                        cudaMemcpyDeviceToHost, s);
-        counts.push_back(count);
+        st = emit(count);
     }
+    cudaError_t err = cudaStreamSynchronize(s);
+    if (st == MT_OK && err != cudaSuccess) st = fail(ctx, MT_ERR_CUDA, "mt_engine_generate: %s", cudaGetErrorString(err));
     if (st == MT_OK) {
-        cudaError_t err = cudaStreamSynchronize(s);
-        if (err != cudaSuccess) st = fail(ctx, MT_ERR_CUDA, "mt_engine_generate: %s", cudaGetErrorString(err));
-    }
-    if (st == MT_OK) {
-        long long total = 0;
-        for (size_t i = 0; i < counts.size(); i++) {
-            for (int r = 0; r < requests; r++)
-                memcpy(pcm_host + r * pcm_stride + total, h_pcm + i * chunk_floats + (size_t)r * e->max_chunk,
-                       counts[i] * sizeof(float));
-            total += counts[i];
-        }
+        for (size_t i = counts.size() > (size_t)kPcmRing ? counts.size() - kPcmRing : 0; i < counts.size(); i++)
+            unpack(i);
         *pcm_count = total;
         if (stop_prob_host)
             for (int n = 0; n < steps; n++)
                 for (int r = 0; r < requests; r++) {
-                    const float* l = h_stop + ((size_t)n * requests + r) * 2;
+                    const float* l = e->stop_host + ((size_t)n * requests + r) * 2;
                     stop_prob_host[(size_t)r * steps + n] = 1.0f / (1.0f + expf(l[0] - l[1]));  // Engine.swift:349
                 }
     }
-    if (d_in) cudaFree(d_in);
-    if (d_noise) cudaFree(d_noise);
-    if (h_pcm) cudaFreeHost(h_pcm);
-    if (h_stop) cudaFreeHost(h_stop);
     return st;
 }
 
