@@ -88,6 +88,19 @@ struct LinearArgs {
 void launch_gemv(const LinearArgs& a, cudaStream_t s);
 mt_status launch_gemm_tc(mt_ctx* ctx, const LinearArgs& a, cudaStream_t s);
 
+// Epilogue specialisations of the tensor-core GEMM: the flag combinations the engine runs are
+// compiled as straight-line code; any other combination takes the runtime-flag path.
+enum EpiKind : int {
+    EPI_GENERIC = 0,
+    EPI_F32 = 1,         // y = acc (+ bias)
+    EPI_F32_ACCUM = 2,   // y += acc (+ bias)
+    EPI_SPLIT = 3,       // hi/lo = split(acc (+ bias))
+    EPI_SPLIT_GELU = 4,  // hi/lo = split(gelu(acc (+ bias)))
+    EPI_SPLIT_GATE = 5,  // hi/lo = split(silu(acc1 (+ bias)) * acc2)
+    EPI_F32_SILU = 6,    // y = silu(acc (+ bias))
+    EPI_RED = 7,         // split-K partial: y += acc (+ bias on the first split), fp32 reductions
+};
+
 // Epilogue/launch parameters of the tensor-core GEMM (gemm_tc.cu).
 struct TcEpi {
     int m, n, k;
@@ -101,6 +114,7 @@ struct TcEpi {
     int split;         // K splits
     int tiles_m, tiles_n;  // activation-row tiles (bn rows) and weight-row tiles (128 rows)
     int mode;          // 0: epilogue in the kernel; 1: split-K reduced into y; 2: split-K sums into ws
+    int kind;          // EPI_* epilogue specialisation chosen by the planner (EPI_GENERIC: runtime flags)
     float* ws; int ldws;
     unsigned int* status;
 };

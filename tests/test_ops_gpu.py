@@ -88,6 +88,53 @@ def test_tensor_core_shapes(ctx, mt, oracle, m, n, k, flags, bias):
     gemv_case(ctx, mt, oracle, m, n, k, flags, bias)
 
 
+@pytest.mark.parametrize("m,n,k,flags,bias,outs", [
+    (384, 1024, 1024, 0, True, "split"),         # specialised: hi/lo out
+    (384, 4096, 1024, 4, True, "split"),         # specialised: GELU, hi/lo out (flow ff1)
+    (64, 9728, 896, 8, False, "split"),          # specialised: SILU gate, hi/lo out (LLM gate/up)
+    (250, 3072, 1024, 0, True, "f32"),           # specialised: fp32 out, ragged rows
+    (384, 1024, 4096, 2, True, "f32"),           # split-K reduction into the residual (flow ff2)
+    (40, 896, 896, 2, False, "f32"),             # residual add, narrow tile
+    (37, 200, 136, 16, True, "f32"),             # specialised: SiLU, ragged rows and columns
+    (37, 200, 136, 4, True, "both"),             # runtime-flag path: GELU, fp32 and hi/lo out
+    (70, 330, 256, 2, True, "both"),             # runtime-flag path: residual add with hi/lo out
+    (21, 300, 896, 8, True, "f32"),              # runtime-flag path: gate with fp32 out
+])
+def test_linear_split_epilogues(ctx, mt, oracle, m, n, k, flags, bias, outs):
+    """mt_linear_split (bf16 hi/lo activations in, fp32 and/or hi/lo out) against the oracle, one
+    case per compiled epilogue of the tensor-core GEMM plus the runtime-flag path."""
+    rng = LCG(oracle, m * 31 + n * 3 + k + flags)
+    x = rng.floats(m * k, 2.0)
+    xh = oracle.bf16_bits(x)
+    xl = oracle.bf16_bits(x - oracle.bf16_to_f32(xh))
+    x_eff = oracle.bf16_to_f32(xh) + oracle.bf16_to_f32(xl)  # exact in fp32
+    w = oracle.bf16_bits(rng.floats(n * k, 0.1))
+    w2 = oracle.bf16_bits(rng.floats(n * k, 0.1))
+    b = oracle.bf16_bits(rng.floats(n))
+    y0 = rng.floats(m * n)
+    f = flags | (mt.BIAS if bias else 0)
+    gated = bool(f & mt.SILU_GATE)
+    want = y0.copy()
+    oracle.linear(x_eff, k, m, w, w2 if gated else None, b, n, k, want, n, f)
+    import torch
+    yd = dev(y0) if outs in ("f32", "both") else None
+    yh = torch.zeros(m * n, dtype=torch.int16, device="cuda") if outs in ("split", "both") else None
+    yl = torch.zeros_like(yh) if yh is not None else None
+    ctx.call("linear_split", dev(xh.view(np.int16)), dev(xl.view(np.int16)), k, m, dev(w), dev(w2) if gated else None,
+             dev(b) if bias else None, n, k, yd, n if yd is not None else 0, yh, yl, n if yh is not None else 0, f)
+    ctx.check()
+    what = f"linear_split m{m} n{n} k{k} flags {f} out {outs}"
+    tol = dict(atol=2e-4 * np.sqrt(k) / 30, rtol=1e-4)
+    if yd is not None:
+        got = host(yd)
+        assert_close(got.reshape(m, n), want.reshape(m, n), what=what + " fp32", **tol)
+        assert rel_err(got, want) <= 1e-3, what
+    if yh is not None:
+        got = oracle.bf16_to_f32(host(yh).view(np.uint16)) + oracle.bf16_to_f32(host(yl).view(np.uint16))
+        assert_close(got.reshape(m, n), want.reshape(m, n), what=what + " hi+lo", atol=tol["atol"], rtol=2e-4)
+        assert rel_err(got, want) <= 1e-3, what
+
+
 def test_gelu_silu_large_inputs(ctx, mt, oracle):
     gemv_case(ctx, mt, oracle, 6, 256, 1024, mt.GELU, True, x_scale=8)
     gemv_case(ctx, mt, oracle, 1, 256, 896, mt.SILU, False, x_scale=8)
