@@ -169,6 +169,13 @@ int mt_linear_route(int m, int n, int k);
 
 /* ---------------------------------------------------------------------------------------------
  * Operators (one per Encoder method, Kernels.swift:89-283)
+ *
+ * Every kernel is launched with programmatic dependent launch: it may start while the previous
+ * kernel on the stream drains, and waits for that kernel before it reads activations or writes
+ * outputs. The tensor-core linear reads its weights (w, w2) before that wait, so the weights must
+ * not be written by the kernel directly before it on the same stream if that kernel triggers
+ * programmatic completion early (kernels of other libraries normally do not; model creation in
+ * this library synchronises).
  * ------------------------------------------------------------------------------------------- */
 
 /* y[m, n] = epi(x[m, :k] . w[n, :k]^T), x row stride ldx floats, y row stride ldy floats.

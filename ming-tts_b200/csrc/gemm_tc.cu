@@ -386,24 +386,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_holder;
     volatile int* abort = &abort_flag;
-    // Barrier init and TMEM allocation above overlap the previous kernel's tail; global memory is
-    // touched only from here on.
-    pdl_wait();
+    // Barrier init and TMEM allocation above overlap the previous kernel's tail. The previous kernel
+    // may still be writing this kernel's activations and outputs, so every access to those waits
+    // for it (pdl_wait); the weights are never written by a kernel and are fetched before the wait.
     pdl_launch();
 
     if (warp == 0) {
         if (lane == 0) {  // TMA producer: one ring of stages across all of this CTA's tiles
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+            if (GATED) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w2)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_xhi)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_xlo)) : "memory");
+            // Weight tiles of the first S stages (fresh stages: no empty-slot wait needed).
+            int pre = 0;
+            for (int t = blockIdx.x; t < tiles_total && pre < S; t += gridDim.x) {
+                const TileCoord tc = tile_coord(e, t);
+                for (int kb = tc.kb_begin; kb < tc.kb_end && pre < S; kb++, pre++) {
+                    uint8_t* st = base + (size_t)pre * stage_bytes;
+                    mbar_expect_tx(&full_bar[pre], stage_bytes);
+                    tma_load_2d(st, &tm_w, &full_bar[pre], kb * TC_BK, tc.n0);
+                    if (GATED) tma_load_2d(st + w_bytes, &tm_w2, &full_bar[pre], kb * TC_BK, tc.n0);
+                }
+            }
+            pdl_wait();
             int g = 0;
             for (int t = blockIdx.x; t < tiles_total && !*abort; t += gridDim.x) {
                 const TileCoord tc = tile_coord(e, t);
                 for (int kb = tc.kb_begin; kb < tc.kb_end; kb++, g++) {
                     const int s = g % S;
-                    if (!mbar_wait(&empty_bar[s], ((g / S) & 1) ^ 1, e.status, 1, abort)) break;
                     uint8_t* st = base + (size_t)s * stage_bytes;
-                    mbar_expect_tx(&full_bar[s], stage_bytes);
                     const int kc = kb * TC_BK;
-                    tma_load_2d(st, &tm_w, &full_bar[s], kc, tc.n0);
-                    if (GATED) tma_load_2d(st + w_bytes, &tm_w2, &full_bar[s], kc, tc.n0);
+                    if (g >= pre) {
+                        if (!mbar_wait(&empty_bar[s], ((g / S) & 1) ^ 1, e.status, 1, abort)) break;
+                        mbar_expect_tx(&full_bar[s], stage_bytes);
+                        tma_load_2d(st, &tm_w, &full_bar[s], kc, tc.n0);
+                        if (GATED) tma_load_2d(st + w_bytes, &tm_w2, &full_bar[s], kc, tc.n0);
+                    }
                     uint8_t* xs = st + w_bytes * (GATED ? 2 : 1);
                     tma_load_2d(xs, &tm_xhi, &full_bar[s], kc, tc.m0);
                     tma_load_2d(xs + x_bytes, &tm_xlo, &full_bar[s], kc, tc.m0);
@@ -443,6 +461,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     } else {  // epilogue warps 2..9: quadrant = warp % 4, the two warps of a quadrant alternate chunks
         const int quad = warp & 3, part = (warp - 2) >> 2;
+        // Pull the epilogue's parameters into registers while the previous kernel drains.
+        asm volatile("" ::"r"(e.kind), "r"(e.flags), "r"(e.m), "r"(e.n), "r"(e.bn), "l"(e.y), "l"(e.y_hi),
+                     "l"(e.bias));
+        pdl_wait();
         int tl = 0;
         for (int t = blockIdx.x; t < tiles_total; t += gridDim.x, tl++) {
             const int b = tl & 1;
