@@ -588,7 +588,7 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     if (a.bn_override > 0) e.bn = a.bn_override;
     else if (a.m <= 32) e.bn = round16(a.m);
     else if (splittable) e.bn = a.m <= 64 ? 32 : a.m <= 128 ? 64 : 128;
-    else e.bn = a.m <= 128 ? 32 : a.m <= 256 ? 64 : 128;
+    else e.bn = a.m <= 128 ? 32 : a.m <= 256 ? 64 : a.m <= 384 ? 96 : 128;
     if (e.bn < 16) e.bn = 16;
     if (gated && e.bn > 64 && a.bn_override <= 0) e.bn = 64;  // two gated accumulators x 2 buffers fit 512 columns
     MT_REQUIRE(ctx, e.bn % 16 == 0 && e.bn <= (gated ? 64 : 128), MT_ERR_SHAPE, "gemm_tc: tile rows %d (16..%d)", e.bn,
@@ -601,8 +601,8 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     MT_REQUIRE(ctx, (size_t)e.stages * stage_bytes + 1024 <= 201 * 1024, MT_ERR_SHAPE, "gemm_tc: tile too large");
     const int kb_total = (a.k + TC_BK - 1) / TC_BK;
     int split = a.split_k;
-    if (split <= 0) {  // automatic: about 160 work units, at least two k blocks each, at most 8 splits
-        split = splittable ? (160 + tiles - 1) / tiles : 1;
+    if (split <= 0) {  // automatic: one wave (work units <= SMs), at least two k blocks each, at most 8 splits
+        split = splittable ? sms / tiles : 1;
         if (split > 8) split = 8;
         if (split > kb_total / 2) split = kb_total / 2;
     }
