@@ -311,6 +311,8 @@ def main():
     ap.add_argument("--cpu-prompt", type=int, default=16)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--groups", type=int, default=0,
+                    help="request groups stepped concurrently (0 = the engine's automatic choice)")
     ap.add_argument("--gemm", type=str, default="",
                     help="M,N,K[,flags]: time one tensor-core GEMM shape alone and exit (for focused profiling)")
     ap.add_argument("--profile", action="store_true",
@@ -341,7 +343,8 @@ def main():
     R, T = args.requests, args.prompt
     total_steps = args.warmup + args.steps
     assert T + total_steps <= cfg.llm_capacity, f"prompt + steps must fit the {cfg.llm_capacity}-position cache"
-    eng = mt.Engine(ctx, model, R, T, max(total_steps, args.e2e_steps), use_graphs=not args.no_graphs)
+    eng = mt.Engine(ctx, model, R, T, max(total_steps, args.e2e_steps), use_graphs=not args.no_graphs,
+                    groups=args.groups)
     ids, noise = request_inputs(mt, cfg, R, T, total_steps, rank * R)
     ids_d, noise_d = torch.from_numpy(ids).cuda(), torch.from_numpy(noise).cuda()
     stream = torch.cuda.current_stream()

@@ -316,6 +316,8 @@ typedef struct {
     int max_steps;     /* generation steps; prompt + steps <= llm_capacity */
     int vae_ring;      /* VAE KV-cache ring positions (0 = 128); must be >= window + 3 */
     int use_graphs;    /* 1: replay steady-state steps from a captured CUDA graph */
+    int groups;        /* request groups stepped concurrently on their own streams (0 = 1; at most
+                          4 and at most the requests); one group measured fastest on B200 */
 } mt_engine_options;
 
 /* Buffers readable after a step (device pointers, request-major). */

@@ -88,7 +88,7 @@ class TensorInfo(ctypes.Structure):
 
 class EngineOptions(ctypes.Structure):
     _fields_ = [("max_requests", c_int), ("max_prompt", c_int), ("max_steps", c_int), ("vae_ring", c_int),
-                ("use_graphs", c_int)]
+                ("use_graphs", c_int), ("groups", c_int)]
 
 
 MT_DTYPE_BF16, MT_DTYPE_F32 = 0, 1
@@ -392,9 +392,9 @@ class Engine:
     """mt_engine: the generation loop for R concurrent requests."""
 
     def __init__(self, ctx: Context, model: Model, max_requests: int, max_prompt: int, max_steps: int,
-                 use_graphs: bool = True, vae_ring: int = 0):
+                 use_graphs: bool = True, vae_ring: int = 0, groups: int = 0):
         self.ctx, self.model = ctx, model
-        self.opt = EngineOptions(max_requests, max_prompt, max_steps, vae_ring, int(use_graphs))
+        self.opt = EngineOptions(max_requests, max_prompt, max_steps, vae_ring, int(use_graphs), groups)
         self._e = c_void_p()
         ctx._check(lib().mt_engine_create(ctx.handle, model.handle, ctypes.byref(self.opt), ctypes.byref(self._e)),
                    "mt_engine_create")

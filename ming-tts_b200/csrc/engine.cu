@@ -59,6 +59,27 @@ struct QwenBufs {
     float* inv_freq = nullptr;  // [32]
 };
 
+constexpr int kMaxGroups = 4;
+
+// A contiguous range of requests whose LLM token, flow head, aggregator and VAE fc1 run as one
+// chain on the group's own stream. Requests never interact, so the groups of a step are
+// independent chains the GPU may run concurrently. The buffers are views into the engine's
+// request-major buffers.
+struct Group {
+    int r0 = 0, R = 0;
+    cudaStream_t s = nullptr;     // group 0 runs on the engine's step stream
+    cudaEvent_t done = nullptr;
+    QwenBufs llm;
+    Act z, agg_norm;
+    float *stop = nullptr, *cemb = nullptr, *y = nullptr, *hist = nullptr, *noise = nullptr, *latents = nullptr,
+          *vel0 = nullptr, *vae_h = nullptr;
+    DitBufs flow, agg;
+    const int* llm_pos = nullptr;  // device: this group's per-request LLM positions
+    std::vector<QwenLayerPlans> llm_dec;
+    std::vector<DitBlockPlans> flow_blocks, agg_blocks;
+    Lin cond, agg_final, stop_lin;
+};
+
 }  // namespace mt
 
 using namespace mt;
@@ -102,9 +123,10 @@ struct mt_engine {
 
     // Plans for the current (R, T).
     int plan_R = -1, plan_T = -1;
-    std::vector<QwenLayerPlans> llm_dec, llm_pre, vae_layers;
-    std::vector<DitBlockPlans> flow_blocks, agg_blocks;
-    Lin cond, agg_final, vae_head, stop_lin;
+    std::vector<QwenLayerPlans> llm_pre, vae_layers;
+    Lin vae_head;
+    Group groups[kMaxGroups];
+    int G = 1;  // groups of the current generation
 
     cudaStream_t sa = nullptr;  // step stream (owned, capturable; joined to the caller's stream)
     cudaStream_t sb = nullptr;  // VAE stream
@@ -262,26 +284,93 @@ mt_status plan_dit(mt_engine* e, std::vector<DitBlockPlans>& plans, const mt_dit
     return MT_OK;
 }
 
+Act act_rows(const Act& a, size_t row) {
+    Act v = a;
+    const size_t off = row * (size_t)a.ld;
+    v.f = a.f ? a.f + off : nullptr;
+    v.hi = a.hi ? a.hi + off : nullptr;
+    v.lo = a.lo ? a.lo + off : nullptr;
+    return v;
+}
+
+DitBufs dit_rows(const DitBufs& d, size_t row, int hidden) {
+    DitBufs v;
+    v.x = d.x + row * hidden;
+    v.norm = act_rows(d.norm, row);
+    v.attn = act_rows(d.attn, row);
+    v.ff = act_rows(d.ff, row);
+    v.qkv = d.qkv + row * 3 * hidden;
+    return v;
+}
+
+// Groups for R requests: the option (default 1); at most kMaxGroups and at most R. Measured on
+// B200 at 64 requests: 1 group 642, 2 groups 560, 4 groups 447 audio-s/s -- concurrent chains
+// contend for whole SMs (a tensor-core GEMM CTA holds 200 KB of shared memory) and CTAs launched
+// early by programmatic dependent launch park on SMs the other chain needs.
+int group_count(const mt_engine* e, int R) {
+    int G = e->opt.groups > 0 ? e->opt.groups : 1;
+    if (G > kMaxGroups) G = kMaxGroups;
+    if (G > R) G = R;
+    return G < 1 ? 1 : G;
+}
+
+// Views and decode-time plans of group g over requests [r0, r0 + Rg).
+mt_status plan_group(mt_engine* e, Group& g, int r0, int Rg) {
+    const mt_model_config& c = e->cfg;
+    const int H = c.llm.hidden, L = c.latent_dim, qkvw = (c.llm.heads + 2 * c.llm.kv_heads) * 64;
+    const size_t req_stride = (size_t)c.llm.layers * 2 * c.llm.kv_heads * e->llm.cap * 64;
+    g.r0 = r0;
+    g.R = Rg;
+    g.llm = e->llm;
+    g.llm.x = e->llm.x + (size_t)r0 * H;
+    g.llm.norm = act_rows(e->llm.norm, r0);
+    g.llm.attn = act_rows(e->llm.attn, r0);
+    g.llm.mlp = act_rows(e->llm.mlp, r0);
+    g.llm.qkv = e->llm.qkv + (size_t)r0 * qkvw;
+    g.llm.kv = e->llm.kv + (size_t)r0 * req_stride;
+    g.z = act_rows(e->z, r0);
+    g.agg_norm = act_rows(e->agg_norm, r0);
+    g.stop = e->stop + (size_t)r0 * 2;
+    g.cemb = e->cemb + (size_t)r0 * c.flow.hidden;
+    g.y = e->y + (size_t)r0 * L;
+    g.hist = e->hist + (size_t)r0 * L;
+    g.noise = e->noise + (size_t)r0 * e->opt.max_steps * L;
+    g.latents = e->latents + (size_t)r0 * e->opt.max_steps * L;
+    g.vel0 = e->vel0 + (size_t)r0 * c.flow_steps * 2 * L;
+    g.vae_h = e->vae_h + (size_t)r0 * VAE_H_RING * c.vae.hidden;
+    g.flow = dit_rows(e->flow, (size_t)6 * r0, c.flow.hidden);
+    g.agg = dit_rows(e->agg, (size_t)2 * r0, c.agg.hidden);
+    g.llm_pos = e->state_dev + st_llm_pos(e->R) + r0;
+    // Split-K workspaces are per stream and the groups run concurrently: group plans use none.
+    TRY(plan_qwen(e, g.llm_dec, e->w.llm, g.llm, Rg, nullptr, 0));
+    TRY(make_lin(e, &g.cond, g.z, Rg, e->w.flow_c_w, nullptr, e->w.flow_c_b, c.flow.hidden, H, g.cemb, c.flow.hidden,
+                 nullptr, 0));
+    {
+        // The stop head has two outputs: always the GEMV (rows processed in chunks of 8).
+        LinearArgs a{};
+        a.x = g.z.f; a.ldx = g.z.ld; a.m = Rg; a.n = 2; a.k = H; a.w = e->w.stop_w; a.bias = e->w.stop_b;
+        a.flags = MT_LINEAR_BIAS; a.y = g.stop; a.ldy = 2;
+        g.stop_lin.tc = false;
+        g.stop_lin.g = a;
+    }
+    TRY(plan_dit(e, g.flow_blocks, e->w.flow, g.flow, 6 * Rg, nullptr, 0));
+    TRY(plan_dit(e, g.agg_blocks, e->w.agg, g.agg, 2 * Rg, nullptr, 0));
+    TRY(make_lin(e, &g.agg_final, g.agg_norm, Rg, e->w.agg.final_w, nullptr, e->w.agg.final_b, c.agg.out_dim,
+                 c.agg.hidden, g.llm.x, H, nullptr, 0));
+    return MT_OK;
+}
+
 mt_status build_plans(mt_engine* e) {
     if (e->plan_R == e->R && e->plan_T == e->T) return MT_OK;
     const int R = e->R, T = e->T;
     const mt_model_config& c = e->cfg;
-    TRY(plan_qwen(e, e->llm_dec, e->w.llm, e->llm, R, e->ws_a, e->ws_a_floats));
     TRY(plan_qwen(e, e->llm_pre, e->w.llm, e->llm, R * T, e->ws_a, e->ws_a_floats));
-    TRY(make_lin(e, &e->cond, e->z, R, e->w.flow_c_w, nullptr, e->w.flow_c_b, c.flow.hidden, c.llm.hidden, e->cemb,
-                 c.flow.hidden, nullptr, 0));
-    {
-        // The stop head has two outputs: always the GEMV (rows processed in chunks of 8).
-        LinearArgs a{};
-        a.x = e->z.f; a.ldx = e->z.ld; a.m = R; a.n = 2; a.k = c.llm.hidden; a.w = e->w.stop_w; a.bias = e->w.stop_b;
-        a.flags = MT_LINEAR_BIAS; a.y = e->stop; a.ldy = 2;
-        e->stop_lin.tc = false;
-        e->stop_lin.g = a;
+    e->G = group_count(e, R);
+    for (int i = 0, r0 = 0; i < e->G; i++) {
+        const int Rg = R / e->G + (i < R % e->G ? 1 : 0);
+        TRY(plan_group(e, e->groups[i], r0, Rg));
+        r0 += Rg;
     }
-    TRY(plan_dit(e, e->flow_blocks, e->w.flow, e->flow, 6 * R, e->ws_a, e->ws_a_floats));
-    TRY(plan_dit(e, e->agg_blocks, e->w.agg, e->agg, 2 * R, e->ws_a, e->ws_a_floats));
-    TRY(make_lin(e, &e->agg_final, e->agg_norm, R, e->w.agg.final_w, nullptr, e->w.agg.final_b, c.agg.out_dim,
-                 c.agg.hidden, e->llm.x, c.llm.hidden, nullptr, 0));
     TRY(plan_qwen(e, e->vae_layers, e->w.vae, e->vae, 4 * R, e->ws_b, e->ws_b_floats));
     TRY(make_lin(e, &e->vae_head, e->vae_hidden, 4 * R, e->w.vae_head_w, nullptr, e->w.vae_head_b, c.nfft + 2,
                  c.vae.hidden, e->spec, c.nfft + 2, nullptr, 0));
@@ -396,48 +485,47 @@ mt_status precompute_temb(mt_engine* e) {
 
 // ---- step pieces ---------------------------------------------------------------------------------
 
-void llm_token(mt_engine* e, cudaStream_t s) {
+void llm_token(mt_engine* e, Group& g, cudaStream_t s) {
     const mt_qwen_config& c = e->cfg.llm;
-    const int R = e->R;
-    qwen_forward(e, e->w.llm, e->llm, e->llm_dec, R, 1, 0, e->state_dev + st_llm_pos(R), e->llm.cap, s);
-    norm(e->llm.x, c.hidden, R, c.hidden, e->w.llm.final_norm, c.eps, e->z, R, true, s);
+    qwen_forward(e, e->w.llm, g.llm, g.llm_dec, g.R, 1, 0, g.llm_pos, g.llm.cap, s);
+    norm(g.llm.x, c.hidden, g.R, c.hidden, e->w.llm.final_norm, c.eps, g.z, g.R, true, s);
 }
 
-void flow_stage(mt_engine* e, cudaStream_t s) {
+void flow_stage(mt_engine* e, Group& g, cudaStream_t s) {
     const mt_model_config& c = e->cfg;
-    const int R = e->R, L = c.latent_dim, Df = c.flow.hidden;
-    run(e->stop_lin, s);
-    run(e->cond, s);
-    launch_flow_begin(e->y, e->hist, e->noise, L, e->opt.max_steps, e->state_dev, R, s); g_kernels++;
+    const int R = g.R, L = c.latent_dim, Df = c.flow.hidden;
+    run(g.stop_lin, s);
+    run(g.cond, s);
+    launch_flow_begin(g.y, g.hist, g.noise, L, e->opt.max_steps, e->state_dev, R, s); g_kernels++;
     for (int k = 0; k < c.flow_steps; k++) {
-        launch_flow_assemble_batched(e->y, e->hist, e->cemb, e->w.flow_c_b, e->temb + (size_t)k * Df, e->w.flow_x_w,
-                                     e->w.flow_x_b, Df, L, e->flow.x, R, s);
+        launch_flow_assemble_batched(g.y, g.hist, g.cemb, e->w.flow_c_b, e->temb + (size_t)k * Df, e->w.flow_x_w,
+                                     e->w.flow_x_b, Df, L, g.flow.x, R, s);
         g_kernels++;
-        dit_blocks(e, e->w.flow, e->flow, e->flow_blocks, 2 * R, 3, s);
+        dit_blocks(e, e->w.flow, g.flow, g.flow_blocks, 2 * R, 3, s);
         FlowFinalArgs fa{};
-        fa.X = e->flow.x; fa.hidden = Df; fa.norm_w = e->w.flow.final_norm; fa.eps = c.flow.eps;
-        fa.final_w = e->w.flow.final_w; fa.final_b = e->w.flow.final_b; fa.latent = L; fa.y = e->y;
-        fa.cfg = e->cfg_scale; fa.dt = e->timesteps[k + 1] - e->timesteps[k]; fa.vel0 = e->vel0;
-        fa.flow_steps = c.flow_steps; fa.k = k; fa.latents = e->latents; fa.steps_cap = e->opt.max_steps;
+        fa.X = g.flow.x; fa.hidden = Df; fa.norm_w = e->w.flow.final_norm; fa.eps = c.flow.eps;
+        fa.final_w = e->w.flow.final_w; fa.final_b = e->w.flow.final_b; fa.latent = L; fa.y = g.y;
+        fa.cfg = e->cfg_scale; fa.dt = e->timesteps[k + 1] - e->timesteps[k]; fa.vel0 = g.vel0;
+        fa.flow_steps = c.flow_steps; fa.k = k; fa.latents = g.latents; fa.steps_cap = e->opt.max_steps;
         fa.state = e->state_dev;
         launch_flow_final(fa, R, s); g_kernels++;
     }
 }
 
 // Aggregator (Engine.swift:406-410): [cls, x_emb(latent)] -> DiT -> final layer of row 0 -> LLM input.
-void agg_stage(mt_engine* e, cudaStream_t s) {
+void agg_stage(mt_engine* e, Group& g, cudaStream_t s) {
     const mt_model_config& c = e->cfg;
-    const int R = e->R, L = c.latent_dim;
+    const int R = g.R, L = c.latent_dim;
     const int Da = c.agg.hidden;
-    launch_agg_assemble(e->y, e->w.agg_cls, e->w.agg_x_w, e->w.agg_x_b, Da, L, e->agg.x, R, s); g_kernels++;
-    dit_blocks(e, e->w.agg, e->agg, e->agg_blocks, R, 2, s);
-    norm(e->agg.x, 2 * Da, R, Da, e->w.agg.final_norm, c.agg.eps, e->agg_norm, R, false, s);
-    run(e->agg_final, s);
+    launch_agg_assemble(g.y, e->w.agg_cls, e->w.agg_x_w, e->w.agg_x_b, Da, L, g.agg.x, R, s); g_kernels++;
+    dit_blocks(e, e->w.agg, g.agg, g.agg_blocks, R, 2, s);
+    norm(g.agg.x, 2 * Da, R, Da, e->w.agg.final_norm, c.agg.eps, g.agg_norm, R, false, s);
+    run(g.agg_final, s);
 }
 
-void vae_fc1(mt_engine* e, cudaStream_t s) {
+void vae_fc1(mt_engine* e, Group& g, cudaStream_t s) {
     const mt_model_config& c = e->cfg;
-    launch_vae_fc1(e->y, e->w.vae_fc1_w, e->w.vae_fc1_b, c.vae.hidden, c.latent_dim, e->vae_h, e->state_dev, e->R, s);
+    launch_vae_fc1(g.y, e->w.vae_fc1_w, e->w.vae_fc1_b, c.vae.hidden, c.latent_dim, g.vae_h, e->state_dev, g.R, s);
     g_kernels++;
 }
 
@@ -489,25 +577,34 @@ void upload_state(mt_engine* e, cudaStream_t s) {
 
 // Enqueues the device work of a step whose state is already uploaded. with_llm: n > 0;
 // with_decode: a VAE decode is due.
+// Forks the VAE decode (stream B) and every group's chain from s, and joins them back into s.
+// Stage events (timed) are recorded on group 0's chain.
 void enqueue_step(mt_engine* e, cudaStream_t s, bool with_llm, bool with_decode, bool timed) {
     cudaEvent_t* ev = e->stage_ev;
     if (timed) cudaEventRecord(ev[0], s);
+    cudaEventRecord(e->ev_fork, s);
     if (with_decode) {
-        cudaEventRecord(e->ev_fork, s);
         cudaStreamWaitEvent(e->sb, e->ev_fork, 0);
         if (timed) cudaEventRecord(ev[4], e->sb);
         vae_decode(e, e->sb);
         if (timed) cudaEventRecord(ev[5], e->sb);
         cudaEventRecord(e->ev_join, e->sb);
     }
-    if (with_llm) llm_token(e, s);
-    if (timed) cudaEventRecord(ev[1], s);
-    flow_stage(e, s);
-    if (timed) cudaEventRecord(ev[2], s);
-    agg_stage(e, s);
-    if (timed) cudaEventRecord(ev[3], s);
+    for (int i = 0; i < e->G; i++) {
+        Group& g = e->groups[i];
+        cudaStream_t gs = i == 0 ? s : g.s;
+        if (i > 0) cudaStreamWaitEvent(gs, e->ev_fork, 0);
+        if (with_llm) llm_token(e, g, gs);
+        if (timed && i == 0) cudaEventRecord(ev[1], gs);
+        flow_stage(e, g, gs);
+        if (timed && i == 0) cudaEventRecord(ev[2], gs);
+        agg_stage(e, g, gs);
+        if (timed && i == 0) cudaEventRecord(ev[3], gs);
+        vae_fc1(e, g, gs);
+        if (i > 0) cudaEventRecord(g.done, gs);
+    }
+    for (int i = 1; i < e->G; i++) cudaStreamWaitEvent(s, e->groups[i].done, 0);
     if (with_decode) cudaStreamWaitEvent(s, e->ev_join, 0);
-    vae_fc1(e, s);
 }
 
 }  // namespace
@@ -587,6 +684,10 @@ mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_o
         cudaEventCreateWithFlags(&e->ev_in, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&e->ev_out, cudaEventDisableTiming) != cudaSuccess)
         return cleanup(fail(ctx, MT_ERR_CUDA, "engine: stream/event creation"));
+    for (int i = 1; i < group_count(e, R); i++)
+        if (cudaStreamCreateWithFlags(&e->groups[i].s, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&e->groups[i].done, cudaEventDisableTiming) != cudaSuccess)
+            return cleanup(fail(ctx, MT_ERR_CUDA, "engine: group stream/event creation"));
     ETRY(precompute_temb(e));
 #undef ETRY
     *out = e;
@@ -599,6 +700,10 @@ void mt_engine_destroy(mt_engine* e) {
     if (e->graph) cudaGraphDestroy(e->graph);
     if (e->sa) cudaStreamDestroy(e->sa);
     if (e->sb) cudaStreamDestroy(e->sb);
+    for (int i = 0; i < kMaxGroups; i++) {
+        if (e->groups[i].s) cudaStreamDestroy(e->groups[i].s);
+        if (e->groups[i].done) cudaEventDestroy(e->groups[i].done);
+    }
     if (e->ev_fork) cudaEventDestroy(e->ev_fork);
     if (e->ev_join) cudaEventDestroy(e->ev_join);
     if (e->ev_in) cudaEventDestroy(e->ev_in);
