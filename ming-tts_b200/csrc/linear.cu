@@ -161,7 +161,68 @@ static int gemv_group(int k) {
     return g;
 }
 
+// Few outputs (n <= 4, e.g. the 2-logit stop head): one warp per row of x; lane l covers k
+// columns 4l + 128t and every output's dot product, so x is read once and all loads of a warp are
+// in flight together. Weights are read before the dependency wait.
+constexpr int NARROW_MAX_N = 4;
+constexpr int NARROW_MAX_T = 8;  // k <= 1024 held in registers; longer k loops
+
+__global__ void __launch_bounds__(256) gemv_narrow_kernel(LinearArgs a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + warp;
+    const int T = a.k / 128;  // k % 128 == 0
+    uint2 w[NARROW_MAX_N][NARROW_MAX_T];
+    const bool fits = T <= NARROW_MAX_T;
+    if (fits) {
+#pragma unroll
+        for (int j = 0; j < NARROW_MAX_N; j++)
+#pragma unroll
+            for (int t = 0; t < NARROW_MAX_T; t++)
+                if (j < a.n && t < T) w[j][t] = *reinterpret_cast<const uint2*>(a.w + (size_t)j * a.k + 4 * lane + 128 * t);
+    }
+    pdl_wait();
+    pdl_launch();
+    if (row >= a.m) return;
+    const float* x = a.x + (size_t)row * a.ldx;
+    float acc[NARROW_MAX_N] = {0.f, 0.f, 0.f, 0.f};
+    for (int t0 = 0; t0 < T; t0 += NARROW_MAX_T) {
+        float4 xv[NARROW_MAX_T];
+#pragma unroll
+        for (int t = 0; t < NARROW_MAX_T; t++)
+            if (t0 + t < T) xv[t] = *reinterpret_cast<const float4*>(x + 4 * lane + 128 * (t0 + t));
+#pragma unroll
+        for (int j = 0; j < NARROW_MAX_N; j++) {
+            if (j >= a.n) break;
+#pragma unroll
+            for (int t = 0; t < NARROW_MAX_T; t++) {
+                if (t0 + t < T) {
+                    const uint2 wv = fits ? w[j][t]
+                                          : *reinterpret_cast<const uint2*>(a.w + (size_t)j * a.k + 4 * lane + 128 * (t0 + t));
+                    acc[j] += xv[t].x * bf16_lo(wv.x) + xv[t].y * bf16_hi(wv.x) + xv[t].z * bf16_lo(wv.y) +
+                              xv[t].w * bf16_hi(wv.y);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < NARROW_MAX_N; j++) acc[j] = warp_sum(acc[j]);
+    if (lane >= a.n) return;
+    float v = acc[0];
+#pragma unroll
+    for (int j = 1; j < NARROW_MAX_N; j++) if (lane == j) v = acc[j];
+    if (a.flags & MT_LINEAR_BIAS) v += bf16f(a.bias[lane]);
+    if (a.flags & MT_LINEAR_GELU) v = gelu_tanh(v);
+    if (a.flags & MT_LINEAR_SILU) v = silu(v);
+    float* yp = a.y + (size_t)row * a.ldy + lane;
+    if (a.flags & MT_LINEAR_ACCUM) v += *yp;
+    *yp = v;
+}
+
 void launch_gemv(const LinearArgs& a, cudaStream_t s) {
+    if (a.n <= NARROW_MAX_N && a.k % 128 == 0 && !(a.flags & MT_LINEAR_SILU_GATE) && a.ldx % 4 == 0) {
+        launch_k(gemv_narrow_kernel, (a.m + 7) / 8, 256, 0, s, a);
+        return;
+    }
     const int G = gemv_group(a.k);
     const bool gated = (a.flags & MT_LINEAR_SILU_GATE) != 0;
     const int mr = a.m <= 1 ? 1 : a.m <= 2 ? 2 : a.m <= 4 ? 4 : 8;

@@ -249,6 +249,7 @@ mt_status check_config(mt_ctx* ctx, const mt_model_config& c) {
     MT_REQUIRE(ctx, ok_qwen(c.llm) && ok_qwen(c.vae) && ok_dit(c.flow) && ok_dit(c.agg), MT_ERR_SHAPE,
                "model config: unsupported stack dimensions (head dim 64, hidden %% 64, heads/kv <= 8)");
     MT_REQUIRE(ctx, c.flow.out_dim == c.latent_dim && c.agg.out_dim == c.llm.hidden && c.latent_dim % 8 == 0 &&
+                        c.latent_dim <= 64 && c.flow.hidden % 128 == 0 && c.flow.hidden <= 1024 &&
                         c.time_dim % 8 == 0 && c.nfft % 4 == 0 && c.hop > 0 && (c.nfft - c.hop) % 2 == 0 &&
                         c.flow_steps > 0 && c.llm_capacity > 1,
                MT_ERR_SHAPE, "model config: inconsistent dimensions");

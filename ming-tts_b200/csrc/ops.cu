@@ -274,62 +274,78 @@ void launch_attention(const AttnArgs& a, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------------------------------------
-// DiT attention: one warp per (sequence, row, head); lane l owns dims 2l, 2l+1 = one interleaved
-// RoPE pair, so q and k rotate with one sincos per position.
+// DiT attention: one warp per (sequence, head) computes every row of the sequence (seq <= 8);
+// lane l owns dims 2l, 2l+1 = one interleaved RoPE pair. All q/k/v loads of the warp are issued
+// before any use, and each position's rotation is computed once.
 // ------------------------------------------------------------------------------------------------
+constexpr int DIT_MAX_SEQ = 8;
+
 __global__ void dit_attention_kernel(DitAttnArgs a) {
     pdl_wait();
     pdl_launch();
     const int work = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (work >= a.batch * a.seq * a.heads) return;
-    const int h = work % a.heads, i = (work / a.heads) % a.seq, b = work / (a.heads * a.seq);
-    const int D = a.heads * 64;
+    if (work >= a.batch * a.heads) return;
+    const int h = work % a.heads, b = work / a.heads;
+    const int D = a.heads * 64, S = a.seq;
     const float freq = a.inv_freq[lane];
-    const float* rows = a.qkv + (size_t)b * a.seq * a.ld + h * 64 + 2 * lane;
-    float s, c;
-    sincosf((float)i * freq, &s, &c);
-    const float2 qr = *reinterpret_cast<const float2*>(rows + (size_t)i * a.ld);
-    const float q0 = qr.x * c - qr.y * s, q1 = qr.y * c + qr.x * s;
-    float sc[8];
-    float mx = -INFINITY;
+    const float* rows = a.qkv + (size_t)b * S * a.ld + h * 64 + 2 * lane;
+    float2 q[DIT_MAX_SEQ], k[DIT_MAX_SEQ], v[DIT_MAX_SEQ];
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        if (j < a.seq) {
+    for (int j = 0; j < DIT_MAX_SEQ; j++) {
+        if (j < S) {
+            q[j] = *reinterpret_cast<const float2*>(rows + (size_t)j * a.ld);
+            k[j] = *reinterpret_cast<const float2*>(rows + (size_t)j * a.ld + D);
+            v[j] = *reinterpret_cast<const float2*>(rows + (size_t)j * a.ld + 2 * D);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < DIT_MAX_SEQ; j++) {  // rotate q and k of position j
+        if (j < S) {
             float sj, cj;
             sincosf((float)j * freq, &sj, &cj);
-            const float2 kr = *reinterpret_cast<const float2*>(rows + (size_t)j * a.ld + D);
-            const float k0 = kr.x * cj - kr.y * sj, k1 = kr.y * cj + kr.x * sj;
-            sc[j] = warp_sum(q0 * k0 + q1 * k1) * 0.125f;
-            mx = fmaxf(mx, sc[j]);
+            q[j] = make_float2(q[j].x * cj - q[j].y * sj, q[j].y * cj + q[j].x * sj);
+            k[j] = make_float2(k[j].x * cj - k[j].y * sj, k[j].y * cj + k[j].x * sj);
         }
     }
-    float sum = 0.f, acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        if (j < a.seq) {
-            const float e = expf(sc[j] - mx);
-            sum += e;
-            const float2 v = *reinterpret_cast<const float2*>(rows + (size_t)j * a.ld + 2 * D);
-            acc0 += e * v.x;
-            acc1 += e * v.y;
+    for (int i = 0; i < DIT_MAX_SEQ; i++) {
+        if (i >= S) break;
+        float sc[DIT_MAX_SEQ];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < DIT_MAX_SEQ; j++) {
+            if (j < S) {
+                sc[j] = warp_sum(q[i].x * k[j].x + q[i].y * k[j].y) * 0.125f;
+                mx = fmaxf(mx, sc[j]);
+            }
         }
-    }
-    const float o0 = acc0 / sum, o1 = acc1 / sum;
-    const size_t row = (size_t)(b * a.seq + i);
-    if (a.out) *reinterpret_cast<float2*>(a.out + row * a.ldo + h * 64 + 2 * lane) = make_float2(o0, o1);
-    if (a.out_hi) {
-        uint16_t h0, l0, h1, l1;
-        split_bf16(o0, h0, l0);
-        split_bf16(o1, h1, l1);
-        const size_t so = row * a.ld_split + h * 64 + 2 * lane;
-        *reinterpret_cast<uint32_t*>(a.out_hi + so) = h0 | ((uint32_t)h1 << 16);
-        *reinterpret_cast<uint32_t*>(a.out_lo + so) = l0 | ((uint32_t)l1 << 16);
+        float sum = 0.f, acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < DIT_MAX_SEQ; j++) {
+            if (j < S) {
+                const float e = expf(sc[j] - mx);
+                sum += e;
+                acc0 += e * v[j].x;
+                acc1 += e * v[j].y;
+            }
+        }
+        const float o0 = acc0 / sum, o1 = acc1 / sum;
+        const size_t row = (size_t)(b * S + i);
+        if (a.out) *reinterpret_cast<float2*>(a.out + row * a.ldo + h * 64 + 2 * lane) = make_float2(o0, o1);
+        if (a.out_hi) {
+            uint16_t h0, l0, h1, l1;
+            split_bf16(o0, h0, l0);
+            split_bf16(o1, h1, l1);
+            const size_t so = row * a.ld_split + h * 64 + 2 * lane;
+            *reinterpret_cast<uint32_t*>(a.out_hi + so) = h0 | ((uint32_t)h1 << 16);
+            *reinterpret_cast<uint32_t*>(a.out_lo + so) = l0 | ((uint32_t)l1 << 16);
+        }
     }
 }
 
 void launch_dit_attention(const DitAttnArgs& a, cudaStream_t s) {
-    const int work = a.batch * a.seq * a.heads;
+    const int work = a.batch * a.heads;
     launch_k(dit_attention_kernel, (work + 7) / 8, 256, 0, s, a);
 }
 

@@ -64,7 +64,7 @@ def gemv_case(ctx, mt, oracle, m, n, k, flags, bias, x_scale=1.0):
 @pytest.mark.parametrize("m,n,k,flags,bias", [
     (1, 1152, 896, 0, True), (2, 2, 896, 0, True), (4, 896, 4864, 2, False), (6, 4096, 1024, 4, True),
     (3, 64, 1024, 0, True), (21, 300, 896, 0, False), (4, 3530, 896, 0, True), (1, 896, 64, 0, True),
-    (8, 2, 896, 0, True),
+    (8, 2, 896, 0, True), (3, 4, 1024, 4, True), (5, 3, 256, 2, False), (7, 1, 1152, 16, True), (2, 2, 200, 0, True),
 ])
 def test_gemv_shapes(ctx, mt, oracle, m, n, k, flags, bias):
     gemv_case(ctx, mt, oracle, m, n, k, flags, bias)
