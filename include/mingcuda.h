@@ -230,6 +230,16 @@ mt_status mt_attention(mt_ctx* ctx, void* stream, const float* q, int ldq, int m
                        int pos0, int window, const float* k_cache, const float* v_cache,
                        int capacity, float* out, int ldo);
 
+/* mt_rope_cache followed by mt_attention in one kernel, for decode steps of m <= 4 rows of one
+ * request (the LLM token, the VAE decode's four frames): rotates the q heads and k, appends k and v
+ * at positions pos0..pos0+m-1 (slot = position % capacity; the cache may be a ring when window > 0
+ * and window + m - 1 <= capacity), attends as mt_attention does, and writes out[m, hq*64]. qkv is
+ * not modified. chunk_keys (0 = automatic) bounds the keys staged in shared memory at once.
+ * Replaces Encoder.ropeCache + Encoder.attention (Kernels.swift:182-206) on the decode path. */
+mt_status mt_rope_attention(mt_ctx* ctx, void* stream, const float* qkv, int ldq, int m, int hq, int hkv, int pos0,
+                            int window, float* k_cache, float* v_cache, int capacity, const float* inv_freq,
+                            float* out, int ldo, int chunk_keys);
+
 /* Full attention over `batch` sequences of `seq` <= 8 rows with interleaved RoPE (pairs 2l, 2l+1,
  * angle = row * inv_freq[l]). qkv rows are [q | k | v] of heads*64 each, row stride ld.
  * Replaces Encoder.ditAttention (Kernels.swift:210-220), dit_attention (Shaders.swift:613-648). */

@@ -112,6 +112,8 @@ PROTOTYPES = {
                                 c_uint32]),
     "mt_linear_static": (c_int, [_P, _P, c_int, c_int, _P, _P, _P, c_int, c_int, _P, c_int, c_uint32]),
     "mt_rmsnorm": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P, _P, c_int, c_float]),
+    "mt_rope_attention": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, c_int, _P, _P, c_int,
+                                  c_int]),
     "mt_copy": (c_int, [_P, _P, _P, c_int, _P]),
     "mt_rope_cache": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, _P, c_int, _P]),
     "mt_attention": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, c_int, _P, c_int]),

@@ -394,6 +394,22 @@ void qwen_forward(mt_engine* e, const mt_qwen_weights& W, QwenBufs& b, std::vect
         float* vc = kc + tensor;
         norm(b.x, c.hidden, rows, c.hidden, L.norm1, c.eps, b.norm, rows, false, s);
         run(plans[l].qkv, s);
+        if (attention_decode_supported(rows_per_req, c.heads, c.kv_heads)) {
+            // Decode: every row of a request in one block, RoPE and the KV append fused in.
+            AttnDecodeArgs da{};
+            da.qkv = b.qkv; da.ldq = qkvw; da.requests = rows / rows_per_req; da.rows_per_req = rows_per_req;
+            da.hq = c.heads; da.hkv = c.kv_heads; da.pos0 = pos0; da.pos_dev = pos_dev; da.window = c.window;
+            da.kc = kc; da.vc = vc; da.req_stride = req_stride; da.cap = b.cap; da.inv_freq = b.inv_freq;
+            if (tc) { da.out_hi = b.attn.hi; da.out_lo = b.attn.lo; da.ld_split = b.attn.ld; }
+            else { da.out = b.attn.f; da.ldo = b.attn.ld; }
+            da.max_keys = max_keys; da.status = e->ctx->d_status;
+            launch_attention_decode(da, s); g_kernels++;
+            run(plans[l].o, s);
+            norm(b.x, c.hidden, rows, c.hidden, L.norm2, c.eps, b.norm, rows, false, s);
+            run(plans[l].gu, s);
+            run(plans[l].down, s);
+            continue;
+        }
         RopeArgs ra{};
         ra.qkv = b.qkv; ra.ldq = qkvw; ra.rows = rows; ra.rows_per_req = rows_per_req; ra.hq = c.heads;
         ra.hkv = c.kv_heads; ra.pos0 = pos0; ra.pos_dev = pos_dev; ra.kc = kc; ra.vc = vc; ra.req_stride = req_stride;

@@ -31,61 +31,8 @@ constexpr int TC_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (
 constexpr int TC_EPI_WARPS = 8;
 constexpr int TC_BM = 128;  // weight rows per tile (MMA M)
 constexpr int TC_BK = 64;   // bf16 K per stage = one 128-byte swizzle span
-constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait
 
 
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Bounded wait on the phase with the given parity: gives up after WAIT_NS of wall time (checked
-// every 256 polls) or as soon as another thread of the CTA has raised *abort; a wait that times out
-// records the site in the status word, raises *abort and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status, unsigned site,
-                                          volatile int* abort) {
-    const uint32_t addr = smem_u32(bar);
-    uint64_t t0 = 0;
-    for (uint32_t i = 0;; i++) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        if ((i & 255u) == 255u) {
-            if (*abort) return false;
-            const uint64_t now = global_ns();
-            if (t0 == 0) t0 = now;
-            else if (now - t0 > WAIT_NS) break;
-        }
-    }
-    report_status(status, DEV_TIMEOUT, site, blockIdx.x);
-    *abort = 1;
-    return false;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
     asm volatile(

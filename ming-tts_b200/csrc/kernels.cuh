@@ -41,6 +41,25 @@ struct AttnArgs {
 size_t attention_smem(int G, int max_keys);
 void launch_attention(const AttnArgs& a, cudaStream_t s);
 
+// Decode attention with RoPE and the KV append fused in, for steps where every row of a request
+// is in one block (rows_per_req <= 4: the LLM token, the VAE decode): block (request, kv head)
+// rotates its rows' q heads and the new k, appends k and v to the cache, and attends over the
+// request's cached keys (bulk-copied into shared memory) plus the new ones.
+struct AttnDecodeArgs {
+    const float* qkv; int ldq; int requests; int rows_per_req; int hq; int hkv;
+    int pos0; const int* pos_dev; int window;
+    float* kc; float* vc; long long req_stride; int cap;
+    const float* inv_freq;                    // [32] NeoX rotation frequencies
+    float* out; int ldo;                      // optional fp32 output
+    uint16_t* out_hi; uint16_t* out_lo; int ld_split;  // optional bf16 hi/lo output
+    int max_keys;                             // keys any row attends to, at most (cache capacity if unbounded)
+    int chunk_keys;                           // keys staged per chunk (0: as many as shared memory holds)
+    unsigned int* status;                     // bounded-wait failures
+};
+constexpr int ATTN_DECODE_MAX_ROWS = 4;
+bool attention_decode_supported(int rows_per_req, int hq, int hkv);
+void launch_attention_decode(const AttnDecodeArgs& a, cudaStream_t s);
+
 struct DitAttnArgs {
     const float* qkv; int ld; int batch; int seq; int heads;
     const float* inv_freq;

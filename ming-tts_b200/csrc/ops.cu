@@ -274,6 +274,300 @@ void launch_attention(const AttnArgs& a, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------------------------------------
+// Fused decode attention (see AttnDecodeArgs). Block (request, kv head), 256 threads. The union of
+// the request rows' key ranges is processed in chunks of SC keys: old keys arrive by bulk copy
+// (cp.async.bulk, at most two segments per chunk when the cache ring wraps) on bounded mbarrier
+// waits, new keys come from the block's own rotation. Scores use a skewed float4 walk over the
+// 64 dims so the 32 keys a warp touches fall in distinct bank groups; softmax is online across
+// chunks; thread groups of P own (row-head, 4 dims) accumulators for P.V.
+// ------------------------------------------------------------------------------------------------
+constexpr int AD_THREADS = 256;
+constexpr int AD_MAX_RG = ATTN_DECODE_MAX_ROWS * 8;  // rows x query heads per kv head
+
+static size_t ad_dyn_bytes(int SC, int nrows, int nrg) {
+    return sizeof(float) * ((size_t)SC * 64 * 2 + (size_t)nrg * 64 + (size_t)nrows * 128 + (size_t)nrg * SC);
+}
+
+__global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecodeArgs a, int SC) {
+    extern __shared__ __align__(128) float sm[];
+    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ float m_run[AD_MAX_RG], l_run[AD_MAX_RG], alpha[AD_MAX_RG];
+    __shared__ float rot_c[ATTN_DECODE_MAX_ROWS][32], rot_s[ATTN_DECODE_MAX_ROWS][32];
+    __shared__ int abort_flag;
+    const int r = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = a.hq / a.hkv, nrows = a.rows_per_req, nrg = nrows * G;
+    float* Ks = sm;
+    float* Vs = Ks + (size_t)SC * 64;
+    float* qs = Vs + (size_t)SC * 64;
+    float* nw = qs + (size_t)nrg * 64;  // [nrows][k | v][64]
+    float* sc = nw + (size_t)nrows * 128;
+    volatile int* abort = &abort_flag;
+
+    // Everything up to pdl_wait reads only what earlier kernels and the host finished long ago:
+    // positions (host-uploaded step state), rotation frequencies, and the cached keys and values
+    // of earlier positions (this launch writes only the new positions' slots).
+    const int base = a.pos0 + (a.pos_dev ? a.pos_dev[r] : 0);
+    const int p_first = base, p_end = base + nrows;  // new keys [p_first, p_end)
+    const int W = a.window;
+    const int jS = W > 0 ? max(0, p_first + 1 - W) : 0;
+    const int nk = p_end - jS;
+    const int chunks = (nk + SC - 1) / SC;
+    float* kc = a.kc + (size_t)r * a.req_stride + (size_t)h * a.cap * 64;
+    float* vc = a.vc + (size_t)r * a.req_stride + (size_t)h * a.cap * 64;
+    // Old keys of chunk c: [c0, min(c1, p_first)); thread 0 arms both barriers and issues the copies.
+    auto issue = [&](int c) {
+        const int c0 = jS + c * SC, c1 = min(c0 + SC, p_end);
+        const int nold = max(0, min(c1, p_first) - c0);
+        const uint32_t bytes = (uint32_t)nold * 256u;
+        mbar_expect_tx(&bar[0], bytes);
+        mbar_expect_tx(&bar[1], bytes);
+        if (nold > 0) {
+            const int s0 = c0 % a.cap;
+            const int len1 = min(nold, a.cap - s0);
+            bulk_load(Ks, kc + (size_t)s0 * 64, (uint32_t)len1 * 256u, &bar[0]);
+            bulk_load(Vs, vc + (size_t)s0 * 64, (uint32_t)len1 * 256u, &bar[1]);
+            if (len1 < nold) {
+                bulk_load(Ks + (size_t)len1 * 64, kc, (uint32_t)(nold - len1) * 256u, &bar[0]);
+                bulk_load(Vs + (size_t)len1 * 64, vc, (uint32_t)(nold - len1) * 256u, &bar[1]);
+            }
+        }
+    };
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        issue(0);
+    }
+    if (tid < nrg) {
+        m_run[tid] = -INFINITY;
+        l_run[tid] = 0.f;
+    }
+    if (tid < nrows * 32) {  // NeoX rotation of position base + i, pair (l, l + 32)
+        const int i = tid >> 5, l = tid & 31;
+        float sn, cs;
+        sincosf((float)(base + i) * a.inv_freq[l], &sn, &cs);
+        rot_c[i][l] = cs;
+        rot_s[i][l] = sn;
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_launch();
+
+    // New rows: item (row i, slot, pair l), slot < G a query head of this kv group, G the key, G + 1
+    // the value. All loads first, then rotate, append k and v to the cache and stash them.
+    constexpr int NR_MAX = (ATTN_DECODE_MAX_ROWS * 10 * 32 + AD_THREADS - 1) / AD_THREADS;
+    const int items = nrows * (G + 2) * 32;
+    float x0[NR_MAX], x1[NR_MAX];
+#pragma unroll
+    for (int u = 0; u < NR_MAX; u++) {
+        const int it = tid + u * AD_THREADS;
+        if (it < items) {
+            const int l = it & 31, slot = (it >> 5) % (G + 2), i = (it >> 5) / (G + 2);
+            const float* row = a.qkv + (size_t)(r * nrows + i) * a.ldq;
+            const int col = slot < G ? (h * G + slot) * 64 : slot == G ? (a.hq + h) * 64 : (a.hq + a.hkv + h) * 64;
+            x0[u] = row[col + l];
+            x1[u] = row[col + l + 32];
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < NR_MAX; u++) {
+        const int it = tid + u * AD_THREADS;
+        if (it < items) {
+            const int l = it & 31, slot = (it >> 5) % (G + 2), i = (it >> 5) / (G + 2);
+            float v0 = x0[u], v1 = x1[u];
+            if (slot <= G) {
+                const float cs = rot_c[i][l], sn = rot_s[i][l];
+                const float r0 = v0 * cs - v1 * sn, r1 = v1 * cs + v0 * sn;
+                v0 = r0;
+                v1 = r1;
+            }
+            if (slot < G) {
+                qs[(i * G + slot) * 64 + l] = v0;
+                qs[(i * G + slot) * 64 + l + 32] = v1;
+            } else {
+                float* dst = (slot == G ? kc : vc) + (size_t)((base + i) % a.cap) * 64;
+                dst[l] = v0;
+                dst[l + 32] = v1;
+                float* st = nw + (i * 2 + (slot - G)) * 64;
+                st[l] = v0;
+                st[l + 32] = v1;
+            }
+        }
+    }
+
+    // P.V ownership: thread (4 dims d4 = tid % 16, row i, part) holds the G heads of row i; the
+    // PP parts split the keys, so the 16 lanes of a part read one V row (256 contiguous bytes).
+    const int d4 = tid & 15, grp = tid >> 4;  // 16 groups of 16 lanes
+    const int PP = (AD_THREADS / 16) / nrows;  // parts per row
+    const int pv_i = grp % nrows, pv_part = grp / nrows;
+    const bool pv_live = pv_part < PP;
+    float4 acc[8];
+#pragma unroll
+    for (int g = 0; g < 8; g++) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+    bool ok = true;
+    for (int c = 0; c < chunks && ok; c++) {
+        const int c0 = jS + c * SC, c1 = min(c0 + SC, p_end), cn = c1 - c0;
+        const int old_end = min(c1, p_first);
+        const int nold = max(0, old_end - c0);
+        __syncthreads();  // the previous chunk's readers are done with Ks, Vs and sc
+        if (c > 0 && tid == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(c);
+        }
+        // New keys of this chunk from the stash.
+        for (int e = tid; e < (cn - nold) * 64; e += AD_THREADS) {
+            const int jj = nold + e / 64, d = e % 64;
+            const int i = c0 + jj - p_first;
+            Ks[(size_t)jj * 64 + d] = nw[(i * 2) * 64 + d];
+            Vs[(size_t)jj * 64 + d] = nw[(i * 2 + 1) * 64 + d];
+        }
+        __syncthreads();
+        if (!mbar_wait(&bar[0], c & 1, a.status, 20, abort)) { ok = false; break; }
+        // Scores: item (key pair p, row i) scores keys k0 and k0 + 8 (same 16-byte skew s = p & 7,
+        // so the eight lanes of a shared-memory phase read eight distinct bank groups of K and one
+        // q chunk serves both keys) against the G heads of row i.
+        const float4* K4 = reinterpret_cast<const float4*>(Ks);
+        const float4* Q4 = reinterpret_cast<const float4*>(qs);
+        const int npairs = ((cn + 15) / 16) * 8;
+        for (int it = tid; it < npairs * nrows; it += AD_THREADS) {
+            const int pr = it % npairs, i = it / npairs;
+            const int k0 = (pr >> 3) * 16 + (pr & 7), k1 = k0 + 8;
+            const int sk = pr & 7;
+            const bool l0 = k0 < cn, l1 = k1 < cn;
+            float s0[8], s1[8];
+#pragma unroll
+            for (int g = 0; g < 8; g++) { s0[g] = 0.f; s1[g] = 0.f; }
+#pragma unroll 4
+            for (int t = 0; t < 16; t++) {
+                const int ch = (t + sk) & 15;
+                const float4 ka = l0 ? K4[k0 * 16 + ch] : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 kb = l1 ? K4[k1 * 16 + ch] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int g = 0; g < 8; g++) {
+                    if (g < G) {
+                        const float4 q4 = Q4[(i * G + g) * 16 + ch];
+                        s0[g] += q4.x * ka.x + q4.y * ka.y + q4.z * ka.z + q4.w * ka.w;
+                        s1[g] += q4.x * kb.x + q4.y * kb.y + q4.z * kb.z + q4.w * kb.w;
+                    }
+                }
+            }
+            const int pos = base + i;
+            const int j0 = c0 + k0, j1 = c0 + k1;
+            const bool v0 = j0 <= pos && (W == 0 || j0 > pos - W);
+            const bool v1 = j1 <= pos && (W == 0 || j1 > pos - W);
+#pragma unroll
+            for (int g = 0; g < 8; g++) {
+                if (g < G) {
+                    if (l0) sc[(size_t)(i * G + g) * SC + k0] = v0 ? s0[g] * 0.125f : -INFINITY;
+                    if (l1) sc[(size_t)(i * G + g) * SC + k1] = v1 ? s1[g] * 0.125f : -INFINITY;
+                }
+            }
+        }
+        __syncthreads();
+        // Online softmax statistics; scores become weights relative to the running maximum.
+        for (int rg = warp; rg < nrg; rg += AD_THREADS / 32) {
+            float* srow = sc + (size_t)rg * SC;
+            float mx = -INFINITY;
+            for (int jj = lane; jj < cn; jj += 32) mx = fmaxf(mx, srow[jj]);
+            mx = warp_max(mx);
+            const float m_old = m_run[rg];
+            const float m_new = fmaxf(m_old, mx);
+            float sum = 0.f;
+            for (int jj = lane; jj < cn; jj += 32) {
+                const float e = m_new == -INFINITY ? 0.f : expf(srow[jj] - m_new);
+                srow[jj] = e;
+                sum += e;
+            }
+            sum = warp_sum(sum);
+            if (lane == 0) {
+                const float al = m_new == -INFINITY ? 1.f : expf(m_old - m_new);
+                alpha[rg] = al;
+                l_run[rg] = l_run[rg] * al + sum;
+                m_run[rg] = m_new;
+            }
+        }
+        __syncthreads();
+        if (!mbar_wait(&bar[1], c & 1, a.status, 21, abort)) { ok = false; break; }
+        if (pv_live) {
+            const float4* V4 = reinterpret_cast<const float4*>(Vs);
+#pragma unroll
+            for (int g = 0; g < 8; g++) {
+                if (g < G) {
+                    const float al = alpha[pv_i * G + g];
+                    acc[g].x *= al; acc[g].y *= al; acc[g].z *= al; acc[g].w *= al;
+                }
+            }
+            for (int jj = pv_part; jj < cn; jj += PP) {
+                const float4 v4 = V4[jj * 16 + d4];
+#pragma unroll
+                for (int g = 0; g < 8; g++) {
+                    if (g < G) {
+                        const float pj = sc[(size_t)(pv_i * G + g) * SC + jj];
+                        acc[g].x += pj * v4.x; acc[g].y += pj * v4.y; acc[g].z += pj * v4.z; acc[g].w += pj * v4.w;
+                    }
+                }
+            }
+        }
+    }
+    if (!ok) return;
+    // Reduce the PP partial sums through shared memory (the K/V chunk area is free now), then
+    // normalise and write: output task = (row i, head g, d4).
+    __syncthreads();
+    float4* part4 = reinterpret_cast<float4*>(Ks);  // [PP][nrows][G][16]
+    if (pv_live) {
+#pragma unroll
+        for (int g = 0; g < 8; g++)
+            if (g < G) part4[((pv_part * nrows + pv_i) * G + g) * 16 + d4] = acc[g];
+    }
+    __syncthreads();
+    for (int t = tid; t < nrg * 16; t += AD_THREADS) {
+        const int dd = t & 15, rg = t >> 4, i = rg / G, g = rg % G;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < PP; q++) {
+            const float4 v = part4[((q * nrows + i) * G + g) * 16 + dd];
+            o.x += v.x; o.y += v.y; o.z += v.z; o.w += v.w;
+        }
+        const float inv = 1.0f / l_run[rg];
+        const float o0 = o.x * inv, o1 = o.y * inv, o2 = o.z * inv, o3 = o.w * inv;
+        const size_t row = (size_t)(r * nrows + i);
+        const int head = h * G + g;
+        if (a.out) *reinterpret_cast<float4*>(a.out + row * a.ldo + head * 64 + dd * 4) = make_float4(o0, o1, o2, o3);
+        if (a.out_hi) {
+            uint16_t h0, l0, h1, l1, h2, l2, h3, l3;
+            split_bf16(o0, h0, l0);
+            split_bf16(o1, h1, l1);
+            split_bf16(o2, h2, l2);
+            split_bf16(o3, h3, l3);
+            const size_t so = row * a.ld_split + head * 64 + dd * 4;
+            *reinterpret_cast<uint2*>(a.out_hi + so) = make_uint2(h0 | ((uint32_t)h1 << 16), h2 | ((uint32_t)h3 << 16));
+            *reinterpret_cast<uint2*>(a.out_lo + so) = make_uint2(l0 | ((uint32_t)l1 << 16), l2 | ((uint32_t)l3 << 16));
+        }
+    }
+}
+
+bool attention_decode_supported(int rows_per_req, int hq, int hkv) {
+    return rows_per_req >= 1 && rows_per_req <= ATTN_DECODE_MAX_ROWS && hkv > 0 && hq % hkv == 0 && hq / hkv <= 8;
+}
+
+void launch_attention_decode(const AttnDecodeArgs& a, cudaStream_t s) {
+    const int G = a.hq / a.hkv, nrg = a.rows_per_req * G;
+    const int nk_max = a.window > 0 ? min(a.window + a.rows_per_req - 1, a.cap) : a.max_keys;
+    constexpr size_t kBudget = 223 * 1024;  // dynamic shared memory: 227 KB per block less the static part
+    int SC = (nk_max + 15) & ~15;
+    if (a.chunk_keys > 0 && a.chunk_keys < SC) SC = (a.chunk_keys + 15) & ~15;
+    if (SC < 8 * G) SC = 8 * G;  // the final reduction reuses the K/V area: 16 x G x 256 bytes
+    while (SC > 16 && ad_dyn_bytes(SC, a.rows_per_req, nrg) > kBudget) SC -= 16;
+    static bool configured = false;  // set once, before any graph capture (the first call is eager)
+    if (!configured) {
+        cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBudget);
+        configured = true;
+    }
+    launch_k(attention_decode_kernel, dim3(a.requests, a.hkv), AD_THREADS, ad_dyn_bytes(SC, a.rows_per_req, nrg), s, a, SC);
+}
+
+// ------------------------------------------------------------------------------------------------
 // DiT attention: one warp per (sequence, head) computes every row of the sequence (seq <= 8);
 // lane l owns dims 2l, 2l+1 = one interleaved RoPE pair. All q/k/v loads of the warp are issued
 // before any use, and each position's rotation is computed once.
@@ -478,6 +772,30 @@ mt_status mt_attention(mt_ctx* ctx, void* stream, const float* q, int ldq, int m
     a.max_keys = max_keys;
     launch_attention(a, as_stream(stream));
     return check_launch(ctx, "mt_attention");
+}
+
+mt_status mt_rope_attention(mt_ctx* ctx, void* stream, const float* qkv, int ldq, int m, int hq, int hkv, int pos0,
+                            int window, float* k_cache, float* v_cache, int capacity, const float* inv_freq,
+                            float* out, int ldo, int chunk_keys) {
+    MT_REQUIRE(ctx, ctx && qkv && k_cache && v_cache && inv_freq && out, MT_ERR_ARG, "mt_rope_attention: null argument");
+    MT_REQUIRE(ctx, m >= 0 && m <= ATTN_DECODE_MAX_ROWS && attention_decode_supported(m > 0 ? m : 1, hq, hkv) &&
+                        ldq >= (hq + 2 * hkv) * 64 && ldo >= hq * 64 && ldo % 4 == 0 && window >= 0 && chunk_keys >= 0,
+               MT_ERR_SHAPE, "mt_rope_attention: m %d (<= %d) hq %d hkv %d ldq %d ldo %d window %d", m,
+               ATTN_DECODE_MAX_ROWS, hq, hkv, ldq, ldo, window);
+    MT_REQUIRE(ctx, pos0 >= 0 && capacity > 0 &&
+                        (pos0 + m <= capacity || (window > 0 && window + m - 1 <= capacity)),
+               MT_ERR_CAPACITY, "mt_rope_attention: positions %d..%d do not fit capacity %d (window %d)", pos0, pos0 + m,
+               capacity, window);
+    MT_REQUIRE(ctx, aligned16(k_cache) && aligned16(v_cache) && aligned16(out), MT_ERR_ARG,
+               "mt_rope_attention: caches and output need 16-byte alignment");
+    if (m == 0) return MT_OK;
+    AttnDecodeArgs a{};
+    a.qkv = qkv; a.ldq = ldq; a.requests = 1; a.rows_per_req = m; a.hq = hq; a.hkv = hkv; a.pos0 = pos0;
+    a.window = window; a.kc = k_cache; a.vc = v_cache; a.req_stride = 0; a.cap = capacity; a.inv_freq = inv_freq;
+    a.out = out; a.ldo = ldo; a.max_keys = window > 0 ? window + m - 1 : pos0 + m; a.chunk_keys = chunk_keys;
+    a.status = ctx->d_status;
+    launch_attention_decode(a, as_stream(stream));
+    return check_launch(ctx, "mt_rope_attention");
 }
 
 mt_status mt_dit_attention(mt_ctx* ctx, void* stream, const float* qkv, int ld, int batch, int seq,

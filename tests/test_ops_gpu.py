@@ -197,6 +197,52 @@ def test_attention_sliding_window(ctx, oracle):
     attention_case(ctx, oracle, 300, 4, 65)
 
 
+@pytest.mark.parametrize("t0,m,window,cap,chunk", [
+    (37, 1, 0, 512, 0), (2, 3, 0, 512, 0), (130, 4, 0, 512, 48), (46, 4, 0, 512, 48), (200, 1, 0, 512, 16),
+    (383, 1, 0, 512, 0),
+    (300, 4, 65, 128, 0), (300, 4, 65, 128, 16), (61, 4, 65, 128, 0),
+])
+def test_rope_attention_fused(ctx, mt, oracle, t0, m, window, cap, chunk):
+    """mt_rope_attention (RoPE, KV append and attention in one kernel) against the oracle's
+    rope_cache + attention; the device cache is a ring when window > 0 and positions pass cap,
+    chunk > 0 forces the online softmax over several staged key chunks."""
+    hq, hkv = 14, 2
+    ld = (hq + 2 * hkv) * 64
+    rng = LCG(oracle, t0 * 17 + m * 5 + window + chunk)
+    total = t0 + m
+    qkv = rng.floats((total + 8) * ld)
+    inv = (1.0 / np.power(np.float32(1e6), np.arange(32, dtype=np.float32) * 2 / 64)).astype(np.float32)
+    cap_o = total + 8
+    kc_o, vc_o = np.zeros(hkv * cap_o * 64, np.float32), np.zeros(hkv * cap_o * 64, np.float32)
+    q_or = qkv.copy()
+    if t0 > 0:
+        oracle.rope_cache(q_or, ld, t0, hq, hkv, 0, kc_o, vc_o, cap_o, inv)
+    # Device cache after the first t0 positions (a ring keeps the most recent cap of them).
+    kc_d, vc_d = np.zeros(hkv * cap * 64, np.float32), np.zeros(hkv * cap * 64, np.float32)
+    for p in range(t0):
+        for h in range(hkv):
+            dst, src = (h * cap + p % cap) * 64, (h * cap_o + p) * 64
+            kc_d[dst:dst + 64] = kc_o[src:src + 64]
+            vc_d[dst:dst + 64] = vc_o[src:src + 64]
+    want = np.zeros(m * hq * 64, np.float32)
+    oracle.rope_cache(q_or[t0 * ld:], ld, m, hq, hkv, t0, kc_o, vc_o, cap_o, inv)
+    oracle.attention(q_or[t0 * ld:], ld, m, hq, hkv, t0, window, kc_o, vc_o, cap_o, want, hq * 64)
+    kcd, vcd, outd = dev(kc_d), dev(vc_d), dev(np.zeros(m * hq * 64, np.float32))
+    qkvd = dev(qkv)
+    ctx.call("rope_attention", qkvd[t0 * ld:], ld, m, hq, hkv, t0, window, kcd, vcd, cap, dev(inv), outd, hq * 64, chunk)
+    ctx.check()
+    what = f"rope_attention t0 {t0} m {m} window {window} cap {cap} chunk {chunk}"
+    assert_close(host(outd).reshape(m, -1), want.reshape(m, -1), atol=2e-5, what=what)
+    kd, vd = host(kcd), host(vcd)
+    for p in range(t0, total):
+        for h in range(hkv):
+            got_k = kd[(h * cap + p % cap) * 64:][:64]
+            got_v = vd[(h * cap + p % cap) * 64:][:64]
+            assert_close(got_k, kc_o[(h * cap_o + p) * 64:][:64], atol=2e-6, what=what + f" k pos {p}")
+            np.testing.assert_array_equal(got_v, vc_o[(h * cap_o + p) * 64:][:64])
+    np.testing.assert_array_equal(host(qkvd), qkv)  # qkv is not modified
+
+
 def test_dit_attention(ctx, oracle):
     for B, S, H in ((2, 3, 16), (1, 2, 16), (3, 8, 4)):
         D = H * 64
