@@ -109,7 +109,10 @@ struct mt_engine {
     float* pcm = nullptr;
     int max_chunk = 0;
     int* state_dev = nullptr;
-    int* state_host = nullptr;  // pinned
+    int* state_host = nullptr;  // pinned step state being filled: one of state_slots
+    int* state_slots[2] = {};   // pinned; step n fills slot n & 1 while step n - 1 may still run
+    cudaEvent_t state_ev[2] = {};  // recorded after the step that read the slot
+    bool state_ev_live[2] = {};
     float* ws_a = nullptr;      // split-K workspace of the main stream (LLM, flow, aggregator)
     float* ws_b = nullptr;      // split-K workspace of the VAE stream
     size_t ws_a_floats = 0, ws_b_floats = 0;
@@ -136,8 +139,8 @@ struct mt_engine {
     cudaEvent_t stage_ev[6] = {};  // A: start, after llm, after flow, after agg; B: decode start, end
     bool stage_valid = false;
     int graph_kernels = 0;      // kernels in the captured step graph
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t graph_exec = nullptr;
+    cudaGraph_t graph[2] = {};  // steady-state step, one per state slot (the upload source differs)
+    cudaGraphExec_t graph_exec[2] = {};
 
     // Host-API staging of mt_engine_generate, allocated once with the engine.
     int32_t* ids_stage = nullptr;  // device copy of the prompt token ids
@@ -683,16 +686,24 @@ mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_o
     ETRY(dalloc(e, &e->ws_a, e->ws_a_floats));
     ETRY(dalloc(e, &e->ws_b, e->ws_b_floats));
     ETRY(dalloc(e, &e->ids_stage, (size_t)R * T));
-    if (cudaMallocHost(&e->state_host, st_size(R) * sizeof(int)) != cudaSuccess ||
+    if (cudaMallocHost(&e->state_slots[0], st_size(R) * sizeof(int)) != cudaSuccess ||
+        cudaMallocHost(&e->state_slots[1], st_size(R) * sizeof(int)) != cudaSuccess ||
         cudaMallocHost(&e->ring_host, (size_t)kPcmRing * R * e->max_chunk * sizeof(float)) != cudaSuccess ||
         cudaMallocHost(&e->stop_host, (size_t)S * R * 2 * sizeof(float)) != cudaSuccess)
         return cleanup(fail(ctx, MT_ERR_NOMEM, "engine: pinned host staging"));
     for (int i = 0; i < kPcmRing; i++)
         if (cudaEventCreateWithFlags(&e->ring_ev[i], cudaEventDisableTiming) != cudaSuccess)
             return cleanup(fail(ctx, MT_ERR_CUDA, "engine: events"));
-    memset(e->state_host, 0, st_size(R) * sizeof(int));
+    memset(e->state_slots[0], 0, st_size(R) * sizeof(int));
+    memset(e->state_slots[1], 0, st_size(R) * sizeof(int));
+    e->state_host = e->state_slots[0];
+    for (int i = 0; i < 2; i++)
+        if (cudaEventCreateWithFlags(&e->state_ev[i], cudaEventDisableTiming) != cudaSuccess)
+            return cleanup(fail(ctx, MT_ERR_CUDA, "engine: events"));
     for (int i = 0; i < 6; i++)
         if (cudaEventCreate(&e->stage_ev[i]) != cudaSuccess) return cleanup(fail(ctx, MT_ERR_CUDA, "engine: events"));
+    // One priority for every stream: a lower-priority VAE stream was measured to slow the VAE
+    // decode (1.8 -> 2.5 ms) without shortening the LLM stage it overlaps.
     if (cudaStreamCreateWithFlags(&e->sa, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&e->sb, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
@@ -712,8 +723,12 @@ mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_o
 
 void mt_engine_destroy(mt_engine* e) {
     if (!e) return;
-    if (e->graph_exec) cudaGraphExecDestroy(e->graph_exec);
-    if (e->graph) cudaGraphDestroy(e->graph);
+    for (int i = 0; i < 2; i++) {
+        if (e->graph_exec[i]) cudaGraphExecDestroy(e->graph_exec[i]);
+        if (e->graph[i]) cudaGraphDestroy(e->graph[i]);
+        if (e->state_ev[i]) cudaEventDestroy(e->state_ev[i]);
+        if (e->state_slots[i]) cudaFreeHost(e->state_slots[i]);
+    }
     if (e->sa) cudaStreamDestroy(e->sa);
     if (e->sb) cudaStreamDestroy(e->sb);
     for (int i = 0; i < kMaxGroups; i++) {
@@ -726,7 +741,6 @@ void mt_engine_destroy(mt_engine* e) {
     for (int i = 0; i < 6; i++)
         if (e->stage_ev[i]) cudaEventDestroy(e->stage_ev[i]);
     if (e->ev_out) cudaEventDestroy(e->ev_out);
-    if (e->state_host) cudaFreeHost(e->state_host);
     if (e->ring_host) cudaFreeHost(e->ring_host);
     if (e->stop_host) cudaFreeHost(e->stop_host);
     for (int i = 0; i < kPcmRing; i++)
@@ -756,11 +770,13 @@ mt_status mt_engine_begin(mt_engine* e, void* stream, int requests, int prompt_r
     e->n = 0;
     e->latents_fed = e->decoded = e->emitted = 0;
     e->prefilled = false;
-    if (e->plan_R != requests && e->graph_exec) {
-        cudaGraphExecDestroy(e->graph_exec);
-        cudaGraphDestroy(e->graph);
-        e->graph_exec = nullptr;
-        e->graph = nullptr;
+    if (e->plan_R != requests) {
+        for (int i = 0; i < 2; i++) {
+            if (e->graph_exec[i]) cudaGraphExecDestroy(e->graph_exec[i]);
+            if (e->graph[i]) cudaGraphDestroy(e->graph[i]);
+            e->graph_exec[i] = nullptr;
+            e->graph[i] = nullptr;
+        }
     }
     TRY(build_plans(e));
     const int H = c.llm.hidden, L = c.latent_dim, S = e->opt.max_steps;
@@ -802,9 +818,14 @@ mt_status mt_engine_step(mt_engine* e, void* stream, int* pcm_count) {
     cudaStream_t caller = as_stream(stream);
     cudaStream_t s = e->sa;
     const int R = e->R, n = e->n;
+    // Step n fills state slot n & 1; the step that last read that slot (n - 2) must be done with it.
+    const int slot = n & 1;
+    if (e->state_ev_live[slot]) {
+        cudaError_t err = cudaEventSynchronize(e->state_ev[slot]);
+        if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "mt_engine_step: %s", cudaGetErrorString(err));
+    }
+    e->state_host = e->state_slots[slot];
     int* st = e->state_host;
-    // The previous step's state upload may still be pending on the device: wait before rewriting.
-    cudaStreamSynchronize(s);
     st[ST_N] = n;
     for (int r = 0; r < R; r++) st[st_llm_pos(R) + r] = e->T + n - 1;
     // Deferred decode (VAEDecoder.deferredDecode, :73-76): latent n-2 once latent n-1 exists.
@@ -819,19 +840,19 @@ mt_status mt_engine_step(mt_engine* e, void* stream, int* pcm_count) {
     cudaStreamWaitEvent(s, e->ev_in, 0);
     e->stage_valid = false;
     if (steady && e->opt.use_graphs && !e->time_stages) {
-        if (!e->graph_exec) {
+        if (!e->graph_exec[slot]) {
             cudaError_t err = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
             if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph capture: %s", cudaGetErrorString(err));
             upload_state(e, s);
             g_kernels = 0;
             enqueue_step(e, s, true, true, false);
             e->graph_kernels = g_kernels;
-            err = cudaStreamEndCapture(s, &e->graph);
+            err = cudaStreamEndCapture(s, &e->graph[slot]);
             if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph capture: %s", cudaGetErrorString(err));
-            err = cudaGraphInstantiate(&e->graph_exec, e->graph, 0);
+            err = cudaGraphInstantiate(&e->graph_exec[slot], e->graph[slot], 0);
             if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph instantiate: %s", cudaGetErrorString(err));
         }
-        cudaGraphLaunch(e->graph_exec, s);
+        cudaGraphLaunch(e->graph_exec[slot], s);
         e->step_kernels = e->graph_kernels;
     } else {
         upload_state(e, s);
@@ -843,6 +864,8 @@ mt_status mt_engine_step(mt_engine* e, void* stream, int* pcm_count) {
     }
     cudaEventRecord(e->ev_out, s);
     cudaStreamWaitEvent(caller, e->ev_out, 0);
+    cudaEventRecord(e->state_ev[slot], s);
+    e->state_ev_live[slot] = true;
     e->latents_fed++;
     e->n++;
     if (pcm_count) *pcm_count = count;
@@ -856,6 +879,9 @@ mt_status mt_engine_flush(mt_engine* e, void* stream, int* pcm_count) {
     if (pcm_count) *pcm_count = 0;
     if (e->decoded >= e->latents_fed) return MT_OK;
     cudaStreamSynchronize(s);
+    for (int i = 0; i < 2; i++)
+        if (e->state_ev_live[i]) cudaEventSynchronize(e->state_ev[i]);
+    e->state_host = e->state_slots[0];
     const int d = e->decoded;
     const int count = plan_decode(e, d, d + 1 < e->latents_fed);
     upload_state(e, s);
