@@ -117,22 +117,30 @@ def dist_setup(args):
     return rank, world, local
 
 
-def dist_max(value: float, world: int) -> float:
+def dist_max(value: float, world: int, device: str = "cuda") -> float:
+    """Maximum of `value` over the ranks (the timing rule: a multi-GPU time is the slowest rank's)."""
     if world == 1:
         return value
     import torch
     import torch.distributed as dist
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
 
-def barrier(world: int):
+def barrier(world: int, device: str = "cuda"):
     import torch
-    torch.cuda.synchronize()
+    if device == "cuda":
+        torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
+
+
+def rank_requests(rank: int, per_rank: int):
+    """Requests of one replica: rank r serves global requests [r * per_rank, (r + 1) * per_rank), so
+    every rank draws different prompts and noise (seeds follow the global request index)."""
+    return rank * per_rank, per_rank
 
 
 def request_inputs(mt, cfg, requests, prompt, steps, first_request):
@@ -345,7 +353,8 @@ def main():
     assert T + total_steps <= cfg.llm_capacity, f"prompt + steps must fit the {cfg.llm_capacity}-position cache"
     eng = mt.Engine(ctx, model, R, T, max(total_steps, args.e2e_steps), use_graphs=not args.no_graphs,
                     groups=args.groups)
-    ids, noise = request_inputs(mt, cfg, R, T, total_steps, rank * R)
+    first, _ = rank_requests(rank, R)
+    ids, noise = request_inputs(mt, cfg, R, T, total_steps, first)
     ids_d, noise_d = torch.from_numpy(ids).cuda(), torch.from_numpy(noise).cuda()
     stream = torch.cuda.current_stream()
 

@@ -162,6 +162,11 @@ const char* mt_version(void);
  * Returns MT_ERR_TIMEOUT if a kernel gave up a wait, MT_ERR_CUDA on a CUDA error.
  * Replaces the command-buffer error check of StepRecorder.finish (Engine.swift:70-85). */
 mt_status mt_ctx_check(mt_ctx* ctx, void* stream);
+/* Tensor-core GEMM tiling for plans made on ctx from now on: -1 automatic (default), 0 single-CTA
+ * tiles of 128 weight rows, 1 CTA pairs (clusters of two SMs sharing 256-weight-row tiles through
+ * tcgen05 cta_group::2). Results agree to rounding; the choice only changes speed. No counterpart
+ * in the reference (its GEMM has one tiling). */
+mt_status mt_ctx_set_gemm_pairs(mt_ctx* ctx, int mode);
 
 /* Which kernel family mt_linear routes a shape to: 0 = CUDA-core GEMV (rows in registers),
  * 1 = tcgen05 tensor-core GEMM. Mirrors Kernels.usesGemm (Kernels.swift:81-86). */

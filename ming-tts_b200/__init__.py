@@ -107,6 +107,7 @@ PROTOTYPES = {
     "mt_version": (c_char_p, []),
     "mt_ctx_check": (c_int, [_P, _P]),
     "mt_linear_route": (c_int, [c_int, c_int, c_int]),
+    "mt_ctx_set_gemm_pairs": (c_int, [_P, c_int]),
     "mt_linear": (c_int, [_P, _P, _P, c_int, c_int, _P, _P, _P, c_int, c_int, _P, c_int, c_uint32]),
     "mt_linear_split": (c_int, [_P, _P, _P, _P, c_int, c_int, _P, _P, _P, c_int, c_int, _P, c_int, _P, _P, c_int,
                                 c_uint32]),
@@ -224,6 +225,10 @@ class Context:
         conv = [ptr(a) if (hasattr(a, "data_ptr") or hasattr(a, "ctypes")) else a for a in args]
         st = fn(self._ctx, stream if stream is not None else current_stream(), *conv)
         self._check(st, "mt_" + name)
+
+    def set_gemm_pairs(self, mode: int):
+        """Tensor-core GEMM tiling for later plans: -1 automatic, 0 single-CTA tiles, 1 CTA pairs."""
+        self._check(lib().mt_ctx_set_gemm_pairs(self._ctx, mode), "mt_ctx_set_gemm_pairs")
 
     # Thin wrappers with the reference's argument order (Kernels.swift:132-281).
     def linear(self, x, ldx, m, w, w2, bias, n, k, y, ldy, flags):

@@ -18,6 +18,7 @@ struct mt_ctx {
     unsigned int* d_status = nullptr;  // [0] = error code, [1] = site id, [2] = detail
     void* scratch = nullptr;           // grows on demand, see mt_scratch()
     size_t scratch_bytes = 0;
+    int gemm_pairs = -1;               // tensor-core GEMM CTA pairs: -1 automatic, 0 never, 1 where valid
     std::string err;
 };
 
@@ -120,6 +121,27 @@ inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// launch_k for kernels that run as clusters of two CTAs along x (grid.x even).
+template <typename... KArgs, typename... Args>
+inline void launch_k_pair(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
     cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 

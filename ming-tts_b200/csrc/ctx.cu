@@ -100,6 +100,13 @@ mt_status mt_ctx_check(mt_ctx* ctx, void* stream) {
     return MT_OK;
 }
 
+mt_status mt_ctx_set_gemm_pairs(mt_ctx* ctx, int mode) {
+    if (!ctx) return MT_ERR_ARG;
+    MT_REQUIRE(ctx, mode >= -1 && mode <= 1, MT_ERR_ARG, "mt_ctx_set_gemm_pairs: mode %d (-1, 0 or 1)", mode);
+    ctx->gemm_pairs = mode;
+    return MT_OK;
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------------------------------------------

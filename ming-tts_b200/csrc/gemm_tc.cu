@@ -433,6 +433,220 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
+// ------------------------------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs computes a 256-weight-row tile with one
+// tcgen05.mma.cta_group::2 (M = 256) per K step. The A operand (weights) is split by rows: CTA
+// rank r holds weight rows n0 + 128 r; the B operand is split by columns: rank 0 holds the x_hi
+// rows, rank 1 the x_lo rows of the same activation rows, so each CTA's shared memory carries one
+// of the two activation planes and the per-CTA bytes per K block drop from W + 2X to W + X. Each
+// CTA's TMEM holds its 128 weight rows x [hi | lo] columns, so the epilogue is the one above.
+// Protocol: both producers' TMA loads complete on the leader's (rank 0) full barrier, whose
+// expected bytes the leader arms for both; the leader's MMA commits arrive on the empty and
+// accumulator-full barriers of both CTAs (commit multicast); both CTAs' epilogue warps arrive on
+// the leader's accumulator-empty barrier. TMA loads never multicast. Every wait is bounded.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Shared::cluster address of `local` (a shared::cta variable) in the CTA of rank `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(const void* local, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
+    return out;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// TMA tile load into this CTA's shared memory, completing on the leader's barrier (cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t leader_bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives once on the barrier at this offset in both CTAs of the pair when the leader's prior MMAs complete.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+__device__ __forceinline__ TileCoord tile_coord_pair(const TcEpi& e, int t, int rank) {
+    const int per_split = e.tiles_m * e.tiles_n;  // tiles_n counts 256-row pair tiles
+    const int z = t / per_split, r = t % per_split;
+    TileCoord c;
+    c.m0 = (r % e.tiles_m) * e.bn;
+    c.n0 = (r / e.tiles_m) * (2 * TC_BM) + rank * TC_BM;
+    const int kb_total = (e.k + TC_BK - 1) / TC_BK;
+    c.kb_begin = z * e.kb_per_split;
+    c.kb_end = min(kb_total, c.kb_begin + e.kb_per_split);
+    return c;
+}
+
+template <bool GATED>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
+                        const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo,
+                        TcEpi e) {
+    extern __shared__ __align__(1024) uint8_t dsmem[];
+    __shared__ uint64_t full_bar[8], empty_bar[8], acc_full[2], acc_empty[2];
+    __shared__ uint32_t tmem_holder;
+    __shared__ int abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+    const int S = e.stages;
+    const int units = e.tiles_m * e.tiles_n * e.split;
+
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
+    const uint32_t w_bytes = TC_BM * 128, x_bytes = (uint32_t)e.bn * 128;
+    const uint32_t stage_bytes = w_bytes * (GATED ? 2 : 1) + x_bytes;  // this CTA's share of a stage
+    const uint32_t acc_cols = (uint32_t)e.bn * (GATED ? 4 : 2);
+    uint32_t ncols = 32;
+    while (ncols < 2 * acc_cols) ncols <<= 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 2 * TC_EPI_WARPS);
+        }
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 2) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_holder)),
+                     "r"(ncols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    cluster_sync_all();  // both CTAs' barriers exist before any remote arrive or load completes on them
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_holder;
+    volatile int* abort = &abort_flag;
+    pdl_launch();
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer (both CTAs)
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+            if (GATED) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w2)) : "memory");
+            const CUtensorMap* tm_x = rank == 0 ? &tm_xhi : &tm_xlo;
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm_x)) : "memory");
+            int pre = 0;
+            for (int t = cluster; t < units && pre < S; t += nclusters) {
+                const TileCoord tc = tile_coord_pair(e, t, rank);
+                for (int kb = tc.kb_begin; kb < tc.kb_end && pre < S; kb++, pre++) {
+                    uint8_t* st = base + (size_t)pre * stage_bytes;
+                    if (rank == 0) mbar_expect_tx(&full_bar[pre], 2 * stage_bytes);
+                    const uint32_t lb = map_to_rank(&full_bar[pre], 0);
+                    tma_load_2d_pair(st, &tm_w, lb, kb * TC_BK, tc.n0);
+                    if (GATED) tma_load_2d_pair(st + w_bytes, &tm_w2, lb, kb * TC_BK, tc.n0);
+                }
+            }
+            pdl_wait();
+            int g = 0;
+            for (int t = cluster; t < units && !*abort; t += nclusters) {
+                const TileCoord tc = tile_coord_pair(e, t, rank);
+                for (int kb = tc.kb_begin; kb < tc.kb_end; kb++, g++) {
+                    const int s = g % S;
+                    uint8_t* st = base + (size_t)s * stage_bytes;
+                    const int kc = kb * TC_BK;
+                    const uint32_t lb = map_to_rank(&full_bar[s], 0);
+                    if (g >= pre) {
+                        if (!mbar_wait(&empty_bar[s], ((g / S) & 1) ^ 1, e.status, 11, abort)) break;
+                        if (rank == 0) mbar_expect_tx(&full_bar[s], 2 * stage_bytes);
+                        tma_load_2d_pair(st, &tm_w, lb, kc, tc.n0);
+                        if (GATED) tma_load_2d_pair(st + w_bytes, &tm_w2, lb, kc, tc.n0);
+                    }
+                    tma_load_2d_pair(st + w_bytes * (GATED ? 2 : 1), tm_x, lb, kc, tc.m0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {  // MMA issuer: the leader only
+            const uint32_t idesc = idesc_bf16(2 * TC_BM, 2 * e.bn);
+            int g = 0, tl = 0;
+            for (int t = cluster; t < units && !*abort; t += nclusters, tl++) {
+                const TileCoord tc = tile_coord_pair(e, t, 0);
+                const int b = tl & 1;
+                if (!mbar_wait(&acc_empty[b], ((tl >> 1) & 1) ^ 1, e.status, 12, abort)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t acc = tmem + b * acc_cols;
+                bool ok = true;
+                for (int kb = tc.kb_begin, i = 0; kb < tc.kb_end; kb++, i++, g++) {
+                    const int s = g % S;
+                    if (!mbar_wait(&full_bar[s], (g / S) & 1, e.status, 13, abort)) { ok = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t wa = smem_u32(base + (size_t)s * stage_bytes);
+                    const uint32_t xa = wa + w_bytes * (GATED ? 2 : 1);
+#pragma unroll
+                    for (int kk = 0; kk < TC_BK / 16; kk++) {
+                        const uint32_t off = kk * 32;
+                        const uint64_t bx = sw128_desc(xa + off);
+                        const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
+                        mma_bf16_pair(acc, sw128_desc(wa + off), bx, idesc, accum);
+                        if (GATED) mma_bf16_pair(acc + 2 * e.bn, sw128_desc(wa + w_bytes + off), bx, idesc, accum);
+                    }
+                    mma_commit_pair(&empty_bar[s]);
+                }
+                if (!ok) break;
+                mma_commit_pair(&acc_full[b]);
+            }
+        }
+    } else {  // epilogue warps 2..9 of both CTAs, each on its own TMEM rows
+        const int quad = warp & 3, part = (warp - 2) >> 2;
+        asm volatile("" ::"r"(e.kind), "r"(e.flags), "r"(e.m), "r"(e.n), "r"(e.bn), "l"(e.y), "l"(e.y_hi),
+                     "l"(e.bias));
+        pdl_wait();
+        int tl = 0;
+        for (int t = cluster; t < units; t += nclusters, tl++) {
+            const int b = tl & 1;
+            if (!mbar_wait(&acc_full[b], (tl >> 1) & 1, e.status, 14, abort)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const TileCoord tc = tile_coord_pair(e, t, rank);
+            epilogue_dispatch<GATED>(e, tc, tmem + b * acc_cols, quad, part, lane, t < e.tiles_m * e.tiles_n);
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(map_to_rank(&acc_empty[b], 0));
+        }
+    }
+    __syncwarp();
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    cluster_sync_all();  // neither CTA leaves while the pair's MMAs or remote arrives may touch it
+    if (warp == 2) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+    }
+}
+
 // Finishes a split-K GEMM whose epilogue is nonlinear: y = epi(ws (+ bias)) from the fp32 sums.
 __global__ void split_epilogue_kernel(TcEpi e) {
     pdl_wait();
@@ -526,7 +740,6 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     e = TcEpi{};
     e.m = a.m; e.n = a.n; e.k = a.k;
     const int sms = ctx->sm_count > 0 ? ctx->sm_count : 148;
-    const int tiles_n = (a.n + TC_BM - 1) / TC_BM;
     const bool linear = !(a.flags & (MT_LINEAR_GELU | MT_LINEAR_SILU | MT_LINEAR_SILU_GATE)) && a.y && !a.y_hi;
     // Split-K by default only where partial sums can be reduced into y without zeroing it first
     // (ACCUM: y holds the residual). Tile rows measured on the engine's shapes: narrow tiles for few
@@ -540,7 +753,12 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     if (gated && e.bn > 64 && a.bn_override <= 0) e.bn = 64;  // two gated accumulators x 2 buffers fit 512 columns
     MT_REQUIRE(ctx, e.bn % 16 == 0 && e.bn <= (gated ? 64 : 128), MT_ERR_SHAPE, "gemm_tc: tile rows %d (16..%d)", e.bn,
                gated ? 64 : 128);
-    const uint32_t stage_bytes = TC_BM * 128 * (gated ? 2 : 1) + 2u * e.bn * 128;
+    // CTA pairs (256 weight rows per tile, one activation plane per CTA): on request only for now.
+    const bool pair = ctx->gemm_pairs == 1;
+    const int tile_rows = pair ? 2 * TC_BM : TC_BM;
+    const int tiles_n = (a.n + tile_rows - 1) / tile_rows;
+    const int slots = pair ? sms / 2 : sms;  // concurrent work units
+    const uint32_t stage_bytes = TC_BM * 128 * (gated ? 2 : 1) + (pair ? 1u : 2u) * e.bn * 128;
     const int tiles = tiles_n * ((a.m + e.bn - 1) / e.bn);
     e.stages = (int)((200 * 1024) / stage_bytes);
     if (e.stages > 8) e.stages = 8;
@@ -549,7 +767,7 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     const int kb_total = (a.k + TC_BK - 1) / TC_BK;
     int split = a.split_k;
     if (split <= 0) {  // automatic: one wave (work units <= SMs), at least two k blocks each, at most 8 splits
-        split = splittable ? sms / tiles : 1;
+        split = splittable ? slots / tiles : 1;
         if (split > 8) split = 8;
         if (split > kb_total / 2) split = kb_total / 2;
     }
@@ -574,13 +792,16 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     ok = ok && make_map(&plan->tl, a.x_lo, a.m, a.k, a.ld_split, e.bn);
     MT_REQUIRE(ctx, ok, MT_ERR_CUDA, "gemm_tc: cuTensorMapEncodeTiled failed (m %d n %d k %d)", a.m, a.n, a.k);
     plan->gated = gated;
+    plan->pair = pair;
     plan->smem = (size_t)e.stages * stage_bytes + 1024;
     const int work = e.tiles_n * e.tiles_m * split;
-    plan->grid = dim3(work < sms ? work : sms, 1, 1);
+    plan->grid = dim3((pair ? 2 : 1) * (work < slots ? work : slots), 1, 1);
     static bool attr_set = false;
     if (!attr_set) {
         cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
         cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+        cudaFuncSetAttribute(gemm_tc_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+        cudaFuncSetAttribute(gemm_tc_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
         attr_set = true;
     }
     return MT_OK;
@@ -617,6 +838,7 @@ mt_status make_gemm_plan_bare(int sm_count, const LinearArgs& a, GemmPlan* plan)
     ok = ok && make_map(&plan->tl, a.x_lo, a.m, a.k, a.ld_split, e.bn);
     if (!ok) return MT_ERR_CUDA;
     plan->gated = gated;
+    plan->pair = false;
     plan->smem = (size_t)e.stages * stage_bytes + 1024;
     const int work = e.tiles_n * e.tiles_m;
     plan->grid = dim3(work < sms ? work : sms, 1, 1);
@@ -634,10 +856,16 @@ void run_gemm_plan(const GemmPlan& p, cudaStream_t s) {
     if (e.mode == 1 && !(e.flags & MT_LINEAR_ACCUM))
         cudaMemset2DAsync(e.y, (size_t)e.ldy * sizeof(float), 0, (size_t)e.n * sizeof(float), e.m, s);
     if (e.mode == 2) cudaMemsetAsync(e.ws, 0, (size_t)e.m * e.ldws * sizeof(float), s);
-    if (p.gated)
+    if (p.pair) {
+        if (p.gated)
+            launch_k_pair(gemm_tc_pair_kernel<true>, p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
+        else
+            launch_k_pair(gemm_tc_pair_kernel<false>, p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
+    } else if (p.gated) {
         launch_k(gemm_tc_kernel<true>, p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
-    else
+    } else {
         launch_k(gemm_tc_kernel<false>, p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
+    }
     if (e.mode == 2) {
         const long long total = (long long)e.m * e.n;
         long long blocks = (total + 255) / 256;

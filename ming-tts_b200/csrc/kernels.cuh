@@ -145,6 +145,7 @@ struct GemmPlan {
     dim3 grid;
     size_t smem;
     bool gated;
+    bool pair;  // CTA-pair kernel (cluster of two, tcgen05 cta_group::2)
 };
 mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan);
 mt_status make_gemm_plan_bare(int sm_count, const LinearArgs& a, GemmPlan* plan);

@@ -99,6 +99,8 @@ def test_tensor_core_shapes(ctx, mt, oracle, m, n, k, flags, bias):
     (37, 200, 136, 4, True, "both"),             # runtime-flag path: GELU, fp32 and hi/lo out
     (70, 330, 256, 2, True, "both"),             # runtime-flag path: residual add with hi/lo out
     (21, 300, 896, 8, True, "f32"),              # runtime-flag path: gate with fp32 out
+    (1024, 4864, 896, 8, False, "split"),        # SILU gate, several tiles per CTA (prefill gate/up)
+    (2048, 1152, 896, 0, True, "f32"),           # several tiles per CTA (prefill qkv)
 ])
 def test_linear_split_epilogues(ctx, mt, oracle, m, n, k, flags, bias, outs):
     """mt_linear_split (bf16 hi/lo activations in, fp32 and/or hi/lo out) against the oracle, one
@@ -133,6 +135,21 @@ def test_linear_split_epilogues(ctx, mt, oracle, m, n, k, flags, bias, outs):
         got = oracle.bf16_to_f32(host(yh).view(np.uint16)) + oracle.bf16_to_f32(host(yl).view(np.uint16))
         assert_close(got.reshape(m, n), want.reshape(m, n), what=what + " hi+lo", atol=tol["atol"], rtol=2e-4)
         assert rel_err(got, want) <= 1e-3, what
+
+
+@pytest.mark.parametrize("m,n,k,flags,bias,outs", [
+    (384, 3072, 1024, 0, True, "f32"), (384, 4096, 1024, 4, True, "split"), (64, 4864, 896, 8, False, "split"),
+    (384, 1024, 4096, 2, True, "f32"), (37, 200, 136, 16, True, "f32"), (70, 330, 256, 2, True, "both"),
+    (1024, 4864, 896, 8, False, "split"), (2048, 1152, 896, 0, True, "f32"),
+])
+def test_linear_split_cta_pairs(ctx, mt, oracle, m, n, k, flags, bias, outs):
+    """The CTA-pair tensor-core GEMM (tcgen05 cta_group::2, 256 weight rows per pair) against the
+    oracle, through the same entry point with pairs forced on."""
+    ctx.set_gemm_pairs(1)
+    try:
+        test_linear_split_epilogues(ctx, mt, oracle, m, n, k, flags, bias, outs)
+    finally:
+        ctx.set_gemm_pairs(-1)
 
 
 def test_gelu_silu_large_inputs(ctx, mt, oracle):
