@@ -249,6 +249,19 @@ def host_model(mt, oracle, cfg, seed):
     return arena, tensors, w, keep
 
 
+def use_all_host_threads() -> int:
+    """The CPU legs use every host core. torchrun sets OMP_NUM_THREADS=1 for its workers, and the
+    OpenMP runtime may already be initialised by the time the oracle runs, so set both the
+    environment and the running runtime's thread count."""
+    n = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    try:
+        ctypes.CDLL("libgomp.so.1").omp_set_num_threads(n)
+    except OSError:
+        pass
+    return n
+
+
 def cpu_oracle_rate(mt, cfg, prompt, warm_steps, timed_steps):
     """Times the oracle's generation loop (one request) per step; returns (audio-s/s, seconds, threads)."""
     import numpy as np
@@ -266,9 +279,9 @@ def cpu_oracle_rate(mt, cfg, prompt, warm_steps, timed_steps):
     n0 = np.ascontiguousarray(noise[0])
     io.noise = n0.ctypes.data
     io.step_seconds = stamps.ctypes.data
+    threads = use_all_host_threads()
     oracle.lib().or_generate(ctypes.addressof(cfg), ctypes.addressof(w), ctypes.byref(io))
     secs = stamps[steps - 1] - stamps[warm_steps - 1]
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     return timed_steps * AUDIO_PER_STEP / secs, secs, threads
 
 
@@ -276,14 +289,19 @@ def cpu_oracle_rate(mt, cfg, prompt, warm_steps, timed_steps):
 def run_reference(args, rank, world):
     if rank != 0:
         return
+    use_all_host_threads()
     mt = load_package()
     cfg = mt.default_config()
-    warm = 1
-    rate, secs, threads = cpu_oracle_rate(mt, cfg, args.cpu_prompt, warm, args.cpu_steps)
-    sample = (f"1 request, {args.cpu_prompt}-token prompt, {warm} untimed + {args.cpu_steps} timed steps of the full "
+    # One step of this arm = one generation step of one request on the host cores (a bounded sample
+    # of the per-GPU workload: ~0.3 s on 16 cores); W untimed and K timed steps, K capped so the
+    # positions fit the 512-entry cache.
+    warm = max(1, args.warmup)
+    timed = max(1, min(args.steps, cfg.llm_capacity - args.cpu_prompt - warm - 1))
+    rate, secs, threads = cpu_oracle_rate(mt, cfg, args.cpu_prompt, warm, timed)
+    sample = (f"1 request, {args.cpu_prompt}-token prompt, {warm} untimed + {timed} timed steps of the full "
               f"model (CPU oracle: C restatement of the reference kernels, fp64 dot products, OpenMP)")
     line = {"impl": "reference", "metric": METRIC, "value": round(rate, 5), "unit": "audio-s/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs / args.cpu_steps * 1e3, 2),
+            "steps": timed, "warmup": warm, "ms_per_step": round(secs / timed * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: random-init weights seed 1, uniform prompt ids, N(0,1) noise",
             "config": config_block(args),
@@ -327,6 +345,10 @@ def main():
                     help="prefill, warm-up and timed steps only (for a profiler's launch list); prints ms/step")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
+    if args.impl == "reference":
+        # The CPU reference arm needs no process group: rank 0 times the oracle, the others exit.
+        run_reference(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
+        return
     rank, world, local = dist_setup(args)
     if args.gemm:
         mt = load_package()
@@ -336,10 +358,6 @@ def main():
         t = time_gemm(mt, ctx, m, n, k, flags, iters=20, rounds=1)
         print(json.dumps({"gemm": [m, n, k, flags], "us": round(t * 1e6, 2),
                           "tflops": round(2.0 * m * n * k / t / 1e12, 1)}), flush=True)
-        return
-    if args.impl == "reference":
-        run_reference(args, rank, world)
-        barrier(world)
         return
 
     import numpy as np
