@@ -312,6 +312,9 @@ def run_reference(args, rank, world):
 
 
 METRIC = "audio-sec/sec of the Ming-3.0-tts-0.5B step loop (config 5 serving, per-GPU replicas)"
+# DRAM bytes (read + write) of one launch of the roofline GEMM, from the ncu capture summarised in
+# profiles/gemm_tc_flow_ff1_m384_n4096_k1024.md (dram__bytes_read.sum + dram__bytes_write.sum).
+ROOFLINE_TRAFFIC_BYTES = 10_044_160
 
 
 def config_block(args):
@@ -466,7 +469,8 @@ def main():
                              "peak": bf16_peak, "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 4),
                              "peak_kind": f"{peak_kind} bf16 dense (burst)",
                              "note": "algorithmic 2MNK; the fp32-faithful hi+lo split issues 2 bf16 MMAs per product",
-                             "ms_per_launch": round(t_gemm * 1e3, 4), "traffic": None},
+                             "ms_per_launch": round(t_gemm * 1e3, 4), "traffic": ROOFLINE_TRAFFIC_BYTES,
+                             "traffic_unit": "bytes per launch (ncu dram read+write)"},
                 "gemv": {"shape": "config 1: M=2 W[4864x896] bf16, fp32 x/y", "gbs": round(gv_bytes / t_gv / 1e9, 1),
                          "frac": round(gv_bytes / t_gv / 1e9 / hbm_peak, 4), "us": round(t_gv * 1e6, 3),
                          "down_proj_gbs": round(gv_down_bytes / t_gv_down / 1e9, 1),
