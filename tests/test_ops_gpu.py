@@ -163,9 +163,10 @@ def test_silu_gate(ctx, mt, oracle):
     gemv_case(ctx, mt, oracle, 5, 256, 896, mt.SILU_GATE, False)
 
 
-def test_rmsnorm(ctx, mt, oracle):
-    rows, k = 5, 896
-    rng = LCG(oracle, 3)
+@pytest.mark.parametrize("rows,k", [(5, 896), (17, 1024), (3, 36), (9, 2048), (2, 4096)])
+def test_rmsnorm(ctx, mt, oracle, rows, k):
+    # widths up to 1024: warp per row; wider rows: block per row
+    rng = LCG(oracle, 3 + k)
     x = rng.floats(rows * k, 3.0)
     w = oracle.bf16_bits(rng.floats(k))
     want = np.zeros_like(x)
@@ -173,7 +174,7 @@ def test_rmsnorm(ctx, mt, oracle):
     yd = dev(np.zeros_like(x))
     ctx.rmsnorm(dev(x), k, rows, k, dev(w), yd, k, 1e-6)
     ctx.check()
-    assert_close(host(yd), want, atol=1e-5, what="rmsnorm")
+    assert_close(host(yd), want, atol=1e-5, what=f"rmsnorm rows {rows} width {k}")
 
 
 def attention_case(ctx, oracle, t0, m, window):
