@@ -99,6 +99,15 @@ __device__ __forceinline__ TileCoord tile_coord(const TcEpi& e, int t) {
     return c;
 }
 
+// Bias of this thread's output column in the tile at column n0 (0 where nothing is added: no BIAS
+// flag, a column past N, or a split-K partial other than the first). Biases are weights, never
+// written by a kernel, so this may run before the wait on the previous kernel.
+__device__ __forceinline__ float tile_bias(const TcEpi& e, int n0, int quad, int lane, bool first_split) {
+    const int n = n0 + quad * 32 + lane;
+    const bool add = (e.flags & MT_LINEAR_BIAS) && n < e.n && (e.mode != 1 || first_split);
+    return add ? bf16f(e.bias[n]) : 0.f;
+}
+
 // Epilogue of one tile for one warp: 16-column chunks `part`, `part + 2`, ... of TMEM lane quadrant
 // `quad` (weight rows n0 + 32 quad + lane).
 template <bool GATED>
@@ -189,13 +198,11 @@ __device__ __forceinline__ void epilogue_tile(const TcEpi& e, const TileCoord& t
 // flag tests and predicated stores stall the epilogue warps).
 template <int KIND, bool GATED>
 __device__ __forceinline__ void epilogue_fast(const TcEpi& e, const TileCoord& tc, uint32_t acc, int quad, int part,
-                                              int lane, bool first_split) {
+                                              int lane, float bval) {
     const int nq = tc.n0 + quad * 32;
     const int n = nq + lane;
     const bool live_n = n < e.n;
     const bool all_live = nq + 32 <= e.n;  // warp-uniform: every lane's output column exists
-    const bool add_bias = (e.flags & MT_LINEAR_BIAS) && live_n && (KIND != EPI_RED || first_split);
-    const float bval = add_bias ? bf16f(e.bias[n]) : 0.f;
     const uint32_t lane_base = acc + ((uint32_t)(quad * 32) << 16);
     const size_t ldy = (size_t)e.ldy, lds = (size_t)e.ld_ysplit;
     for (int c0 = part * 16; c0 < e.bn; c0 += 32) {
@@ -273,23 +280,26 @@ __device__ __forceinline__ void epilogue_fast(const TcEpi& e, const TileCoord& t
 template <bool GATED>
 __device__ __forceinline__ void epilogue_dispatch(const TcEpi& e, const TileCoord& tc, uint32_t acc, int quad,
                                                   int part, int lane, bool first_split) {
+    const float bval = tile_bias(e, tc.n0, quad, lane, first_split);
     if constexpr (GATED) {
-        if (e.kind == EPI_SPLIT_GATE) epilogue_fast<EPI_SPLIT_GATE, true>(e, tc, acc, quad, part, lane, first_split);
+        if (e.kind == EPI_SPLIT_GATE) epilogue_fast<EPI_SPLIT_GATE, true>(e, tc, acc, quad, part, lane, bval);
         else epilogue_tile<true>(e, tc, acc, quad, part, lane, first_split);
     } else {
         switch (e.kind) {
-            case EPI_F32: epilogue_fast<EPI_F32, false>(e, tc, acc, quad, part, lane, first_split); break;
-            case EPI_F32_ACCUM: epilogue_fast<EPI_F32_ACCUM, false>(e, tc, acc, quad, part, lane, first_split); break;
-            case EPI_SPLIT: epilogue_fast<EPI_SPLIT, false>(e, tc, acc, quad, part, lane, first_split); break;
-            case EPI_SPLIT_GELU: epilogue_fast<EPI_SPLIT_GELU, false>(e, tc, acc, quad, part, lane, first_split); break;
-            case EPI_F32_SILU: epilogue_fast<EPI_F32_SILU, false>(e, tc, acc, quad, part, lane, first_split); break;
-            case EPI_RED: epilogue_fast<EPI_RED, false>(e, tc, acc, quad, part, lane, first_split); break;
+            case EPI_F32: epilogue_fast<EPI_F32, false>(e, tc, acc, quad, part, lane, bval); break;
+            case EPI_F32_ACCUM: epilogue_fast<EPI_F32_ACCUM, false>(e, tc, acc, quad, part, lane, bval); break;
+            case EPI_SPLIT: epilogue_fast<EPI_SPLIT, false>(e, tc, acc, quad, part, lane, bval); break;
+            case EPI_SPLIT_GELU: epilogue_fast<EPI_SPLIT_GELU, false>(e, tc, acc, quad, part, lane, bval); break;
+            case EPI_F32_SILU: epilogue_fast<EPI_F32_SILU, false>(e, tc, acc, quad, part, lane, bval); break;
+            case EPI_RED: epilogue_fast<EPI_RED, false>(e, tc, acc, quad, part, lane, bval); break;
             default: epilogue_tile<false>(e, tc, acc, quad, part, lane, first_split); break;
         }
     }
 }
 
-template <bool GATED>
+// One kernel per (gated, epilogue kind): a launch carries only its own epilogue's code (measured:
+// the runtime switch over all epilogues cost ~0.4 us of instruction fetch per launch).
+template <bool GATED, int KIND>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
                    const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo, TcEpi e) {
@@ -408,20 +418,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     } else {  // epilogue warps 2..9: quadrant = warp % 4, the two warps of a quadrant alternate chunks
         const int quad = warp & 3, part = (warp - 2) >> 2;
-        // Pull the epilogue's parameters into registers while the previous kernel drains.
-        asm volatile("" ::"r"(e.kind), "r"(e.flags), "r"(e.m), "r"(e.n), "r"(e.bn), "l"(e.y), "l"(e.y_hi),
-                     "l"(e.bias));
+        // Pull the epilogue's parameters and the first tile's bias into registers while the
+        // previous kernel drains; a later tile's bias loads while its accumulator fills.
+        asm volatile("" ::"r"(e.flags), "r"(e.m), "r"(e.n), "r"(e.bn), "l"(e.y), "l"(e.y_hi), "l"(e.bias));
+        const int per_split = e.tiles_m * e.tiles_n;
+        int t = blockIdx.x;
+        float bval = t < tiles_total ? tile_bias(e, tile_coord(e, t).n0, quad, lane, t < per_split) : 0.f;
         pdl_wait();
-        int tl = 0;
-        for (int t = blockIdx.x; t < tiles_total; t += gridDim.x, tl++) {
+        for (int tl = 0; t < tiles_total; t += gridDim.x, tl++) {
             const int b = tl & 1;
             if (!mbar_wait(&acc_full[b], (tl >> 1) & 1, e.status, 4, abort)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const TileCoord tc = tile_coord(e, t);
-            epilogue_dispatch<GATED>(e, tc, tmem + b * acc_cols, quad, part, lane, t < e.tiles_m * e.tiles_n);
+            if constexpr (KIND == EPI_GENERIC)
+                epilogue_tile<GATED>(e, tc, tmem + b * acc_cols, quad, part, lane, t < per_split);
+            else
+                epilogue_fast<KIND, GATED>(e, tc, tmem + b * acc_cols, quad, part, lane, bval);
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[b]);
+            const int tn = t + gridDim.x;
+            if (KIND != EPI_GENERIC && tn < tiles_total) bval = tile_bias(e, tile_coord(e, tn).n0, quad, lane, tn < per_split);
         }
     }
     __syncwarp();
@@ -725,6 +742,38 @@ static int epi_kind(const TcEpi& e, bool gated) {
     return EPI_GENERIC;
 }
 
+using GemmKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, TcEpi);
+
+// The kernel instantiation for a plan: gated plans have the gate epilogue or the generic one.
+static GemmKernel gemm_kernel_for(bool gated, int kind) {
+    if (gated) return kind == EPI_SPLIT_GATE ? gemm_tc_kernel<true, EPI_SPLIT_GATE> : gemm_tc_kernel<true, EPI_GENERIC>;
+    switch (kind) {
+        case EPI_F32: return gemm_tc_kernel<false, EPI_F32>;
+        case EPI_F32_ACCUM: return gemm_tc_kernel<false, EPI_F32_ACCUM>;
+        case EPI_SPLIT: return gemm_tc_kernel<false, EPI_SPLIT>;
+        case EPI_SPLIT_GELU: return gemm_tc_kernel<false, EPI_SPLIT_GELU>;
+        case EPI_F32_SILU: return gemm_tc_kernel<false, EPI_F32_SILU>;
+        case EPI_RED: return gemm_tc_kernel<false, EPI_RED>;
+        default: return gemm_tc_kernel<false, EPI_GENERIC>;
+    }
+}
+
+// Shared-memory opt-in for every instantiation (once per process; plans exist per device but the
+// attribute is per function).
+static void set_gemm_attributes() {
+    static bool done = false;
+    if (done) return;
+    const int kinds[] = {EPI_GENERIC, EPI_F32, EPI_F32_ACCUM, EPI_SPLIT, EPI_SPLIT_GELU, EPI_SPLIT_GATE,
+                         EPI_F32_SILU, EPI_RED};
+    for (int kd : kinds) {
+        cudaFuncSetAttribute(gemm_kernel_for(false, kd), cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+        cudaFuncSetAttribute(gemm_kernel_for(true, kd), cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+    }
+    cudaFuncSetAttribute(gemm_tc_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+    cudaFuncSetAttribute(gemm_tc_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+    done = true;
+}
+
 mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     const bool gated = (a.flags & MT_LINEAR_SILU_GATE) != 0;
     MT_REQUIRE(ctx, a.m > 0 && a.n > 0 && a.k > 0, MT_ERR_SHAPE, "gemm_tc: empty shape m %d n %d k %d", a.m, a.n, a.k);
@@ -796,14 +845,7 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     plan->smem = (size_t)e.stages * stage_bytes + 1024;
     const int work = e.tiles_n * e.tiles_m * split;
     plan->grid = dim3((pair ? 2 : 1) * (work < slots ? work : slots), 1, 1);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
-        cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
-        cudaFuncSetAttribute(gemm_tc_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
-        cudaFuncSetAttribute(gemm_tc_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
-        attr_set = true;
-    }
+    set_gemm_attributes();
     return MT_OK;
 }
 
@@ -842,12 +884,7 @@ mt_status make_gemm_plan_bare(int sm_count, const LinearArgs& a, GemmPlan* plan)
     plan->smem = (size_t)e.stages * stage_bytes + 1024;
     const int work = e.tiles_n * e.tiles_m;
     plan->grid = dim3(work < sms ? work : sms, 1, 1);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
-        cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
-        attr_set = true;
-    }
+    set_gemm_attributes();
     return MT_OK;
 }
 
@@ -861,10 +898,8 @@ void run_gemm_plan(const GemmPlan& p, cudaStream_t s) {
             launch_k_pair(gemm_tc_pair_kernel<true>, p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
         else
             launch_k_pair(gemm_tc_pair_kernel<false>, p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
-    } else if (p.gated) {
-        launch_k(gemm_tc_kernel<true>, p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
     } else {
-        launch_k(gemm_tc_kernel<false>, p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
+        launch_k(gemm_kernel_for(p.gated, e.kind), p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
     }
     if (e.mode == 2) {
         const long long total = (long long)e.m * e.n;

@@ -101,6 +101,10 @@ def test_tensor_core_shapes(ctx, mt, oracle, m, n, k, flags, bias):
     (21, 300, 896, 8, True, "f32"),              # runtime-flag path: gate with fp32 out
     (1024, 4864, 896, 8, False, "split"),        # SILU gate, several tiles per CTA (prefill gate/up)
     (2048, 1152, 896, 0, True, "f32"),           # several tiles per CTA (prefill qkv)
+    (64, 4864, 896, 8, False, "split"),          # SILU gate, one tile per CTA (LLM decode gate/up)
+    (130, 1024, 128, 2, True, "f32"),            # residual add without split-K (two k blocks)
+    (100, 520, 256, 0, True, "split"),           # hi/lo out, ragged rows and columns
+    (64, 1030, 128, 0, True, "f32"),             # odd row stride
 ])
 def test_linear_split_epilogues(ctx, mt, oracle, m, n, k, flags, bias, outs):
     """mt_linear_split (bf16 hi/lo activations in, fp32 and/or hi/lo out) against the oracle, one
