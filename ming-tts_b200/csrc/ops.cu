@@ -314,22 +314,32 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
     const int chunks = (nk + SC - 1) / SC;
     float* kc = a.kc + (size_t)r * a.req_stride + (size_t)h * a.cap * 64;
     float* vc = a.vc + (size_t)r * a.req_stride + (size_t)h * a.cap * 64;
-    // Old keys of chunk c: [c0, min(c1, p_first)); thread 0 arms both barriers and issues the copies.
-    auto issue = [&](int c) {
+    // Old keys of chunk c: [c0, min(c1, p_first)). Thread 0 arms both barriers for the chunk's
+    // bytes (arm), then lane 0 of every warp copies one slice of the keys and values (issue): one
+    // thread's bulk copies stream one after another at a few bytes per clock from DRAM, so the
+    // slices of eight warps keep eight times as many bytes in flight.
+    auto old_keys = [&](int c) {
         const int c0 = jS + c * SC, c1 = min(c0 + SC, p_end);
-        const int nold = max(0, min(c1, p_first) - c0);
-        const uint32_t bytes = (uint32_t)nold * 256u;
+        return max(0, min(c1, p_first) - c0);
+    };
+    auto arm = [&](int c) {
+        const uint32_t bytes = (uint32_t)old_keys(c) * 256u;
         mbar_expect_tx(&bar[0], bytes);
         mbar_expect_tx(&bar[1], bytes);
-        if (nold > 0) {
-            const int s0 = c0 % a.cap;
-            const int len1 = min(nold, a.cap - s0);
-            bulk_load(Ks, kc + (size_t)s0 * 64, (uint32_t)len1 * 256u, &bar[0]);
-            bulk_load(Vs, vc + (size_t)s0 * 64, (uint32_t)len1 * 256u, &bar[1]);
-            if (len1 < nold) {
-                bulk_load(Ks + (size_t)len1 * 64, kc, (uint32_t)(nold - len1) * 256u, &bar[0]);
-                bulk_load(Vs + (size_t)len1 * 64, vc, (uint32_t)(nold - len1) * 256u, &bar[1]);
-            }
+    };
+    auto issue = [&](int c) {  // lane 0 of warp `warp`
+        const int nold = old_keys(c);
+        const int per = (nold + AD_THREADS / 32 - 1) / (AD_THREADS / 32);
+        const int k0 = warp * per, k1 = min(nold, k0 + per);
+        if (k0 >= k1) return;
+        const int s0 = (jS + c * SC + k0) % a.cap;  // ring slot of this slice's first key
+        const int len1 = min(k1 - k0, a.cap - s0);
+        bulk_load(Ks + (size_t)k0 * 64, kc + (size_t)s0 * 64, (uint32_t)len1 * 256u, &bar[0]);
+        bulk_load(Vs + (size_t)k0 * 64, vc + (size_t)s0 * 64, (uint32_t)len1 * 256u, &bar[1]);
+        if (k0 + len1 < k1) {  // the slice wraps around the ring
+            const uint32_t rest = (uint32_t)(k1 - k0 - len1) * 256u;
+            bulk_load(Ks + (size_t)(k0 + len1) * 64, kc, rest, &bar[0]);
+            bulk_load(Vs + (size_t)(k0 + len1) * 64, vc, rest, &bar[1]);
         }
     };
     if (tid == 0) {
@@ -337,7 +347,7 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
         mbar_init(&bar[1], 1);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        issue(0);
+        arm(0);
     }
     if (tid < nrg) {
         m_run[tid] = -INFINITY;
@@ -351,6 +361,7 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
         rot_s[i][l] = sn;
     }
     __syncthreads();
+    if (lane == 0) issue(0);
     pdl_wait();
     pdl_launch();
 
@@ -412,10 +423,7 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
         const int old_end = min(c1, p_first);
         const int nold = max(0, old_end - c0);
         __syncthreads();  // the previous chunk's readers are done with Ks, Vs and sc
-        if (c > 0 && tid == 0) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(c);
-        }
+        if (c > 0 && tid == 0) arm(c);
         // New keys of this chunk from the stash.
         for (int e = tid; e < (cn - nold) * 64; e += AD_THREADS) {
             const int jj = nold + e / 64, d = e % 64;
@@ -423,7 +431,11 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
             Ks[(size_t)jj * 64 + d] = nw[(i * 2) * 64 + d];
             Vs[(size_t)jj * 64 + d] = nw[(i * 2 + 1) * 64 + d];
         }
-        __syncthreads();
+        __syncthreads();  // chunk c armed (thread 0) and the previous chunk's reads done
+        if (c > 0 && lane == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(c);
+        }
         if (!mbar_wait(&bar[0], c & 1, a.status, 20, abort)) { ok = false; break; }
         // Scores: item (key pair p, row i) scores keys k0 and k0 + 8 (same 16-byte skew s = p & 7,
         // so the eight lanes of a shared-memory phase read eight distinct bank groups of K and one
