@@ -42,6 +42,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
 // Shared-memory matrix descriptor: K-major operand in the 128-byte swizzle canonical layout
 // (8-row x 128-byte atoms, 1024 bytes apart), sm_100 descriptor version 1.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
@@ -366,29 +374,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
             }
             pdl_wait();
-            int g = 0;
+            // Stage s and the parity of its current use advance incrementally: a division by the
+            // runtime stage count on every k block cost more than the MMAs of a k block.
+            int g = 0, s = 0;
+            uint32_t ph = 0;
             for (int t = blockIdx.x; t < tiles_total && !*abort; t += gridDim.x) {
                 const TileCoord tc = tile_coord(e, t);
-                for (int kb = tc.kb_begin; kb < tc.kb_end; kb++, g++) {
-                    const int s = g % S;
+                for (int kb = tc.kb_begin; kb < tc.kb_end; kb++, g++, s = s + 1 == S ? 0 : s + 1, ph ^= s == 0) {
                     uint8_t* st = base + (size_t)s * stage_bytes;
                     const int kc = kb * TC_BK;
                     if (g >= pre) {
-                        if (!mbar_wait(&empty_bar[s], ((g / S) & 1) ^ 1, e.status, 1, abort)) break;
+                        if (!mbar_wait(&empty_bar[s], ph ^ 1, e.status, 1, abort)) break;
                         mbar_expect_tx(&full_bar[s], stage_bytes);
                         tma_load_2d(st, &tm_w, &full_bar[s], kc, tc.n0);
                         if (GATED) tma_load_2d(st + w_bytes, &tm_w2, &full_bar[s], kc, tc.n0);
                     }
                     uint8_t* xs = st + w_bytes * (GATED ? 2 : 1);
-                    tma_load_2d(xs, &tm_xhi, &full_bar[s], kc, tc.m0);
-                    tma_load_2d(xs + x_bytes, &tm_xlo, &full_bar[s], kc, tc.m0);
+                    if (e.x_planes) {  // both planes, one copy (the two planes' order is free: the epilogue sums them)
+                        tma_load_3d(xs, &tm_xhi, &full_bar[s], kc, tc.m0, 0);
+                    } else {
+                        tma_load_2d(xs, &tm_xhi, &full_bar[s], kc, tc.m0);
+                        tma_load_2d(xs + x_bytes, &tm_xlo, &full_bar[s], kc, tc.m0);
+                    }
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer: one MMA of N = 2 bn per 16-wide K step per weight matrix
             const uint32_t idesc = idesc_bf16(TC_BM, 2 * e.bn);
-            int g = 0, tl = 0;
+            int s = 0, tl = 0;
+            uint32_t ph = 0;
             for (int t = blockIdx.x; t < tiles_total && !*abort; t += gridDim.x, tl++) {
                 const TileCoord tc = tile_coord(e, t);
                 const int b = tl & 1;
@@ -396,9 +411,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t acc = tmem + b * acc_cols;
                 bool ok = true;
-                for (int kb = tc.kb_begin, i = 0; kb < tc.kb_end; kb++, i++, g++) {
-                    const int s = g % S;
-                    if (!mbar_wait(&full_bar[s], (g / S) & 1, e.status, 3, abort)) { ok = false; break; }
+                for (int kb = tc.kb_begin, i = 0; kb < tc.kb_end; kb++, i++, s = s + 1 == S ? 0 : s + 1, ph ^= s == 0) {
+                    if (!mbar_wait(&full_bar[s], ph, e.status, 3, abort)) { ok = false; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t wa = smem_u32(base + (size_t)s * stage_bytes);
                     const uint32_t xa = wa + w_bytes * (GATED ? 2 : 1);
@@ -720,6 +734,26 @@ static bool make_map(CUtensorMap* map, const void* ptr, int rows, int cols, int 
     return r == CUDA_SUCCESS;
 }
 
+// 3-D map over both activation planes: [plane][rows][cols] with the planes |x_lo - x_hi| bytes
+// apart, based at the lower one; box = 64 cols x box_rows x 2 planes, so one TMA copy fills a
+// stage's [plane 0 rows | plane 1 rows] (an SM's TMA takes a few hundred cycles per copy, so a
+// stage's copies, not its bytes, set the pace of small GEMMs). False where TMA cannot address it.
+static bool make_planes_map(CUtensorMap* map, const void* hi, const void* lo, int rows, int cols, int ld, int box_rows) {
+    const uintptr_t a = (uintptr_t)hi, b = (uintptr_t)lo;
+    const uintptr_t base = a < b ? a : b, gap = a < b ? b - a : a - b;
+    if (gap == 0 || (gap & 15u) || gap >= ((uintptr_t)1 << 40)) return false;
+    auto enc = get_encode();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, 2};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)gap};
+    cuuint32_t box[3] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows, 2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, reinterpret_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 static int round16(int v) { return (v + 15) & ~15; }
 
 // The compile-time epilogue for this plan's flags and outputs, or EPI_GENERIC.
@@ -837,8 +871,9 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
 
     bool ok = make_map(&plan->tw, a.w, a.n, a.k, a.k, TC_BM);
     ok = ok && make_map(&plan->tw2, gated ? a.w2 : a.w, a.n, a.k, a.k, TC_BM);
-    ok = ok && make_map(&plan->th, a.x_hi, a.m, a.k, a.ld_split, e.bn);
     ok = ok && make_map(&plan->tl, a.x_lo, a.m, a.k, a.ld_split, e.bn);
+    e.x_planes = !pair && make_planes_map(&plan->th, a.x_hi, a.x_lo, a.m, a.k, a.ld_split, e.bn) ? 1 : 0;
+    if (!e.x_planes) ok = ok && make_map(&plan->th, a.x_hi, a.m, a.k, a.ld_split, e.bn);
     MT_REQUIRE(ctx, ok, MT_ERR_CUDA, "gemm_tc: cuTensorMapEncodeTiled failed (m %d n %d k %d)", a.m, a.n, a.k);
     plan->gated = gated;
     plan->pair = pair;
