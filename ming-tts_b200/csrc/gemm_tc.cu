@@ -30,7 +30,8 @@ namespace mt {
 constexpr int TC_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (warp 2 owns TMEM)
 constexpr int TC_EPI_WARPS = 8;
 constexpr int TC_BM = 128;  // weight rows per tile (MMA M)
-constexpr int TC_BK = 64;   // bf16 K per stage = one 128-byte swizzle span
+constexpr int TC_BK = 64;   // bf16 K per atom = one 128-byte swizzle span
+constexpr int TC_KA_MAX = 2;  // K atoms per pipeline stage (TcEpi::ka): one barrier round trip and commit per stage
 
 
 
@@ -305,9 +306,11 @@ __device__ __forceinline__ void epilogue_dispatch(const TcEpi& e, const TileCoor
     }
 }
 
-// One kernel per (gated, epilogue kind): a launch carries only its own epilogue's code (measured:
-// the runtime switch over all epilogues cost ~0.4 us of instruction fetch per launch).
-template <bool GATED, int KIND>
+// One kernel per (gated, epilogue kind, K atoms per stage): a launch carries only its own
+// epilogue's code (measured: the runtime switch over all epilogues cost ~0.4 us of instruction
+// fetch per launch), and the MMA thread's per-stage loop has no runtime trip counts (the loop runs
+// at a few hundred cycles per stage; a runtime atom count alone slowed it by 5-10%).
+template <bool GATED, int KIND, int KA>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
                    const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo, TcEpi e) {
@@ -322,7 +325,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
     const uint32_t w_bytes = TC_BM * 128, x_bytes = (uint32_t)e.bn * 128;
-    const uint32_t stage_bytes = w_bytes * (GATED ? 2 : 1) + 2 * x_bytes;
+    // A stage holds KA K atoms, each [weights (both matrices when gated) | x planes]; one full
+    // barrier, one empty barrier and one MMA commit per stage.
+    const uint32_t atom_bytes = w_bytes * (GATED ? 2 : 1) + 2 * x_bytes;
+    const uint32_t stage_bytes = KA * atom_bytes;
     // One accumulator = [W.x_hi | W.x_lo] per weight matrix (2 bn columns each); two of them.
     const uint32_t acc_cols = (uint32_t)e.bn * (GATED ? 4 : 2);
     uint32_t ncols = 32;
@@ -366,11 +372,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             int pre = 0;
             for (int t = blockIdx.x; t < tiles_total && pre < S; t += gridDim.x) {
                 const TileCoord tc = tile_coord(e, t);
-                for (int kb = tc.kb_begin; kb < tc.kb_end && pre < S; kb++, pre++) {
+                for (int kb = tc.kb_begin; kb < tc.kb_end && pre < S; kb += KA, pre++) {
+                    const int na = KA == 1 ? 1 : min(KA, tc.kb_end - kb);
                     uint8_t* st = base + (size_t)pre * stage_bytes;
-                    mbar_expect_tx(&full_bar[pre], stage_bytes);
-                    tma_load_2d(st, &tm_w, &full_bar[pre], kb * TC_BK, tc.n0);
-                    if (GATED) tma_load_2d(st + w_bytes, &tm_w2, &full_bar[pre], kb * TC_BK, tc.n0);
+                    mbar_expect_tx(&full_bar[pre], na * atom_bytes);
+                    for (int a = 0; a < na; a++) {
+                        tma_load_2d(st + a * atom_bytes, &tm_w, &full_bar[pre], (kb + a) * TC_BK, tc.n0);
+                        if (GATED) tma_load_2d(st + a * atom_bytes + w_bytes, &tm_w2, &full_bar[pre], (kb + a) * TC_BK, tc.n0);
+                    }
                 }
             }
             pdl_wait();
@@ -380,21 +389,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             uint32_t ph = 0;
             for (int t = blockIdx.x; t < tiles_total && !*abort; t += gridDim.x) {
                 const TileCoord tc = tile_coord(e, t);
-                for (int kb = tc.kb_begin; kb < tc.kb_end; kb++, g++, s = s + 1 == S ? 0 : s + 1, ph ^= s == 0) {
+                for (int kb = tc.kb_begin; kb < tc.kb_end; kb += KA, g++, s = s + 1 == S ? 0 : s + 1, ph ^= s == 0) {
+                    const int na = KA == 1 ? 1 : min(KA, tc.kb_end - kb);
                     uint8_t* st = base + (size_t)s * stage_bytes;
-                    const int kc = kb * TC_BK;
                     if (g >= pre) {
                         if (!mbar_wait(&empty_bar[s], ph ^ 1, e.status, 1, abort)) break;
-                        mbar_expect_tx(&full_bar[s], stage_bytes);
-                        tma_load_2d(st, &tm_w, &full_bar[s], kc, tc.n0);
-                        if (GATED) tma_load_2d(st + w_bytes, &tm_w2, &full_bar[s], kc, tc.n0);
+                        mbar_expect_tx(&full_bar[s], na * atom_bytes);
+                        for (int a = 0; a < na; a++) {
+                            tma_load_2d(st + a * atom_bytes, &tm_w, &full_bar[s], (kb + a) * TC_BK, tc.n0);
+                            if (GATED)
+                                tma_load_2d(st + a * atom_bytes + w_bytes, &tm_w2, &full_bar[s], (kb + a) * TC_BK, tc.n0);
+                        }
                     }
-                    uint8_t* xs = st + w_bytes * (GATED ? 2 : 1);
-                    if (e.x_planes) {  // both planes, one copy (the two planes' order is free: the epilogue sums them)
-                        tma_load_3d(xs, &tm_xhi, &full_bar[s], kc, tc.m0, 0);
-                    } else {
-                        tma_load_2d(xs, &tm_xhi, &full_bar[s], kc, tc.m0);
-                        tma_load_2d(xs + x_bytes, &tm_xlo, &full_bar[s], kc, tc.m0);
+                    for (int a = 0; a < na; a++) {
+                        uint8_t* xs = st + a * atom_bytes + w_bytes * (GATED ? 2 : 1);
+                        const int kc = (kb + a) * TC_BK;
+                        if (e.x_planes) {  // both planes, one copy (their order is free: the epilogue sums them)
+                            tma_load_3d(xs, &tm_xhi, &full_bar[s], kc, tc.m0, 0);
+                        } else {
+                            tma_load_2d(xs, &tm_xhi, &full_bar[s], kc, tc.m0);
+                            tma_load_2d(xs + x_bytes, &tm_xlo, &full_bar[s], kc, tc.m0);
+                        }
                     }
                 }
             }
@@ -411,18 +426,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t acc = tmem + b * acc_cols;
                 bool ok = true;
-                for (int kb = tc.kb_begin, i = 0; kb < tc.kb_end; kb++, i++, s = s + 1 == S ? 0 : s + 1, ph ^= s == 0) {
+                for (int kb = tc.kb_begin, i = 0; kb < tc.kb_end; kb += KA, i++, s = s + 1 == S ? 0 : s + 1, ph ^= s == 0) {
+                    const int na = KA == 1 ? 1 : min(KA, tc.kb_end - kb);
                     if (!mbar_wait(&full_bar[s], ph, e.status, 3, abort)) { ok = false; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t wa = smem_u32(base + (size_t)s * stage_bytes);
-                    const uint32_t xa = wa + w_bytes * (GATED ? 2 : 1);
+                    const uint32_t sa = smem_u32(base + (size_t)s * stage_bytes);
 #pragma unroll
-                    for (int kk = 0; kk < TC_BK / 16; kk++) {
-                        const uint32_t off = kk * 32;  // 16 bf16 along K inside the swizzle span
-                        const uint64_t bx = sw128_desc(xa + off);
-                        const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
-                        mma_bf16(acc, sw128_desc(wa + off), bx, idesc, accum);
-                        if (GATED) mma_bf16(acc + 2 * e.bn, sw128_desc(wa + w_bytes + off), bx, idesc, accum);
+                    for (int a = 0; a < KA; a++) {
+                        if (KA > 1 && a >= na) break;
+                        const uint32_t wa = sa + a * atom_bytes;
+                        const uint32_t xa = wa + w_bytes * (GATED ? 2 : 1);
+#pragma unroll
+                        for (int kk = 0; kk < TC_BK / 16; kk++) {
+                            const uint32_t off = kk * 32;  // 16 bf16 along K inside the swizzle span
+                            const uint64_t bx = sw128_desc(xa + off);
+                            const uint32_t accum = (i > 0 || a > 0 || kk > 0) ? 1u : 0u;
+                            mma_bf16(acc, sw128_desc(wa + off), bx, idesc, accum);
+                            if (GATED) mma_bf16(acc + 2 * e.bn, sw128_desc(wa + w_bytes + off), bx, idesc, accum);
+                        }
                     }
                     mma_commit(&empty_bar[s]);
                 }
@@ -778,18 +799,24 @@ static int epi_kind(const TcEpi& e, bool gated) {
 
 using GemmKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, TcEpi);
 
-// The kernel instantiation for a plan: gated plans have the gate epilogue or the generic one.
-static GemmKernel gemm_kernel_for(bool gated, int kind) {
-    if (gated) return kind == EPI_SPLIT_GATE ? gemm_tc_kernel<true, EPI_SPLIT_GATE> : gemm_tc_kernel<true, EPI_GENERIC>;
+template <int KA>
+static GemmKernel gemm_kernel_ka(bool gated, int kind) {
+    if (gated)
+        return kind == EPI_SPLIT_GATE ? gemm_tc_kernel<true, EPI_SPLIT_GATE, KA> : gemm_tc_kernel<true, EPI_GENERIC, KA>;
     switch (kind) {
-        case EPI_F32: return gemm_tc_kernel<false, EPI_F32>;
-        case EPI_F32_ACCUM: return gemm_tc_kernel<false, EPI_F32_ACCUM>;
-        case EPI_SPLIT: return gemm_tc_kernel<false, EPI_SPLIT>;
-        case EPI_SPLIT_GELU: return gemm_tc_kernel<false, EPI_SPLIT_GELU>;
-        case EPI_F32_SILU: return gemm_tc_kernel<false, EPI_F32_SILU>;
-        case EPI_RED: return gemm_tc_kernel<false, EPI_RED>;
-        default: return gemm_tc_kernel<false, EPI_GENERIC>;
+        case EPI_F32: return gemm_tc_kernel<false, EPI_F32, KA>;
+        case EPI_F32_ACCUM: return gemm_tc_kernel<false, EPI_F32_ACCUM, KA>;
+        case EPI_SPLIT: return gemm_tc_kernel<false, EPI_SPLIT, KA>;
+        case EPI_SPLIT_GELU: return gemm_tc_kernel<false, EPI_SPLIT_GELU, KA>;
+        case EPI_F32_SILU: return gemm_tc_kernel<false, EPI_F32_SILU, KA>;
+        case EPI_RED: return gemm_tc_kernel<false, EPI_RED, KA>;
+        default: return gemm_tc_kernel<false, EPI_GENERIC, KA>;
     }
+}
+
+// The kernel instantiation for a plan: gated plans have the gate epilogue or the generic one.
+static GemmKernel gemm_kernel_for(bool gated, int kind, int ka) {
+    return ka == 2 ? gemm_kernel_ka<2>(gated, kind) : gemm_kernel_ka<1>(gated, kind);
 }
 
 // Shared-memory opt-in for every instantiation (once per process; plans exist per device but the
@@ -800,8 +827,10 @@ static void set_gemm_attributes() {
     const int kinds[] = {EPI_GENERIC, EPI_F32, EPI_F32_ACCUM, EPI_SPLIT, EPI_SPLIT_GELU, EPI_SPLIT_GATE,
                          EPI_F32_SILU, EPI_RED};
     for (int kd : kinds) {
-        cudaFuncSetAttribute(gemm_kernel_for(false, kd), cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
-        cudaFuncSetAttribute(gemm_kernel_for(true, kd), cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+        for (int ka = 1; ka <= TC_KA_MAX; ka++) {
+            cudaFuncSetAttribute(gemm_kernel_for(false, kd, ka), cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+            cudaFuncSetAttribute(gemm_kernel_for(true, kd, ka), cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+        }
     }
     cudaFuncSetAttribute(gemm_tc_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
     cudaFuncSetAttribute(gemm_tc_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
@@ -841,7 +870,12 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     const int tile_rows = pair ? 2 * TC_BM : TC_BM;
     const int tiles_n = (a.n + tile_rows - 1) / tile_rows;
     const int slots = pair ? sms / 2 : sms;  // concurrent work units
-    const uint32_t stage_bytes = TC_BM * 128 * (gated ? 2 : 1) + (pair ? 1u : 2u) * e.bn * 128;
+    // Two K atoms per stage where three such stages still fit (the MMA thread's fixed cost per stage
+    // is then spread over twice the MMAs), one otherwise (fewer bytes in flight lost more than the
+    // round trips saved at the 96- and 128-row tiles of the flow DiT).
+    const uint32_t atom_bytes = TC_BM * 128 * (gated ? 2 : 1) + 2u * e.bn * 128;
+    e.ka = !pair && 3 * TC_KA_MAX * atom_bytes <= 200 * 1024 ? TC_KA_MAX : 1;
+    const uint32_t stage_bytes = pair ? TC_BM * 128 * (gated ? 2 : 1) + e.bn * 128 : e.ka * atom_bytes;
     const int tiles = tiles_n * ((a.m + e.bn - 1) / e.bn);
     e.stages = (int)((200 * 1024) / stage_bytes);
     if (e.stages > 8) e.stages = 8;
@@ -898,6 +932,7 @@ mt_status make_gemm_plan_bare(int sm_count, const LinearArgs& a, GemmPlan* plan)
     if (e.bn < 16) e.bn = 16;
     if (gated && e.bn > 64) e.bn = 64;
     e.tiles_m = (a.m + e.bn - 1) / e.bn;
+    e.ka = 1;
     const uint32_t stage_bytes = TC_BM * 128 * (gated ? 2 : 1) + 2u * e.bn * 128;
     e.stages = (int)((200 * 1024) / stage_bytes);
     if (e.stages > 8) e.stages = 8;
@@ -934,7 +969,7 @@ void run_gemm_plan(const GemmPlan& p, cudaStream_t s) {
         else
             launch_k_pair(gemm_tc_pair_kernel<false>, p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
     } else {
-        launch_k(gemm_kernel_for(p.gated, e.kind), p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
+        launch_k(gemm_kernel_for(p.gated, e.kind, e.ka), p.grid, TC_THREADS, p.smem, s, p.tw, p.tw2, p.th, p.tl, p.e);
     }
     if (e.mode == 2) {
         const long long total = (long long)e.m * e.n;

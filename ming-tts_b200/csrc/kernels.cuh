@@ -135,6 +135,7 @@ struct TcEpi {
     int mode;          // 0: epilogue in the kernel; 1: split-K reduced into y; 2: split-K sums into ws
     int kind;          // EPI_* epilogue specialisation chosen by the planner (EPI_GENERIC: runtime flags)
     int x_planes;      // 1: the x_hi map is 3-D and one copy loads both activation planes of a stage
+    int ka;            // K atoms (64-wide K blocks) per pipeline stage, 1 or 2
     float* ws; int ldws;
     unsigned int* status;
 };
