@@ -68,6 +68,14 @@ __device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) 
     lo = f32_to_bf16_rne(x - bf16f(hi));
 }
 
+// The same split for two values with packed conversions (round to nearest even; bf16 bits of x0 in
+// the low halves of hi2/lo2, of x1 in the high halves): one conversion per two values per term.
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi2, uint32_t& lo2) {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi2) : "f"(x1), "f"(x0));
+    const float r0 = x0 - bf16_lo(hi2), r1 = x1 - bf16_hi(hi2);
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo2) : "f"(r1), "f"(r0));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

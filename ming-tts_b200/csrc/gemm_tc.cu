@@ -266,7 +266,12 @@ __device__ __forceinline__ void epilogue_fast(const TcEpi& e, const TileCoord& t
             uint16_t* __restrict__ lp = e.y_lo + row0 * lds + n;
             uint16_t h[16], l[16];
 #pragma unroll
-            for (int j = 0; j < 16; j++) split_bf16(v[j], h[j], l[j]);
+            for (int j = 0; j < 16; j += 2) {
+                uint32_t h2, l2;
+                split_bf16x2(v[j], v[j + 1], h2, l2);
+                h[j] = (uint16_t)h2, h[j + 1] = (uint16_t)(h2 >> 16);
+                l[j] = (uint16_t)l2, l[j + 1] = (uint16_t)(l2 >> 16);
+            }
             if (full) {
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
