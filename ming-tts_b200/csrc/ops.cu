@@ -51,15 +51,11 @@ __global__ void __launch_bounds__(RMS_THREADS) rmsnorm_kernel(RmsArgs a) {
         o.w = v[i].w * scale * bf16_hi(wv.y);
         if (a.y) reinterpret_cast<float4*>(a.y + (size_t)row * a.ldy)[c] = o;
         if (a.y_hi) {
-            uint16_t h[4], l[4];
-            split_bf16(o.x, h[0], l[0]);
-            split_bf16(o.y, h[1], l[1]);
-            split_bf16(o.z, h[2], l[2]);
-            split_bf16(o.w, h[3], l[3]);
-            reinterpret_cast<uint2*>(a.y_hi + (size_t)row * a.ld_split)[c] =
-                make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
-            reinterpret_cast<uint2*>(a.y_lo + (size_t)row * a.ld_split)[c] =
-                make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
+            uint32_t h01, l01, h23, l23;
+            split_bf16x2(o.x, o.y, h01, l01);
+            split_bf16x2(o.z, o.w, h23, l23);
+            reinterpret_cast<uint2*>(a.y_hi + (size_t)row * a.ld_split)[c] = make_uint2(h01, h23);
+            reinterpret_cast<uint2*>(a.y_lo + (size_t)row * a.ld_split)[c] = make_uint2(l01, l23);
         }
     }
 }
@@ -77,15 +73,11 @@ __global__ void split_kernel(const float* __restrict__ x, int ldx, int rows, int
          i += (long long)gridDim.x * blockDim.x) {
         const int r = (int)(i / c4), c = (int)(i % c4);
         const float4 v = reinterpret_cast<const float4*>(x + (size_t)r * ldx)[c];
-        uint16_t h[4], l[4];
-        split_bf16(v.x, h[0], l[0]);
-        split_bf16(v.y, h[1], l[1]);
-        split_bf16(v.z, h[2], l[2]);
-        split_bf16(v.w, h[3], l[3]);
-        reinterpret_cast<uint2*>(hi + (size_t)r * ld_split)[c] =
-            make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
-        reinterpret_cast<uint2*>(lo + (size_t)r * ld_split)[c] =
-            make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
+        uint32_t h01, l01, h23, l23;
+        split_bf16x2(v.x, v.y, h01, l01);
+        split_bf16x2(v.z, v.w, h23, l23);
+        reinterpret_cast<uint2*>(hi + (size_t)r * ld_split)[c] = make_uint2(h01, h23);
+        reinterpret_cast<uint2*>(lo + (size_t)r * ld_split)[c] = make_uint2(l01, l23);
     }
 }
 
@@ -547,14 +539,12 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
         const int head = h * G + g;
         if (a.out) *reinterpret_cast<float4*>(a.out + row * a.ldo + head * 64 + dd * 4) = make_float4(o0, o1, o2, o3);
         if (a.out_hi) {
-            uint16_t h0, l0, h1, l1, h2, l2, h3, l3;
-            split_bf16(o0, h0, l0);
-            split_bf16(o1, h1, l1);
-            split_bf16(o2, h2, l2);
-            split_bf16(o3, h3, l3);
+            uint32_t h01, l01, h23, l23;
+            split_bf16x2(o0, o1, h01, l01);
+            split_bf16x2(o2, o3, h23, l23);
             const size_t so = row * a.ld_split + head * 64 + dd * 4;
-            *reinterpret_cast<uint2*>(a.out_hi + so) = make_uint2(h0 | ((uint32_t)h1 << 16), h2 | ((uint32_t)h3 << 16));
-            *reinterpret_cast<uint2*>(a.out_lo + so) = make_uint2(l0 | ((uint32_t)l1 << 16), l2 | ((uint32_t)l3 << 16));
+            *reinterpret_cast<uint2*>(a.out_hi + so) = make_uint2(h01, h23);
+            *reinterpret_cast<uint2*>(a.out_lo + so) = make_uint2(l01, l23);
         }
     }
 }
@@ -642,12 +632,11 @@ __global__ void dit_attention_kernel(DitAttnArgs a) {
         const size_t row = (size_t)(b * S + i);
         if (a.out) *reinterpret_cast<float2*>(a.out + row * a.ldo + h * 64 + 2 * lane) = make_float2(o0, o1);
         if (a.out_hi) {
-            uint16_t h0, l0, h1, l1;
-            split_bf16(o0, h0, l0);
-            split_bf16(o1, h1, l1);
+            uint32_t h01, l01;
+            split_bf16x2(o0, o1, h01, l01);
             const size_t so = row * a.ld_split + h * 64 + 2 * lane;
-            *reinterpret_cast<uint32_t*>(a.out_hi + so) = h0 | ((uint32_t)h1 << 16);
-            *reinterpret_cast<uint32_t*>(a.out_lo + so) = l0 | ((uint32_t)l1 << 16);
+            *reinterpret_cast<uint32_t*>(a.out_hi + so) = h01;
+            *reinterpret_cast<uint32_t*>(a.out_lo + so) = l01;
         }
     }
 }
