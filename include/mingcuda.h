@@ -39,7 +39,8 @@ typedef enum {
     MT_ERR_CUDA = 4,      /* a CUDA runtime error (message has the CUDA string) */
     MT_ERR_TIMEOUT = 5,   /* a bounded device wait gave up (status word set by a kernel) */
     MT_ERR_NOMEM = 6,     /* a library allocation failed (engine/model creation only) */
-    MT_ERR_STATE = 7      /* call out of order (engine not begun, already flushed, ...) */
+    MT_ERR_STATE = 7,     /* call out of order (engine not begun, already flushed, ...) */
+    MT_ERR_CHECKPOINT = 8 /* unreadable or malformed checkpoint, missing tensor, wrong dtype or size */
 } mt_status;
 
 /* Epilogue flags of a linear, same bits as GemvFlags (Kernels.swift:21-27, Shaders.swift:40-44).
@@ -315,6 +316,23 @@ mt_status mt_model_create_random(mt_ctx* ctx, const mt_model_config* cfg, uint64
 /* Wraps a caller-owned device arena laid out as mt_model_tensors describes (e.g. a loaded checkpoint). */
 mt_status mt_model_create_from_arena(mt_ctx* ctx, const mt_model_config* cfg, void* device_arena,
                                      int with_embeddings, mt_model** out);
+/* ---------------------------------------------------------------------------------------------
+ * Checkpoint: a safetensors file (replaces SafeTensors.swift:7-87, WeightArena.tensor/linear
+ * Weights.swift:32-62 and the tensor names of the *Weights initialisers, Weights.swift:116-263).
+ * Every table tensor is found by its checkpoint name: bf16 tensors are copied as stored, the q/k/v
+ * projections (weights and biases) concatenated along their first axis into the table's
+ * "...qkv_proj" / "...to_qkv" tensor, fp32 table entries (rotary inv_freq, ISTFT window, the
+ * aggregator cls row) decoded from BF16 or F32. Failures return MT_ERR_CHECKPOINT with the
+ * reference's messages ("bad checkpoint: ...", "missing tensor NAME").
+ * ------------------------------------------------------------------------------------------- */
+/* Fills a host buffer of arena_bytes (>= mt_model_arena_bytes) laid out as mt_model_tensors
+ * describes; padding bytes are zero. Host-only: needs no context and no GPU. The message of a
+ * failure goes to err (err_len bytes, may be NULL). */
+mt_status mt_checkpoint_fill_arena(const char* path, const mt_model_config* cfg, int with_embeddings,
+                                   void* host_arena, size_t arena_bytes, char* err, size_t err_len);
+/* Loads the checkpoint into a new model whose device arena the model owns. */
+mt_status mt_model_load_safetensors(mt_ctx* ctx, const mt_model_config* cfg, const char* path,
+                                    int with_embeddings, mt_model** out);
 const mt_model_weights* mt_model_get_weights(const mt_model* model);
 const mt_model_config* mt_model_get_config(const mt_model* model);
 mt_status mt_model_arena(const mt_model* model, void** ptr, size_t* bytes);

@@ -17,9 +17,10 @@ from ctypes import POINTER, c_char_p, c_float, c_int, c_size_t, c_uint32, c_uint
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmingcuda.so")
 
-MT_OK, MT_ERR_ARG, MT_ERR_SHAPE, MT_ERR_CAPACITY, MT_ERR_CUDA, MT_ERR_TIMEOUT, MT_ERR_NOMEM, MT_ERR_STATE = range(8)
+(MT_OK, MT_ERR_ARG, MT_ERR_SHAPE, MT_ERR_CAPACITY, MT_ERR_CUDA, MT_ERR_TIMEOUT, MT_ERR_NOMEM, MT_ERR_STATE,
+ MT_ERR_CHECKPOINT) = range(9)
 STATUS_NAMES = ["MT_OK", "MT_ERR_ARG", "MT_ERR_SHAPE", "MT_ERR_CAPACITY", "MT_ERR_CUDA", "MT_ERR_TIMEOUT",
-                "MT_ERR_NOMEM", "MT_ERR_STATE"]
+                "MT_ERR_NOMEM", "MT_ERR_STATE", "MT_ERR_CHECKPOINT"]
 
 BIAS, ACCUM, GELU, SILU_GATE, SILU = 1, 2, 4, 8, 16
 
@@ -133,6 +134,9 @@ PROTOTYPES = {
     "mt_model_get_config": (_P, [_P]),
     "mt_model_arena": (c_int, [_P, POINTER(c_void_p), POINTER(c_size_t)]),
     "mt_model_destroy": (None, [_P]),
+    "mt_checkpoint_fill_arena": (c_int, [ctypes.c_char_p, POINTER(ModelConfig), c_int, _P, c_size_t, ctypes.c_char_p,
+                                         c_size_t]),
+    "mt_model_load_safetensors": (c_int, [_P, POINTER(ModelConfig), ctypes.c_char_p, c_int, POINTER(c_void_p)]),
     "mt_engine_create": (c_int, [_P, _P, POINTER(EngineOptions), POINTER(c_void_p)]),
     "mt_engine_destroy": (None, [_P]),
     "mt_engine_begin": (c_int, [_P, _P, c_int, c_int, _P, _P, _P, _P, c_int, c_float]),
@@ -331,17 +335,51 @@ def weights_struct(cfg: ModelConfig, base: int, tensors: list[TensorInfo]):
     return w, keep
 
 
-class Model:
-    """An mt_model with a device arena (random-init from `seed`)."""
+class CheckpointError(MingError):
+    """A safetensors file the loader cannot use (MT_ERR_CHECKPOINT)."""
 
-    def __init__(self, ctx: Context, cfg: ModelConfig | None = None, seed: int = 1, with_embeddings: bool = True):
+
+def checkpoint_fill_arena(path: str, cfg: ModelConfig | None = None, with_embeddings: bool = True):
+    """Host numpy uint8 arena (mt_model_tensors layout) filled from a safetensors file. No GPU."""
+    import numpy as np
+    cfg = cfg if cfg is not None else default_config()
+    nbytes = lib().mt_model_arena_bytes(ctypes.byref(cfg), int(with_embeddings))
+    arena = np.empty(nbytes, np.uint8)
+    err = ctypes.create_string_buffer(512)
+    st = lib().mt_checkpoint_fill_arena(str(path).encode(), ctypes.byref(cfg), int(with_embeddings),
+                                        arena.ctypes.data, nbytes, err, len(err))
+    if st != MT_OK:
+        raise (CheckpointError if st == MT_ERR_CHECKPOINT else MingError)(st, f"mt_checkpoint_fill_arena: {err.value.decode()}")
+    return arena
+
+
+class Model:
+    """An mt_model with a device arena: random-init from `seed`, or a checkpoint (Model.load)."""
+
+    def __init__(self, ctx: Context, cfg: ModelConfig | None = None, seed: int = 1, with_embeddings: bool = True,
+                 _handle=None):
         self.ctx = ctx
         self.cfg = cfg if cfg is not None else default_config()
         self.seed = seed
         self.with_embeddings = with_embeddings
         self._m = c_void_p()
+        if _handle is not None:
+            self._m = _handle
+            return
         ctx._check(lib().mt_model_create_random(ctx.handle, ctypes.byref(self.cfg), seed, int(with_embeddings),
                                                 ctypes.byref(self._m)), "mt_model_create_random")
+
+    @classmethod
+    def load(cls, ctx: Context, path: str, cfg: ModelConfig | None = None, with_embeddings: bool = True) -> "Model":
+        """A model whose arena is filled from a safetensors checkpoint (mt_model_load_safetensors)."""
+        cfg = cfg if cfg is not None else default_config()
+        h = c_void_p()
+        st = lib().mt_model_load_safetensors(ctx.handle, ctypes.byref(cfg), str(path).encode(), int(with_embeddings),
+                                             ctypes.byref(h))
+        if st != MT_OK:
+            msg = lib().mt_last_error(ctx.handle).decode()
+            raise (CheckpointError if st == MT_ERR_CHECKPOINT else MingError)(st, f"mt_model_load_safetensors: {msg}")
+        return cls(ctx, cfg, seed=0, with_embeddings=with_embeddings, _handle=h)
 
     @property
     def handle(self):

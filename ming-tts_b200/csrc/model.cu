@@ -156,6 +156,12 @@ struct mt_model {
     mt_model_weights w{};
 };
 
+namespace mt {
+void model_own_arena(mt_model* m) {
+    if (m) m->owns_arena = true;
+}
+}  // namespace mt
+
 namespace {
 
 template <typename T>
