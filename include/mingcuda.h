@@ -403,6 +403,22 @@ mt_status mt_engine_stage_ms(mt_engine* engine, float* ms4);
 mt_status mt_engine_generate(mt_engine* engine, void* stream, int requests, int prompt_rows, const float* embeds_host,
                              const int32_t* ids_host, const float* noise_host, int steps, float cfg, float* pcm_host,
                              long long pcm_stride, long long* pcm_count, float* stop_prob_host);
+/* Streaming delivery (replaces MingTTSModel.stream / synthesize(onChunk:), MingTTS.swift:46-61):
+ * the same generation as mt_engine_generate, but each PCM chunk is handed to on_chunk on the calling
+ * thread as soon as its copy has reached pinned host memory, in order: chunk index, requests, count
+ * samples per request, pcm[r * request_stride + j]. The pointer is valid only during the call.
+ * A non-zero return cancels: nothing further is enqueued and the call returns MT_ERR_STATE (the
+ * reference's Task cancellation ends the stream with an error the same way). pcm_count receives the
+ * samples delivered per request; stop_prob_host may be NULL. */
+typedef int (*mt_pcm_chunk_fn)(void* user, int chunk, int requests, int count, const float* pcm,
+                               long long request_stride);
+mt_status mt_engine_generate_stream(mt_engine* engine, void* stream, int requests, int prompt_rows,
+                                    const float* embeds_host, const int32_t* ids_host, const float* noise_host,
+                                    int steps, float cfg, mt_pcm_chunk_fn on_chunk, void* user,
+                                    long long* pcm_count, float* stop_prob_host);
+/* Mono IEEE-float WAV file (RIFF, 16-byte fmt chunk, format 3, 32 bits), as writeWav
+ * (main.swift:134-144). Host only. MT_ERR_ARG if the file cannot be written. */
+mt_status mt_write_wav_f32(const char* path, const float* samples, long long count, int sample_rate);
 
 /* ---------------------------------------------------------------------------------------------
  * Synthetic data (seeded random-init weights and noise)

@@ -23,6 +23,7 @@ STATUS_NAMES = ["MT_OK", "MT_ERR_ARG", "MT_ERR_SHAPE", "MT_ERR_CAPACITY", "MT_ER
                 "MT_ERR_NOMEM", "MT_ERR_STATE", "MT_ERR_CHECKPOINT"]
 
 BIAS, ACCUM, GELU, SILU_GATE, SILU = 1, 2, 4, 8, 16
+SAMPLE_RATE = 44100  # MingTTSModel.sampleRate: hop 882 samples per 20 ms frame
 
 
 class MingError(RuntimeError):
@@ -150,6 +151,9 @@ PROTOTYPES = {
     "mt_engine_stage_ms": (c_int, [_P, _P]),
     "mt_engine_generate": (c_int, [_P, _P, c_int, c_int, _P, _P, _P, c_int, c_float, _P, ctypes.c_longlong,
                                    POINTER(ctypes.c_longlong), _P]),
+    "mt_engine_generate_stream": (c_int, [_P, _P, c_int, c_int, _P, _P, _P, c_int, c_float, _P, _P,
+                                          POINTER(ctypes.c_longlong), _P]),
+    "mt_write_wav_f32": (c_int, [ctypes.c_char_p, _P, ctypes.c_longlong, c_int]),
     "mt_gaussian_noise_host": (None, [_P, c_size_t, c_uint64]),
     "mt_randn_bf16_host": (None, [_P, c_size_t, c_uint64, c_float]),
     "mt_randn_bf16": (c_int, [_P, _P, _P, c_size_t, c_uint64, c_float]),
@@ -433,6 +437,18 @@ def device_to_numpy(address: int, shape, dtype="float32"):
     return device_view(address, shape, dtype).cpu().numpy().copy()
 
 
+PCM_CHUNK_FN = ctypes.CFUNCTYPE(c_int, c_void_p, c_int, c_int, c_int, c_void_p, ctypes.c_longlong)
+
+
+def write_wav(path: str, samples, sample_rate: int = SAMPLE_RATE) -> None:
+    """Mono float32 WAV, by default at the model's 44.1 kHz (mt_write_wav_f32; main.swift:134-144)."""
+    import numpy as np
+    x = np.ascontiguousarray(samples, np.float32)
+    st = lib().mt_write_wav_f32(str(path).encode(), x.ctypes.data, x.size, sample_rate)
+    if st != MT_OK:
+        raise MingError(st, f"mt_write_wav_f32: cannot write {path}")
+
+
 class Engine:
     """mt_engine: the generation loop for R concurrent requests."""
 
@@ -505,6 +521,34 @@ class Engine:
                                                  cfg, ptr(pcm), stride, ctypes.byref(cnt), ptr(stop)),
                         "mt_engine_generate")
         return pcm[:, :cnt.value], stop
+
+    def generate_stream(self, requests, prompt_rows, noise_host, steps, on_chunk, cfg=2.0, embeds_host=None,
+                        ids_host=None, stream=None):
+        """mt_engine_generate_stream: on_chunk(index, pcm[requests, count]) gets each PCM chunk (a
+        numpy copy) as soon as it reaches the host; a truthy return cancels (MingError MT_ERR_STATE).
+        Returns (samples per request, stop probabilities [requests, steps])."""
+        import numpy as np
+        stop = np.zeros((requests, steps), np.float32)
+        cnt = ctypes.c_longlong()
+        errors = []
+
+        def trampoline(user, chunk, reqs, count, pcm, request_stride):
+            try:
+                view = np.ctypeslib.as_array(ctypes.cast(pcm, POINTER(c_float)), shape=(reqs * request_stride,))
+                block = view.reshape(reqs, request_stride)[:, :count].copy()
+                return 1 if on_chunk(chunk, block) else 0
+            except BaseException as exc:  # surface callback errors after the C call returns
+                errors.append(exc)
+                return 1
+
+        cb = PCM_CHUNK_FN(trampoline)
+        st = lib().mt_engine_generate_stream(self._e, stream if stream is not None else current_stream(), requests,
+                                             prompt_rows, ptr(embeds_host), ptr(ids_host), ptr(noise_host), steps,
+                                             cfg, ctypes.cast(cb, c_void_p), None, ctypes.byref(cnt), ptr(stop))
+        if errors:
+            raise errors[0]
+        self.ctx._check(st, "mt_engine_generate_stream")
+        return cnt.value, stop
 
     def close(self):
         if self._e:

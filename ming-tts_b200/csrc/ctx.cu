@@ -100,6 +100,42 @@ mt_status mt_ctx_check(mt_ctx* ctx, void* stream) {
     return MT_OK;
 }
 
+mt_status mt_write_wav_f32(const char* path, const float* samples, long long count, int sample_rate) {
+    if (!path || (!samples && count > 0) || count < 0 || sample_rate <= 0 || count * 4 > 0xFFFFFFFFLL - 36)
+        return MT_ERR_ARG;
+    FILE* f = fopen(path, "wb");
+    if (!f) return MT_ERR_ARG;
+    auto u32 = [&](uint32_t v) {
+        const unsigned char b[4] = {(unsigned char)v, (unsigned char)(v >> 8), (unsigned char)(v >> 16),
+                                    (unsigned char)(v >> 24)};
+        fwrite(b, 1, 4, f);
+    };
+    auto u16 = [&](uint16_t v) {
+        const unsigned char b[2] = {(unsigned char)v, (unsigned char)(v >> 8)};
+        fwrite(b, 1, 2, f);
+    };
+    const uint32_t bytes = (uint32_t)(count * 4);
+    fwrite("RIFF", 1, 4, f);
+    u32(36 + bytes);
+    fwrite("WAVEfmt ", 1, 8, f);
+    u32(16);
+    u16(3);  // IEEE float
+    u16(1);  // mono
+    u32((uint32_t)sample_rate);
+    u32((uint32_t)sample_rate * 4);
+    u16(4);
+    u16(32);
+    fwrite("data", 1, 4, f);
+    u32(bytes);
+    for (long long i = 0; i < count; i++) {  // little-endian fp32
+        uint32_t u;
+        memcpy(&u, &samples[i], 4);
+        u32(u);
+    }
+    const bool ok = ferror(f) == 0;
+    return fclose(f) == 0 && ok ? MT_OK : MT_ERR_ARG;
+}
+
 mt_status mt_ctx_set_gemm_pairs(mt_ctx* ctx, int mode) {
     if (!ctx) return MT_ERR_ARG;
     MT_REQUIRE(ctx, mode >= -1 && mode <= 1, MT_ERR_ARG, "mt_ctx_set_gemm_pairs: mode %d (-1, 0 or 1)", mode);

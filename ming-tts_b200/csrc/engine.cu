@@ -929,20 +929,27 @@ mt_status mt_engine_stage_ms(mt_engine* e, float* ms4) {
     return MT_OK;
 }
 
-mt_status mt_engine_generate(mt_engine* e, void* stream, int requests, int prompt_rows, const float* embeds_host,
-                             const int32_t* ids_host, const float* noise_host, int steps, float cfg, float* pcm_host,
-                             long long pcm_stride, long long* pcm_count, float* stop_prob_host) {
-    if (!e) return MT_ERR_ARG;
+}  // extern "C"
+
+namespace {
+
+// The generation loop shared by mt_engine_generate and mt_engine_generate_stream: prompt and noise
+// in, prefill, `steps` steps, flush. Each PCM emission ([R][max_chunk] on the device) is copied into
+// the next pinned ring slot behind an event; `sink(i, count, slot, request_stride)` receives emission
+// i in order as soon as its copy has landed (polled after every enqueue, waited for only when the
+// ring is full or at the end), so the host handles chunk i while the GPU runs later steps. A
+// non-zero sink return cancels: no further work is enqueued and MT_ERR_STATE is returned.
+template <typename Sink>
+mt_status generate_loop(mt_engine* e, void* stream, int requests, int prompt_rows, const float* embeds_host,
+                        const int32_t* ids_host, const float* noise_host, int steps, float cfg, long long pcm_limit,
+                        float* stop_prob_host, long long* pcm_count, const char* who, Sink&& sink) {
     mt_ctx* ctx = e->ctx;
-    MT_REQUIRE(ctx, (embeds_host || ids_host) && noise_host && pcm_host && pcm_count, MT_ERR_ARG,
-               "mt_engine_generate: null argument");
     const mt_model_config& c = e->cfg;
-    MT_REQUIRE(ctx, pcm_stride >= 4LL * c.hop * steps, MT_ERR_CAPACITY,
-               "mt_engine_generate: pcm_stride %lld < %lld samples", pcm_stride, 4LL * c.hop * steps);
     MT_REQUIRE(ctx, requests >= 1 && requests <= e->opt.max_requests && prompt_rows >= 1 &&
                         prompt_rows <= e->opt.max_prompt && steps >= 1 && steps <= e->opt.max_steps,
-               MT_ERR_CAPACITY, "mt_engine_generate: requests %d prompt %d steps %d exceed the engine", requests,
-               prompt_rows, steps);
+               MT_ERR_CAPACITY, "%s: requests %d prompt %d steps %d exceed the engine", who, requests, prompt_rows,
+               steps);
+    (void)c;
     cudaStream_t s = as_stream(stream);
     // Prompt and noise go straight from the caller's buffers into the engine (begin copies embeds and
     // noise from host or device memory); token ids go through a device stage for the gather kernel.
@@ -951,43 +958,54 @@ mt_status mt_engine_generate(mt_engine* e, void* stream, int requests, int promp
     if (!embeds_host) {
         cudaError_t err = cudaMemcpyAsync(e->ids_stage, ids_host, (size_t)requests * prompt_rows * sizeof(int32_t),
                                           cudaMemcpyHostToDevice, s);
-        if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "mt_engine_generate: %s", cudaGetErrorString(err));
+        if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
         ids_dev = e->ids_stage;
     }
     st = mt_engine_begin(e, stream, requests, prompt_rows, embeds_host, ids_dev, noise_host, nullptr, steps, cfg);
     if (st == MT_OK) st = mt_engine_prefill(e, stream);
 
-    // Each emission is copied into the next pinned ring slot; the slot's previous emission is unpacked
-    // into pcm_host (after its event) before the copy is enqueued, so the host unpacks emission i - 4
-    // while the GPU runs the steps after it.
     const size_t chunk_floats = (size_t)requests * e->max_chunk;
     std::vector<int> counts;
-    std::vector<long long> offsets;
+    size_t delivered = 0;
     long long total = 0;
-    auto unpack = [&](size_t i) {
+    bool cancelled = false;
+    auto deliver = [&](size_t i) -> bool {
         const float* src = e->ring_host + (i % kPcmRing) * chunk_floats;
-        for (int r = 0; r < requests; r++)
-            memcpy(pcm_host + r * pcm_stride + offsets[i], src + (size_t)r * e->max_chunk, counts[i] * sizeof(float));
+        if (sink(i, counts[i], src, (long long)e->max_chunk) != 0) cancelled = true;
+        return !cancelled;
+    };
+    // Hands over every emission whose copy has landed; with wait, also waits for emission `upto - 1`.
+    auto drain = [&](size_t upto, bool wait) -> mt_status {
+        while (delivered < upto && !cancelled) {
+            cudaEvent_t ev = e->ring_ev[delivered % kPcmRing];
+            cudaError_t q = cudaEventQuery(ev);
+            if (q == cudaErrorNotReady) {
+                if (!wait) break;
+                q = cudaEventSynchronize(ev);
+            }
+            if (q != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "%s: %s", who, cudaGetErrorString(q));
+            deliver(delivered++);
+        }
+        return MT_OK;
     };
     auto emit = [&](int count) -> mt_status {
-        MT_REQUIRE(ctx, total + count <= pcm_stride, MT_ERR_CAPACITY,
-                   "mt_engine_generate: %lld samples exceed pcm_stride %lld", total + count, pcm_stride);
+        MT_REQUIRE(ctx, total + count <= pcm_limit, MT_ERR_CAPACITY, "%s: %lld samples exceed %lld", who,
+                   total + count, pcm_limit);
         const size_t i = counts.size();
-        const int slot = (int)(i % kPcmRing);
-        if (i >= (size_t)kPcmRing) {
-            cudaError_t err = cudaEventSynchronize(e->ring_ev[slot]);
-            if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "mt_engine_generate: %s", cudaGetErrorString(err));
-            unpack(i - kPcmRing);
+        if (i >= (size_t)kPcmRing) {  // the slot's previous emission must be handed over first
+            mt_status d = drain(i - kPcmRing + 1, true);
+            if (d != MT_OK) return d;
         }
+        const int slot = (int)(i % kPcmRing);
         cudaMemcpyAsync(e->ring_host + slot * chunk_floats, e->pcm, chunk_floats * sizeof(float),
                         cudaMemcpyDeviceToHost, s);
         cudaEventRecord(e->ring_ev[slot], s);
-        offsets.push_back(total);
         counts.push_back(count);
         total += count;
-        return MT_OK;
+        return drain(counts.size(), false);
     };
-    for (int n = 0; st == MT_OK && n < steps; n++) {
+    int n = 0;
+    for (; st == MT_OK && !cancelled && n < steps; n++) {
         int count = 0;
         st = mt_engine_step(e, stream, &count);
         if (st != MT_OK) break;
@@ -995,26 +1013,66 @@ mt_status mt_engine_generate(mt_engine* e, void* stream, int requests, int promp
                         cudaMemcpyDeviceToHost, s);
         if (count > 0) st = emit(count);
     }
-    while (st == MT_OK) {
+    while (st == MT_OK && !cancelled) {
         int count = 0;
         st = mt_engine_flush(e, stream, &count);
         if (st != MT_OK || count == 0) break;
         st = emit(count);
     }
     cudaError_t err = cudaStreamSynchronize(s);
-    if (st == MT_OK && err != cudaSuccess) st = fail(ctx, MT_ERR_CUDA, "mt_engine_generate: %s", cudaGetErrorString(err));
+    if (st == MT_OK && err != cudaSuccess) st = fail(ctx, MT_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
+    if (st == MT_OK && !cancelled) st = drain(counts.size(), true);
+    if (st == MT_OK && cancelled)
+        st = fail(ctx, MT_ERR_STATE, "%s: cancelled by the chunk callback after chunk %zu", who, delivered - 1);
     if (st == MT_OK) {
-        for (size_t i = counts.size() > (size_t)kPcmRing ? counts.size() - kPcmRing : 0; i < counts.size(); i++)
-            unpack(i);
-        *pcm_count = total;
+        if (pcm_count) *pcm_count = total;
         if (stop_prob_host)
-            for (int n = 0; n < steps; n++)
+            for (int k = 0; k < steps; k++)
                 for (int r = 0; r < requests; r++) {
-                    const float* l = e->stop_host + ((size_t)n * requests + r) * 2;
-                    stop_prob_host[(size_t)r * steps + n] = 1.0f / (1.0f + expf(l[0] - l[1]));  // Engine.swift:349
+                    const float* l = e->stop_host + ((size_t)k * requests + r) * 2;
+                    stop_prob_host[(size_t)r * steps + k] = 1.0f / (1.0f + expf(l[0] - l[1]));  // Engine.swift:349
                 }
     }
     return st;
+}
+
+}  // namespace
+
+extern "C" {
+
+mt_status mt_engine_generate(mt_engine* e, void* stream, int requests, int prompt_rows, const float* embeds_host,
+                             const int32_t* ids_host, const float* noise_host, int steps, float cfg, float* pcm_host,
+                             long long pcm_stride, long long* pcm_count, float* stop_prob_host) {
+    if (!e) return MT_ERR_ARG;
+    mt_ctx* ctx = e->ctx;
+    MT_REQUIRE(ctx, (embeds_host || ids_host) && noise_host && pcm_host && pcm_count, MT_ERR_ARG,
+               "mt_engine_generate: null argument");
+    MT_REQUIRE(ctx, pcm_stride >= 4LL * e->cfg.hop * steps, MT_ERR_CAPACITY,
+               "mt_engine_generate: pcm_stride %lld < %lld samples", pcm_stride, 4LL * e->cfg.hop * steps);
+    long long offset = 0;
+    return generate_loop(e, stream, requests, prompt_rows, embeds_host, ids_host, noise_host, steps, cfg, pcm_stride,
+                         stop_prob_host, pcm_count, "mt_engine_generate",
+                         [&](size_t, int count, const float* src, long long src_stride) {
+                             for (int r = 0; r < requests; r++)
+                                 memcpy(pcm_host + r * pcm_stride + offset, src + r * src_stride, count * sizeof(float));
+                             offset += count;
+                             return 0;
+                         });
+}
+
+mt_status mt_engine_generate_stream(mt_engine* e, void* stream, int requests, int prompt_rows,
+                                    const float* embeds_host, const int32_t* ids_host, const float* noise_host,
+                                    int steps, float cfg, mt_pcm_chunk_fn on_chunk, void* user,
+                                    long long* pcm_count, float* stop_prob_host) {
+    if (!e) return MT_ERR_ARG;
+    mt_ctx* ctx = e->ctx;
+    MT_REQUIRE(ctx, (embeds_host || ids_host) && noise_host && on_chunk, MT_ERR_ARG,
+               "mt_engine_generate_stream: null argument");
+    return generate_loop(e, stream, requests, prompt_rows, embeds_host, ids_host, noise_host, steps, cfg,
+                         1LL << 62, stop_prob_host, pcm_count, "mt_engine_generate_stream",
+                         [&](size_t i, int count, const float* src, long long src_stride) {
+                             return on_chunk(user, (int)i, requests, count, src, src_stride);
+                         });
 }
 
 }  // extern "C"

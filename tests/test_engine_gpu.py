@@ -173,6 +173,37 @@ def test_generate_host_api_matches_steps(ctx, mt, oracle):
         np.testing.assert_allclose(stop[r], p, atol=1e-5)
 
 
+def test_generate_stream_delivers_generate_chunks(ctx, mt, oracle):
+    """mt_engine_generate_stream hands over the same PCM as mt_engine_generate, chunk by chunk in
+    order (4 hop-sized frames per step from step 2 on, then the flush), and a truthy callback
+    return cancels with MT_ERR_STATE leaving the engine usable."""
+    cfg = mt.small_config()
+    model = mt.Model(ctx, cfg, seed=9)
+    R, T, steps = 3, 4, 6
+    rs = np.random.default_rng(9)
+    embeds = (0.5 * rs.standard_normal((R, T, cfg.llm.hidden))).astype(np.float32)
+    noise = rs.standard_normal((R, steps, cfg.latent_dim)).astype(np.float32)
+    eng = mt.Engine(ctx, model, R, T, steps)
+    pcm, stop = eng.generate(R, T, noise, steps, embeds_host=embeds)
+    chunks = []
+    count, stop_s = eng.generate_stream(R, T, noise, steps, lambda i, block: chunks.append((i, block)),
+                                        embeds_host=embeds)
+    assert [i for i, _ in chunks] == list(range(len(chunks)))
+    assert all(b.shape[0] == R for _, b in chunks)
+    streamed = np.concatenate([b for _, b in chunks], axis=1)
+    assert count == streamed.shape[1] == pcm.shape[1]
+    for r in range(R):
+        assert cosine(streamed[r], pcm[r]) > 0.999999 and rel_err(streamed[r], pcm[r]) < 1e-4
+    np.testing.assert_allclose(stop_s, stop, atol=1e-5)
+    seen = []
+    with pytest.raises(mt.MingError) as e:
+        eng.generate_stream(R, T, noise, steps, lambda i, block: seen.append(i) or i == 1, embeds_host=embeds)
+    assert e.value.status == mt.MT_ERR_STATE and seen == [0, 1]
+    pcm2, _ = eng.generate(R, T, noise, steps, embeds_host=embeds)
+    for r in range(R):
+        assert rel_err(pcm2[r], pcm[r]) < 1e-4
+
+
 def test_full_model_parity(ctx, mt, oracle):
     # Reference dimensions (Ming-3.0-tts-0.5B), two requests, four steps and the flush.
     compare(mt, oracle, ctx, mt.default_config(), R=2, T=8, steps=4, seed=1, use_ids=True)
