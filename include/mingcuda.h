@@ -421,6 +421,57 @@ mt_status mt_engine_generate_stream(mt_engine* engine, void* stream, int request
 mt_status mt_write_wav_f32(const char* path, const float* samples, long long count, int sample_rate);
 
 /* ---------------------------------------------------------------------------------------------
+ * Clone path: the audio VAE encoder (VAEEncoder.swift:56-107) and the aggregator over reference
+ * latents (MingEngine.aggregate, Engine.swift:236-256). Not on the per-step path; built from the
+ * operator entry points above with per-call device buffers.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct mt_encoder mt_encoder;
+
+/* VAEEncoderWeights (Weights.swift:229-262). The encoder stack has the VAE decoder's dimensions
+ * (window 65); the patch aggregator the same with 4 layers. */
+typedef struct {
+    int frame;           /* samples per frame = hop (882) */
+    int padded_frame;    /* frame rounded up to 64 columns (896): fc1's stored K */
+    int patch;           /* frames per latent (4) */
+    int max_frames;      /* longest clip mt_vae_encode takes (1600 frames = 32 s) */
+    const mt_bf16* fc1_w;               /* [hidden, padded_frame], zero past frame; no bias */
+    const mt_bf16 *fc2_w, *fc2_b;       /* [hidden, hidden] */
+    mt_qwen_weights stack;              /* audio.encoder.encoder */
+    mt_qwen_weights aggregator;         /* audio.encoder.aggregator */
+    const float* cls;                   /* audio.encoder.cls_embed [hidden] */
+    const mt_bf16 *fc3_w, *fc3_b;       /* posterior head [2 * latent_dim, hidden] */
+} mt_encoder_weights;
+
+int mt_encoder_tensors(const mt_model_config* cfg, uint64_t seed, mt_tensor_info* out, int cap);
+size_t mt_encoder_arena_bytes(const mt_model_config* cfg);
+/* bf16 N(0, 0.02) weights (fc1 zero past frame), norm gains 1.0, fp32 cls N(0, 0.02). */
+mt_status mt_encoder_create_random(mt_ctx* ctx, const mt_model_config* cfg, uint64_t seed, mt_encoder** out);
+mt_status mt_encoder_create_from_arena(mt_ctx* ctx, const mt_model_config* cfg, void* device_arena,
+                                       mt_encoder** out);
+/* The encoder tensors of a safetensors checkpoint ("audio.encoder.*", fc1 stored [hidden, frame]
+ * and padded with zero columns as WeightArena.paddedLinear does, Weights.swift:64-77). */
+mt_status mt_checkpoint_fill_encoder_arena(const char* path, const mt_model_config* cfg, void* host_arena,
+                                           size_t arena_bytes, char* err, size_t err_len);
+mt_status mt_encoder_load_safetensors(mt_ctx* ctx, const mt_model_config* cfg, const char* path,
+                                      mt_encoder** out);
+const mt_encoder_weights* mt_encoder_get_weights(const mt_encoder* enc);
+mt_status mt_encoder_arena(const mt_encoder* enc, void** ptr, size_t* bytes);
+void mt_encoder_destroy(mt_encoder* enc);
+
+/* VAEEncoder.encode: count samples (host, a non-zero multiple of frame * patch, at most max_frames
+ * frames) rounded to bf16, then fc1 -> fc2 -> encoder stack -> [4 frame rows | cls] per latent ->
+ * aggregator -> fc3 on the cls rows; mean_host and std_host receive [count / (frame * patch),
+ * latent_dim]: mean, and softplus(scale) + 1e-4. Synchronises `stream`. */
+mt_status mt_vae_encode(mt_encoder* enc, void* stream, const float* samples_host, long long count,
+                        float* mean_host, float* std_host);
+/* MingEngine.aggregate: the aggregator DiT over count reference latents at once (batch count,
+ * sequence [cls, x_embedder(latent)]), row 0 of each sequence; latents_host [count, latent_dim]
+ * -> rows_host [count, llm.hidden] (the reference voice's LLM input rows). count <=
+ * llm_capacity. Synchronises `stream`. */
+mt_status mt_aggregate_latents(mt_ctx* ctx, const mt_model* model, void* stream, const float* latents_host,
+                               int count, float* rows_host);
+
+/* ---------------------------------------------------------------------------------------------
  * Synthetic data (seeded random-init weights and noise)
  * ------------------------------------------------------------------------------------------- */
 

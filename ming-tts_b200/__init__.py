@@ -88,6 +88,12 @@ class TensorInfo(ctypes.Structure):
                 ("init", c_int), ("std", c_float), ("seed", c_uint64)]
 
 
+class EncoderWeights(ctypes.Structure):
+    _fields_ = [("frame", c_int), ("padded_frame", c_int), ("patch", c_int), ("max_frames", c_int),
+                ("fc1_w", c_void_p), ("fc2_w", c_void_p), ("fc2_b", c_void_p), ("stack", QwenWeights),
+                ("aggregator", QwenWeights), ("cls", c_void_p), ("fc3_w", c_void_p), ("fc3_b", c_void_p)]
+
+
 class EngineOptions(ctypes.Structure):
     _fields_ = [("max_requests", c_int), ("max_prompt", c_int), ("max_steps", c_int), ("vae_ring", c_int),
                 ("use_graphs", c_int), ("groups", c_int)]
@@ -151,6 +157,18 @@ PROTOTYPES = {
     "mt_engine_stage_ms": (c_int, [_P, _P]),
     "mt_engine_generate": (c_int, [_P, _P, c_int, c_int, _P, _P, _P, c_int, c_float, _P, ctypes.c_longlong,
                                    POINTER(ctypes.c_longlong), _P]),
+    "mt_encoder_tensors": (c_int, [POINTER(ModelConfig), c_uint64, _P, c_int]),
+    "mt_encoder_arena_bytes": (c_size_t, [POINTER(ModelConfig)]),
+    "mt_encoder_create_random": (c_int, [_P, POINTER(ModelConfig), c_uint64, POINTER(c_void_p)]),
+    "mt_encoder_create_from_arena": (c_int, [_P, POINTER(ModelConfig), _P, POINTER(c_void_p)]),
+    "mt_checkpoint_fill_encoder_arena": (c_int, [ctypes.c_char_p, POINTER(ModelConfig), _P, c_size_t,
+                                                 ctypes.c_char_p, c_size_t]),
+    "mt_encoder_load_safetensors": (c_int, [_P, POINTER(ModelConfig), ctypes.c_char_p, POINTER(c_void_p)]),
+    "mt_encoder_get_weights": (_P, [_P]),
+    "mt_encoder_arena": (c_int, [_P, POINTER(c_void_p), POINTER(c_size_t)]),
+    "mt_encoder_destroy": (None, [_P]),
+    "mt_vae_encode": (c_int, [_P, _P, _P, ctypes.c_longlong, _P, _P]),
+    "mt_aggregate_latents": (c_int, [_P, _P, _P, _P, c_int, _P]),
     "mt_engine_generate_stream": (c_int, [_P, _P, c_int, c_int, _P, _P, _P, c_int, c_float, _P, _P,
                                           POINTER(ctypes.c_longlong), _P]),
     "mt_write_wav_f32": (c_int, [ctypes.c_char_p, _P, ctypes.c_longlong, c_int]),
@@ -413,6 +431,130 @@ class Model:
             self.close()
         except Exception:
             pass
+
+
+def encoder_tensor_table(cfg: ModelConfig, seed: int = 0) -> list[TensorInfo]:
+    n = lib().mt_encoder_tensors(ctypes.byref(cfg), seed, None, 0)
+    arr = (TensorInfo * n)()
+    lib().mt_encoder_tensors(ctypes.byref(cfg), seed, arr, n)
+    return list(arr)
+
+
+def encoder_weights_struct(cfg: ModelConfig, base: int, tensors: list[TensorInfo]):
+    """mt_encoder_weights over an arena at `base` (device or host) laid out as `tensors`.
+    Returns (struct, keepalive)."""
+    off = {t.name.decode(): t.offset for t in tensors}
+    at = lambda name: base + off[name]
+    keep = []
+
+    def qwen(prefix, qc):
+        layers = (QwenLayer * qc.layers)()
+        for l in range(qc.layers):
+            p = f"{prefix}.layers.{l}"
+            layers[l] = QwenLayer(at(p + ".input_layernorm.weight"), at(p + ".self_attn.qkv_proj.weight"),
+                                  at(p + ".self_attn.qkv_proj.bias"), at(p + ".self_attn.o_proj.weight"),
+                                  at(p + ".post_attention_layernorm.weight"), at(p + ".mlp.gate_proj.weight"),
+                                  at(p + ".mlp.up_proj.weight"), at(p + ".mlp.down_proj.weight"))
+        keep.append(layers)
+        return QwenWeights(qc, ctypes.cast(layers, POINTER(QwenLayer)), at(prefix + ".norm.weight"))
+
+    e = "audio.encoder"
+    agg_cfg = QwenConfig.from_buffer_copy(cfg.vae)
+    agg_cfg.layers = 4
+    w = EncoderWeights()
+    w.frame, w.padded_frame, w.patch, w.max_frames = cfg.hop, (cfg.hop + 63) // 64 * 64, 4, 1600
+    w.fc1_w, w.fc2_w, w.fc2_b = at(e + ".fc1.weight"), at(e + ".fc2.weight"), at(e + ".fc2.bias")
+    w.stack = qwen(e + ".encoder", cfg.vae)
+    w.aggregator = qwen(e + ".aggregator", agg_cfg)
+    w.cls, w.fc3_w, w.fc3_b = at(e + ".cls_embed"), at(e + ".fc3.weight"), at(e + ".fc3.bias")
+    return w, keep
+
+
+def checkpoint_fill_encoder_arena(path: str, cfg: ModelConfig | None = None):
+    """Host numpy uint8 encoder arena filled from a safetensors file. No GPU."""
+    import numpy as np
+    cfg = cfg if cfg is not None else default_config()
+    nbytes = lib().mt_encoder_arena_bytes(ctypes.byref(cfg))
+    arena = np.empty(nbytes, np.uint8)
+    err = ctypes.create_string_buffer(512)
+    st = lib().mt_checkpoint_fill_encoder_arena(str(path).encode(), ctypes.byref(cfg), arena.ctypes.data, nbytes, err,
+                                                len(err))
+    if st != MT_OK:
+        raise (CheckpointError if st == MT_ERR_CHECKPOINT else MingError)(
+            st, f"mt_checkpoint_fill_encoder_arena: {err.value.decode()}")
+    return arena
+
+
+class Encoder:
+    """mt_encoder: the audio VAE encoder of the clone path (random-init from `seed`, or Encoder.load)."""
+
+    def __init__(self, ctx: Context, cfg: ModelConfig | None = None, seed: int = 1, _handle=None):
+        self.ctx = ctx
+        self.cfg = cfg if cfg is not None else default_config()
+        self.seed = seed
+        self._e = c_void_p()
+        if _handle is not None:
+            self._e = _handle
+            return
+        ctx._check(lib().mt_encoder_create_random(ctx.handle, ctypes.byref(self.cfg), seed, ctypes.byref(self._e)),
+                   "mt_encoder_create_random")
+
+    @classmethod
+    def load(cls, ctx: Context, path: str, cfg: ModelConfig | None = None) -> "Encoder":
+        cfg = cfg if cfg is not None else default_config()
+        h = c_void_p()
+        st = lib().mt_encoder_load_safetensors(ctx.handle, ctypes.byref(cfg), str(path).encode(), ctypes.byref(h))
+        if st != MT_OK:
+            msg = lib().mt_last_error(ctx.handle).decode()
+            raise (CheckpointError if st == MT_ERR_CHECKPOINT else MingError)(st, f"mt_encoder_load_safetensors: {msg}")
+        return cls(ctx, cfg, seed=0, _handle=h)
+
+    def tensors(self):
+        return encoder_tensor_table(self.cfg, self.seed)
+
+    def arena(self):
+        p, n = c_void_p(), c_size_t()
+        lib().mt_encoder_arena(self._e, ctypes.byref(p), ctypes.byref(n))
+        return p.value, n.value
+
+    def arena_to_host(self):
+        import numpy as np
+        p, nbytes = self.arena()
+        return device_to_numpy(p, (nbytes,), np.uint8)
+
+    def encode(self, samples, stream=None):
+        """VAEEncoder.encode: posterior (mean, std), each [latents, latent_dim]."""
+        import numpy as np
+        x = np.ascontiguousarray(samples, np.float32)
+        frames_per_latent = 4 * self.cfg.hop
+        latents = x.size // frames_per_latent
+        mean = np.zeros((latents, self.cfg.latent_dim), np.float32)
+        std = np.zeros_like(mean)
+        self.ctx._check(lib().mt_vae_encode(self._e, stream if stream is not None else current_stream(), x.ctypes.data,
+                                            x.size, mean.ctypes.data, std.ctypes.data), "mt_vae_encode")
+        return mean, std
+
+    def close(self):
+        if self._e:
+            lib().mt_encoder_destroy(self._e)
+            self._e = c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def aggregate_latents(ctx: Context, model: "Model", latents, stream=None):
+    """MingEngine.aggregate: [count, latent_dim] reference latents -> [count, llm.hidden] LLM input rows."""
+    import numpy as np
+    x = np.ascontiguousarray(latents, np.float32)
+    count = x.shape[0]
+    rows = np.zeros((count, model.cfg.llm.hidden), np.float32)
+    ctx._check(lib().mt_aggregate_latents(ctx.handle, model.handle, stream if stream is not None else current_stream(),
+                                          x.ctypes.data, count, rows.ctypes.data), "mt_aggregate_latents")
+    return rows
 
 
 class _DeviceView:

@@ -306,14 +306,18 @@ std::vector<std::string> sources(const std::string& name) {
     return {name};
 }
 
-// Fills `arena` (arena_bytes, laid out as the tensor table) from the file; err gets the message.
-bool fill_arena(const SafeTensorsFile& f, const mt_model_config& cfg, bool embeddings, uint8_t* arena,
-                size_t arena_bytes, std::string& err) {
-    const int n = mt_model_tensors(&cfg, 0, embeddings ? 1 : 0, nullptr, 0);
-    std::vector<mt_tensor_info> table((size_t)n);
-    mt_model_tensors(&cfg, 0, embeddings ? 1 : 0, table.data(), n);
-    if (mt_model_arena_bytes(&cfg, embeddings ? 1 : 0) > arena_bytes) {
-        err = "checkpoint: arena buffer smaller than the model's arena";
+// A bf16 [rows, stored] checkpoint tensor laid out as [rows, padded] with zero columns past
+// `stored` (WeightArena.paddedLinear, Weights.swift:64-77: the encoder's fc1 frames of 882 samples).
+struct Padded {
+    std::string name;
+    long long rows = 0, stored = 0, padded = 0;
+};
+
+// Fills `arena` (arena_bytes, laid out as `table`) from the file; err gets the message.
+bool fill_table(const SafeTensorsFile& f, const std::vector<mt_tensor_info>& table, size_t table_bytes,
+                const std::vector<Padded>& padded, uint8_t* arena, size_t arena_bytes, std::string& err) {
+    if (table_bytes > arena_bytes) {
+        err = "checkpoint: arena buffer smaller than the table's arena";
         return false;
     }
     memset(arena, 0, arena_bytes);
@@ -321,6 +325,24 @@ bool fill_arena(const SafeTensorsFile& f, const mt_model_config& cfg, bool embed
     for (const mt_tensor_info& t : table) {
         const std::vector<std::string> src = sources(t.name);
         uint8_t* dst = arena + t.offset;
+        const Padded* pad = nullptr;
+        for (const Padded& p : padded)
+            if (p.name == t.name) pad = &p;
+        if (pad) {
+            const Entry* e = f.find(pad->name);
+            if (!e) { err = "missing tensor " + pad->name; return false; }
+            if (e->dtype != "BF16" || e->shape.size() != 2 || e->shape[0] != pad->rows || e->shape[1] != pad->stored ||
+                e->end - e->begin != e->count() * 2) {
+                snprintf(buf, sizeof(buf), "bad checkpoint: %s is %s [%lld, %lld], expected BF16 [%lld, %lld]",
+                         pad->name.c_str(), e->dtype.c_str(), e->shape.size() > 0 ? e->shape[0] : -1LL,
+                         e->shape.size() > 1 ? e->shape[1] : -1LL, pad->rows, pad->stored);
+                err = buf;
+                return false;
+            }
+            for (long long r = 0; r < pad->rows; r++)
+                memcpy(dst + (size_t)r * pad->padded * 2, f.bytes(*e) + (size_t)r * pad->stored * 2, (size_t)pad->stored * 2);
+            continue;
+        }
         if (t.dtype == MT_DTYPE_BF16) {
             long long total = 0;
             for (const std::string& s : src) {
@@ -381,6 +403,27 @@ bool fill_arena(const SafeTensorsFile& f, const mt_model_config& cfg, bool embed
     return true;
 }
 
+bool fill_arena(const SafeTensorsFile& f, const mt_model_config& cfg, bool embeddings, uint8_t* arena,
+                size_t arena_bytes, std::string& err) {
+    const int n = mt_model_tensors(&cfg, 0, embeddings ? 1 : 0, nullptr, 0);
+    std::vector<mt_tensor_info> table((size_t)n);
+    mt_model_tensors(&cfg, 0, embeddings ? 1 : 0, table.data(), n);
+    return fill_table(f, table, mt_model_arena_bytes(&cfg, embeddings ? 1 : 0), {}, arena, arena_bytes, err);
+}
+
+bool fill_encoder_arena(const SafeTensorsFile& f, const mt_model_config& cfg, uint8_t* arena, size_t arena_bytes,
+                        std::string& err) {
+    const int n = mt_encoder_tensors(&cfg, 0, nullptr, 0);
+    std::vector<mt_tensor_info> table((size_t)n);
+    mt_encoder_tensors(&cfg, 0, table.data(), n);
+    Padded fc1;
+    fc1.name = "audio.encoder.fc1.weight";
+    fc1.rows = cfg.vae.hidden;
+    fc1.stored = cfg.hop;
+    fc1.padded = (cfg.hop + 63) & ~63;
+    return fill_table(f, table, mt_encoder_arena_bytes(&cfg), {fc1}, arena, arena_bytes, err);
+}
+
 }  // namespace
 
 }  // namespace mt
@@ -400,6 +443,59 @@ mt_status mt_checkpoint_fill_arena(const char* path, const mt_model_config* cfg,
     std::string msg;
     if (!mt::fill_arena(f, *cfg, with_embeddings != 0, static_cast<uint8_t*>(host_arena), arena_bytes, msg))
         return report(MT_ERR_CHECKPOINT, msg);
+    return MT_OK;
+}
+
+mt_status mt_checkpoint_fill_encoder_arena(const char* path, const mt_model_config* cfg, void* host_arena,
+                                           size_t arena_bytes, char* err, size_t err_len) {
+    if (err && err_len) err[0] = 0;
+    auto report = [&](mt_status st, const std::string& msg) {
+        if (err && err_len) snprintf(err, err_len, "%s", msg.c_str());
+        return st;
+    };
+    if (!path || !cfg || !host_arena) return report(MT_ERR_ARG, "mt_checkpoint_fill_encoder_arena: null argument");
+    mt::SafeTensorsFile f;
+    if (!f.open_file(path)) return report(MT_ERR_CHECKPOINT, f.err);
+    std::string msg;
+    if (!mt::fill_encoder_arena(f, *cfg, static_cast<uint8_t*>(host_arena), arena_bytes, msg))
+        return report(MT_ERR_CHECKPOINT, msg);
+    return MT_OK;
+}
+
+mt_status mt_encoder_load_safetensors(mt_ctx* ctx, const mt_model_config* cfg, const char* path, mt_encoder** out) {
+    if (!ctx) return MT_ERR_ARG;
+    MT_REQUIRE(ctx, cfg && path && out, MT_ERR_ARG, "mt_encoder_load_safetensors: null argument");
+    *out = nullptr;
+    const size_t bytes = mt_encoder_arena_bytes(cfg);
+    void* host = nullptr;
+    if (cudaMallocHost(&host, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return mt::fail(ctx, MT_ERR_NOMEM, "mt_encoder_load_safetensors: %zu bytes of pinned host memory", bytes);
+    }
+    std::vector<char> msg(512);
+    mt_status st = mt_checkpoint_fill_encoder_arena(path, cfg, host, bytes, msg.data(), msg.size());
+    if (st != MT_OK) {
+        cudaFreeHost(host);
+        return mt::fail(ctx, st, "%s", msg.data());
+    }
+    void* dev = nullptr;
+    if (cudaMalloc(&dev, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFreeHost(host);
+        return mt::fail(ctx, MT_ERR_NOMEM, "mt_encoder_load_safetensors: %zu bytes of device memory", bytes);
+    }
+    const cudaError_t ce = cudaMemcpy(dev, host, bytes, cudaMemcpyHostToDevice);
+    cudaFreeHost(host);
+    if (ce != cudaSuccess) {
+        cudaFree(dev);
+        return mt::fail(ctx, MT_ERR_CUDA, "mt_encoder_load_safetensors: copy to the device: %s", cudaGetErrorString(ce));
+    }
+    st = mt_encoder_create_from_arena(ctx, cfg, dev, out);
+    if (st != MT_OK) {
+        cudaFree(dev);
+        return st;
+    }
+    mt::encoder_own_arena(*out);
     return MT_OK;
 }
 

@@ -30,6 +30,9 @@ enum : unsigned int { DEV_OK = 0, DEV_TIMEOUT = 1, DEV_BAD_ARG = 2 };
 mt_status fail(mt_ctx* ctx, mt_status code, const char* fmt, ...);
 // Hands a model's arena (from mt_model_create_from_arena) to the model: mt_model_destroy frees it.
 void model_own_arena(mt_model* m);
+void encoder_own_arena(mt_encoder* e);
+mt_ctx* encoder_ctx(const mt_encoder* e);
+int encoder_latent_dim(const mt_encoder* e);
 mt_status check_launch(mt_ctx* ctx, const char* what);
 // Returns a device buffer of at least `bytes` owned by ctx. Grows (synchronising `stream` first)
 // when too small.

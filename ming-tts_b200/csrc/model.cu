@@ -110,6 +110,38 @@ std::vector<mt_tensor_info> table(const mt_model_config& c, uint64_t seed, bool 
     return b.list;
 }
 
+// VAEEncoderWeights (Weights.swift:229-262): frame projections, the encoder stack (the decoder's
+// dimensions), the 4-layer patch aggregator with its cls row, and the posterior head.
+constexpr int kEncoderAggLayers = 4, kEncoderPatch = 4, kEncoderMaxFrames = 1600;
+int encoder_padded_frame(const mt_model_config& c) { return (c.hop + 63) & ~63; }
+mt_qwen_config encoder_agg_config(const mt_model_config& c) {
+    mt_qwen_config a = c.vae;
+    a.layers = kEncoderAggLayers;
+    return a;
+}
+
+std::vector<mt_tensor_info> encoder_table(const mt_model_config& c, uint64_t seed) {
+    Builder b(seed);
+    const std::string e = "audio.encoder";
+    const size_t h = c.vae.hidden;
+    b.bf(e + ".fc1.weight", h * (size_t)encoder_padded_frame(c));
+    b.bf(e + ".fc2.weight", h * h);
+    b.bf(e + ".fc2.bias", h);
+    add_qwen(b, e + ".encoder", c.vae);
+    add_qwen(b, e + ".aggregator", encoder_agg_config(c));
+    b.add(e + ".cls_embed", h, MT_DTYPE_F32, MT_INIT_NORMAL);
+    b.bf(e + ".fc3.weight", 2 * (size_t)c.latent_dim * h);
+    b.bf(e + ".fc3.bias", 2 * (size_t)c.latent_dim);
+    return b.list;
+}
+
+size_t table_bytes(const std::vector<mt_tensor_info>& t) {
+    if (t.empty()) return 0;
+    const auto& last = t.back();
+    const size_t bytes = last.numel * (last.dtype == MT_DTYPE_BF16 ? 2 : 4);
+    return last.offset + ((bytes + 255) & ~size_t(255));
+}
+
 // Fills fp32 tensors of the table on the device: inv_freq, Hann window, N(0, std) fp32 values
 // (bf16-representable, same stream as the bf16 tensors).
 __global__ void fill_f32_kernel(float* out, size_t n, int init, uint64_t seed, float std) {
@@ -156,13 +188,35 @@ struct mt_model {
     mt_model_weights w{};
 };
 
+struct mt_encoder {
+    mt_ctx* ctx = nullptr;
+    mt_model_config cfg{};
+    std::vector<mt_tensor_info> tensors;
+    uint8_t* arena = nullptr;
+    size_t arena_bytes = 0;
+    bool owns_arena = false;
+    std::vector<mt_qwen_layer> stack_layers, agg_layers;
+    mt_encoder_weights w{};
+};
+
 namespace mt {
 void model_own_arena(mt_model* m) {
     if (m) m->owns_arena = true;
 }
+void encoder_own_arena(mt_encoder* e) {
+    if (e) e->owns_arena = true;
+}
+mt_ctx* encoder_ctx(const mt_encoder* e) { return e ? e->ctx : nullptr; }
+int encoder_latent_dim(const mt_encoder* e) { return e ? e->cfg.latent_dim : 0; }
 }  // namespace mt
 
 namespace {
+
+template <typename T>
+const T* at(mt_encoder* m, const std::string& name) {
+    const mt_tensor_info* i = find(m->tensors, name);
+    return i ? reinterpret_cast<const T*>(m->arena + i->offset) : nullptr;
+}
 
 template <typename T>
 const T* at(mt_model* m, const std::string& name) {
@@ -170,7 +224,8 @@ const T* at(mt_model* m, const std::string& name) {
     return i ? reinterpret_cast<const T*>(m->arena + i->offset) : nullptr;
 }
 
-void bind_qwen(mt_model* m, const std::string& prefix, const mt_qwen_config& c, std::vector<mt_qwen_layer>& layers,
+template <typename M>
+void bind_qwen(M* m, const std::string& prefix, const mt_qwen_config& c, std::vector<mt_qwen_layer>& layers,
                mt_qwen_weights& w) {
     layers.resize(c.layers);
     for (int l = 0; l < c.layers; l++) {
@@ -242,6 +297,46 @@ void bind(mt_model* m) {
     m->w.vae_head_b = at<mt_bf16>(m, v + ".head.out.bias");
     m->w.vae_window = at<float>(m, v + ".head.istft.window");
     m->w.embed_tokens = at<mt_bf16>(m, "model.model.embed_tokens.weight");
+}
+
+void bind_encoder(mt_encoder* e) {
+    const mt_model_config& c = e->cfg;
+    const std::string p = "audio.encoder";
+    e->w.frame = c.hop;
+    e->w.padded_frame = encoder_padded_frame(c);
+    e->w.patch = kEncoderPatch;
+    e->w.max_frames = kEncoderMaxFrames;
+    e->w.fc1_w = at<mt_bf16>(e, p + ".fc1.weight");
+    e->w.fc2_w = at<mt_bf16>(e, p + ".fc2.weight");
+    e->w.fc2_b = at<mt_bf16>(e, p + ".fc2.bias");
+    bind_qwen(e, p + ".encoder", c.vae, e->stack_layers, e->w.stack);
+    bind_qwen(e, p + ".aggregator", encoder_agg_config(c), e->agg_layers, e->w.aggregator);
+    e->w.cls = at<float>(e, p + ".cls_embed");
+    e->w.fc3_w = at<mt_bf16>(e, p + ".fc3.weight");
+    e->w.fc3_b = at<mt_bf16>(e, p + ".fc3.bias");
+}
+
+// Random fill of a table's tensors in `arena` (see mt_model_create_random).
+cudaError_t fill_random(mt_ctx* ctx, const std::vector<mt_tensor_info>& tensors, uint8_t* arena) {
+    for (const auto& t : tensors) {
+        void* p = arena + t.offset;
+        const unsigned blocks = (unsigned)std::min<size_t>((t.numel + 255) / 256, (size_t)ctx->sm_count * 8);
+        if (t.dtype == MT_DTYPE_BF16) {
+            if (t.init == MT_INIT_ONES) fill_bf16_ones_kernel<<<blocks, 256>>>(static_cast<uint16_t*>(p), t.numel);
+            else mt_randn_bf16(ctx, nullptr, static_cast<mt_bf16*>(p), t.numel, t.seed, t.std);
+        } else if (t.init == MT_INIT_NORMAL) {
+            // bf16-representable fp32 values: draw as bf16 into a temporary, widen into the slot.
+            uint16_t* tmp = nullptr;
+            cudaMalloc(&tmp, t.numel * 2);
+            mt_randn_bf16(ctx, nullptr, tmp, t.numel, t.seed, t.std);
+            bf16_to_f32_kernel<<<blocks, 256>>>(tmp, static_cast<float*>(p), t.numel);
+            cudaDeviceSynchronize();
+            cudaFree(tmp);
+        } else {
+            fill_f32_kernel<<<blocks, 256>>>(static_cast<float*>(p), t.numel, t.init, t.seed, t.std);
+        }
+    }
+    return cudaDeviceSynchronize();
 }
 
 mt_status check_config(mt_ctx* ctx, const mt_model_config& c) {
@@ -317,25 +412,7 @@ mt_status mt_model_create_random(mt_ctx* ctx, const mt_model_config* cfg, uint64
         return fail(ctx, MT_ERR_NOMEM, "model arena of %zu bytes: %s", m->arena_bytes, cudaGetErrorString(e));
     }
     m->owns_arena = true;
-    for (const auto& t : m->tensors) {
-        void* p = m->arena + t.offset;
-        const unsigned blocks = (unsigned)std::min<size_t>((t.numel + 255) / 256, (size_t)ctx->sm_count * 8);
-        if (t.dtype == MT_DTYPE_BF16) {
-            if (t.init == MT_INIT_ONES) fill_bf16_ones_kernel<<<blocks, 256>>>(static_cast<uint16_t*>(p), t.numel);
-            else mt_randn_bf16(ctx, nullptr, static_cast<mt_bf16*>(p), t.numel, t.seed, t.std);
-        } else if (t.init == MT_INIT_NORMAL) {
-            // bf16-representable fp32 values: draw as bf16 into the tail of the slot, widen in place.
-            uint16_t* tmp = nullptr;
-            cudaMalloc(&tmp, t.numel * 2);
-            mt_randn_bf16(ctx, nullptr, tmp, t.numel, t.seed, t.std);
-            bf16_to_f32_kernel<<<blocks, 256>>>(tmp, static_cast<float*>(p), t.numel);
-            cudaDeviceSynchronize();
-            cudaFree(tmp);
-        } else {
-            fill_f32_kernel<<<blocks, 256>>>(static_cast<float*>(p), t.numel, t.init, t.seed, t.std);
-        }
-    }
-    e = cudaDeviceSynchronize();
+    e = fill_random(ctx, m->tensors, m->arena);
     if (e != cudaSuccess) {
         cudaFree(m->arena);
         delete m;
@@ -380,6 +457,84 @@ void mt_model_destroy(mt_model* m) {
     if (!m) return;
     if (m->owns_arena && m->arena) cudaFree(m->arena);
     delete m;
+}
+
+int mt_encoder_tensors(const mt_model_config* cfg, uint64_t seed, mt_tensor_info* out, int cap) {
+    if (!cfg) return -1;
+    auto t = encoder_table(*cfg, seed);
+    if (out)
+        for (int i = 0; i < (int)t.size() && i < cap; i++) out[i] = t[i];
+    return (int)t.size();
+}
+
+size_t mt_encoder_arena_bytes(const mt_model_config* cfg) { return cfg ? table_bytes(encoder_table(*cfg, 0)) : 0; }
+
+mt_status mt_encoder_create_random(mt_ctx* ctx, const mt_model_config* cfg, uint64_t seed, mt_encoder** out) {
+    MT_REQUIRE(ctx, ctx && cfg && out, MT_ERR_ARG, "mt_encoder_create_random: null argument");
+    *out = nullptr;
+    mt_status st = check_config(ctx, *cfg);
+    if (st != MT_OK) return st;
+    mt_encoder* e = new mt_encoder();
+    e->ctx = ctx;
+    e->cfg = *cfg;
+    e->tensors = encoder_table(*cfg, seed);
+    e->arena_bytes = table_bytes(e->tensors);
+    cudaError_t err = cudaMalloc(&e->arena, e->arena_bytes);
+    if (err != cudaSuccess) {
+        delete e;
+        return fail(ctx, MT_ERR_NOMEM, "encoder arena of %zu bytes: %s", e->arena_bytes, cudaGetErrorString(err));
+    }
+    e->owns_arena = true;
+    err = fill_random(ctx, e->tensors, e->arena);
+    if (err == cudaSuccess) {  // fc1 columns past the frame are zero, as WeightArena.paddedLinear stores them
+        const int pf = encoder_padded_frame(*cfg), f = cfg->hop;
+        if (pf > f)
+            err = cudaMemset2D(e->arena + e->tensors[0].offset + (size_t)f * 2, (size_t)pf * 2, 0, (size_t)(pf - f) * 2,
+                               (size_t)cfg->vae.hidden);
+        if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    }
+    if (err != cudaSuccess) {
+        cudaFree(e->arena);
+        delete e;
+        return fail(ctx, MT_ERR_CUDA, "encoder init: %s", cudaGetErrorString(err));
+    }
+    bind_encoder(e);
+    *out = e;
+    return MT_OK;
+}
+
+mt_status mt_encoder_create_from_arena(mt_ctx* ctx, const mt_model_config* cfg, void* device_arena, mt_encoder** out) {
+    MT_REQUIRE(ctx, ctx && cfg && device_arena && out, MT_ERR_ARG, "mt_encoder_create_from_arena: null argument");
+    MT_REQUIRE(ctx, ((uintptr_t)device_arena & 255u) == 0, MT_ERR_ARG,
+               "mt_encoder_create_from_arena: arena needs 256-byte alignment");
+    *out = nullptr;
+    mt_status st = check_config(ctx, *cfg);
+    if (st != MT_OK) return st;
+    mt_encoder* e = new mt_encoder();
+    e->ctx = ctx;
+    e->cfg = *cfg;
+    e->tensors = encoder_table(*cfg, 0);
+    e->arena_bytes = table_bytes(e->tensors);
+    e->arena = static_cast<uint8_t*>(device_arena);
+    e->owns_arena = false;
+    bind_encoder(e);
+    *out = e;
+    return MT_OK;
+}
+
+const mt_encoder_weights* mt_encoder_get_weights(const mt_encoder* e) { return e ? &e->w : nullptr; }
+
+mt_status mt_encoder_arena(const mt_encoder* e, void** ptr, size_t* bytes) {
+    if (!e || !ptr || !bytes) return MT_ERR_ARG;
+    *ptr = e->arena;
+    *bytes = e->arena_bytes;
+    return MT_OK;
+}
+
+void mt_encoder_destroy(mt_encoder* e) {
+    if (!e) return;
+    if (e->owns_arena && e->arena) cudaFree(e->arena);
+    delete e;
 }
 
 }  // extern "C"

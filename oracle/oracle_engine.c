@@ -310,3 +310,73 @@ int or_llm_decode(const mt_qwen_weights* w, float* cache, int cap, int length, c
     free(s.mlp);
     return 0;
 }
+
+/* bf16Rounded (VAEEncoder.swift:110-114). */
+static float bf16_rounded(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+    float r;
+    memcpy(&r, &u, 4);
+    return r;
+}
+
+int or_vae_encode(const mt_model_config* cfg, const mt_encoder_weights* w, const float* samples, long count,
+                  float* mean, float* std_out) {
+    const int frame = w->frame, patch = w->patch, pf = w->padded_frame, H = w->stack.cfg.hidden;
+    const int L = cfg->latent_dim;
+    if (count <= 0 || count % ((long)frame * patch) != 0) return -1;
+    const int frames = (int)(count / frame), latents = frames / patch, prow = latents * (patch + 1);
+    float* fr = ALLOC((size_t)frames * pf);
+    float* proj = ALLOC((size_t)frames * H);
+    float* x = ALLOC((size_t)frames * H);
+    float* normed = ALLOC((size_t)frames * H);
+    float* patches = ALLOC((size_t)prow * H);
+    float* pnormed = ALLOC((size_t)prow * H);
+    float* cls_rows = ALLOC((size_t)latents * H);
+    float* post = ALLOC((size_t)latents * 2 * L);
+    for (int f = 0; f < frames; f++)
+        for (int i = 0; i < frame; i++) fr[(size_t)f * pf + i] = bf16_rounded(samples[(size_t)f * frame + i]);
+    or_linear(fr, pf, frames, w->fc1_w, NULL, NULL, H, pf, proj, H, 0);
+    or_linear(proj, H, frames, w->fc2_w, NULL, w->fc2_b, H, H, x, H, MT_LINEAR_BIAS);
+    qwen_state st;
+    qwen_init(&st, &w->stack, frames, frames);
+    qwen_forward(&st, x, frames, frames, normed, NULL, NULL);
+    qwen_free(&st);
+    for (int p = 0; p < latents; p++) {  /* [patch frame rows | cls] (VAEEncoder.swift:88-92) */
+        memcpy(patches + (size_t)p * (patch + 1) * H, normed + (size_t)p * patch * H, sizeof(float) * (size_t)patch * H);
+        memcpy(patches + ((size_t)p * (patch + 1) + patch) * H, w->cls, sizeof(float) * (size_t)H);
+    }
+    qwen_state ag;
+    qwen_init(&ag, &w->aggregator, prow, prow);
+    qwen_forward(&ag, patches, prow, prow, pnormed, NULL, NULL);
+    qwen_free(&ag);
+    for (int p = 0; p < latents; p++)
+        memcpy(cls_rows + (size_t)p * H, pnormed + ((size_t)p * (patch + 1) + patch) * H, sizeof(float) * (size_t)H);
+    or_linear(cls_rows, H, latents, w->fc3_w, NULL, w->fc3_b, 2 * L, H, post, 2 * L, MT_LINEAR_BIAS);
+    for (int p = 0; p < latents; p++)
+        for (int i = 0; i < L; i++) {
+            const float s = post[(size_t)p * 2 * L + L + i];
+            mean[(size_t)p * L + i] = post[(size_t)p * 2 * L + i];
+            std_out[(size_t)p * L + i] = (s > 20.0f ? s : log1pf(expf(s))) + 1e-4f;  /* softplus + 1e-4 */
+        }
+    free(fr); free(proj); free(x); free(normed); free(patches); free(pnormed); free(cls_rows); free(post);
+    return 0;
+}
+
+int or_aggregate_latents(const mt_model_config* cfg, const mt_model_weights* w, const float* latents, int count,
+                         float* rows) {
+    const int h = cfg->agg.hidden, L = cfg->latent_dim, od = cfg->agg.out_dim;
+    float* x = ALLOC((size_t)2 * count * h);
+    float* out = ALLOC((size_t)2 * count * od);
+    for (int p = 0; p < count; p++) memcpy(x + (size_t)2 * p * h, w->agg_cls, sizeof(float) * (size_t)h);
+    or_linear(latents, L, count, w->agg_x_w, NULL, w->agg_x_b, h, L, x + h, 2 * h, MT_LINEAR_BIAS);
+    dit_state ds;
+    dit_init(&ds, &w->agg, 2 * count);
+    dit_forward(&ds, x, count, 2, 2 * count, out);
+    dit_free(&ds);
+    for (int p = 0; p < count; p++) memcpy(rows + (size_t)p * od, out + (size_t)2 * p * od, sizeof(float) * (size_t)od);
+    free(x);
+    free(out);
+    return 0;
+}

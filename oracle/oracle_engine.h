@@ -42,6 +42,13 @@ typedef struct {
 int or_generate(const mt_model_config* cfg, const mt_model_weights* w, or_generate_io* io);
 int or_llm_decode(const mt_qwen_weights* w, float* cache, int cap, int length, const float* x_in, int rows,
                   float* z_out);
+/* VAEEncoder.encode (VAEEncoder.swift:56-107): count samples (a multiple of frame * patch) ->
+ * mean/std [count / (frame * patch), latent]. Returns 0, or -1 on a bad count. */
+int or_vae_encode(const mt_model_config* cfg, const mt_encoder_weights* w, const float* samples, long count,
+                  float* mean, float* std_out);
+/* MingEngine.aggregate (Engine.swift:236-256): count latents [count, latent] -> rows [count, llm.hidden]. */
+int or_aggregate_latents(const mt_model_config* cfg, const mt_model_weights* w, const float* latents, int count,
+                         float* rows);
 
 #ifdef __cplusplus
 }

@@ -17,7 +17,7 @@ import safetensors_io as sio
 def qkv_parts(name: str, numel: int, cfg):
     """The checkpoint tensors a table entry is gathered from, with their element counts."""
     if ".self_attn.qkv_proj." in name:
-        qc = cfg.vae if name.startswith("audio.decoder") else cfg.llm
+        qc = cfg.vae if name.startswith("audio.") else cfg.llm
         unit = numel // (qc.heads + 2 * qc.kv_heads)
         return [(name.replace(".qkv_proj.", f".{p}_proj."), unit * c)
                 for p, c in (("q", qc.heads), ("k", qc.kv_heads), ("v", qc.kv_heads))]
@@ -54,6 +54,39 @@ def build_checkpoint(mt, cfg, seed=0, with_embeddings=True, f32_as_bf16=("linear
             arena[t.offset:t.offset + raw.size] = raw
     # a tensor the per-step path does not use (the VAE encoder's) is ignored
     tensors["audio.encoder.fc1.weight"] = ("BF16", [4, 8], sio.bf16_bits(rng, 32).tobytes())
+    return tensors, arena
+
+
+def build_encoder_checkpoint(mt, cfg, seed=0):
+    """(tensors for the file, expected host encoder arena): fc1 stored [hidden, frame] as in the
+    checkpoint, the arena holding it [hidden, padded_frame] with zero columns."""
+    rng = np.random.default_rng(seed)
+    table = mt.encoder_tensor_table(cfg, 0)
+    arena = np.zeros(mt.lib().mt_encoder_arena_bytes(mt.ctypes.byref(cfg)), np.uint8)
+    tensors = {}
+    h, frame, padded = cfg.vae.hidden, cfg.hop, (cfg.hop + 63) // 64 * 64
+    for t in table:
+        name = t.name.decode()
+        if name == "audio.encoder.fc1.weight":
+            bits = sio.bf16_bits(rng, h * frame).reshape(h, frame)
+            tensors[name] = ("BF16", [h, frame], bits.tobytes())
+            full = np.zeros((h, padded), np.uint16)
+            full[:, :frame] = bits
+            raw = full.view(np.uint8).ravel()
+            arena[t.offset:t.offset + raw.size] = raw
+        elif t.dtype == mt.MT_DTYPE_BF16:
+            parts = []
+            for src, n in qkv_parts(name, t.numel, cfg):
+                bits = sio.bf16_bits(rng, n)
+                tensors[src] = ("BF16", [n], bits.tobytes())
+                parts.append(bits)
+            raw = np.concatenate(parts).view(np.uint8)
+            arena[t.offset:t.offset + raw.size] = raw
+        else:
+            vals = (rng.standard_normal(t.numel) * 0.5).astype(np.float32)
+            tensors[name] = ("F32", [t.numel], vals.tobytes())
+            raw = vals.view(np.uint8)
+            arena[t.offset:t.offset + raw.size] = raw
     return tensors, arena
 
 
@@ -169,3 +202,29 @@ def test_model_load_safetensors_device_arena(mt, ctx, small, tmp_path):
         model.close()
     with pytest.raises(mt.CheckpointError):
         mt.Model.load(ctx, tmp_path / "absent.safetensors", small)
+
+
+def test_encoder_fill_arena_pads_fc1(mt, small, tmp_path):
+    for cfg in (small, mt.default_config()):
+        if cfg is not small:  # the full encoder table only: names, offsets and fc1 padding of 882 -> 896
+            t = {x.name.decode(): x for x in mt.encoder_tensor_table(cfg, 0)}
+            assert t["audio.encoder.fc1.weight"].numel == 896 * 896
+            assert t["audio.encoder.fc3.weight"].numel == 128 * 896
+            assert "audio.encoder.aggregator.layers.3.mlp.down_proj.weight" in t
+            assert "audio.encoder.aggregator.layers.4.mlp.down_proj.weight" not in t
+            assert "audio.encoder.encoder.layers.23.self_attn.qkv_proj.bias" in t
+            continue
+        tensors, want = build_encoder_checkpoint(mt, cfg, seed=4)
+        sio.write(tmp_path / "m.safetensors", tensors)
+        got = mt.checkpoint_fill_encoder_arena(tmp_path / "m.safetensors", cfg)
+        assert np.array_equal(got, want)
+
+
+def test_encoder_fc1_shape_is_checked(mt, small, tmp_path):
+    tensors, _ = build_encoder_checkpoint(mt, small, seed=4)
+    _, shape, raw = tensors["audio.encoder.fc1.weight"]
+    tensors["audio.encoder.fc1.weight"] = ("BF16", [shape[1], shape[0]], raw)
+    sio.write(tmp_path / "m.safetensors", tensors)
+    with pytest.raises(mt.CheckpointError) as e:
+        mt.checkpoint_fill_encoder_arena(tmp_path / "m.safetensors", small)
+    assert "audio.encoder.fc1.weight is BF16" in str(e.value)
