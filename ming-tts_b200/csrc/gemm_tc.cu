@@ -422,6 +422,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer: one MMA of N = 2 bn per 16-wide K step per weight matrix
             const uint32_t idesc = idesc_bf16(TC_BM, 2 * e.bn);
+            const uint64_t a_desc0 = sw128_desc(smem_u32(base));
+            const uint64_t b_desc0 = sw128_desc(smem_u32(base) + w_bytes * (GATED ? 2 : 1));
             int s = 0, tl = 0;
             uint32_t ph = 0;
             for (int t = blockIdx.x; t < tiles_total && !*abort; t += gridDim.x, tl++) {
@@ -435,19 +437,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const int na = KA == 1 ? 1 : min(KA, tc.kb_end - kb);
                     if (!mbar_wait(&full_bar[s], ph, e.status, 3, abort)) { ok = false; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t sa = smem_u32(base + (size_t)s * stage_bytes);
+                    // Descriptors advance by offsets in their 16-byte address field (shared memory
+                    // < 256 KB, so the field never carries into the other bits).
+                    const uint64_t sd = (uint64_t)(((uint32_t)s * stage_bytes) >> 4);
 #pragma unroll
                     for (int a = 0; a < KA; a++) {
                         if (KA > 1 && a >= na) break;
-                        const uint32_t wa = sa + a * atom_bytes;
-                        const uint32_t xa = wa + w_bytes * (GATED ? 2 : 1);
+                        const uint64_t ad = a_desc0 + sd + (uint64_t)((a * atom_bytes) >> 4);
+                        const uint64_t bd = b_desc0 + sd + (uint64_t)((a * atom_bytes) >> 4);
 #pragma unroll
-                        for (int kk = 0; kk < TC_BK / 16; kk++) {
-                            const uint32_t off = kk * 32;  // 16 bf16 along K inside the swizzle span
-                            const uint64_t bx = sw128_desc(xa + off);
+                        for (int kk = 0; kk < TC_BK / 16; kk++) {  // 16 bf16 along K = 32 bytes = 2 units
                             const uint32_t accum = (i > 0 || a > 0 || kk > 0) ? 1u : 0u;
-                            mma_bf16(acc, sw128_desc(wa + off), bx, idesc, accum);
-                            if (GATED) mma_bf16(acc + 2 * e.bn, sw128_desc(wa + w_bytes + off), bx, idesc, accum);
+                            mma_bf16(acc, ad + 2 * kk, bd + 2 * kk, idesc, accum);
+                            if (GATED) mma_bf16(acc + 2 * e.bn, ad + (w_bytes >> 4) + 2 * kk, bd + 2 * kk, idesc, accum);
                         }
                     }
                     mma_commit(&empty_bar[s]);

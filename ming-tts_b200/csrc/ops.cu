@@ -17,11 +17,19 @@ constexpr int RMS_THREADS = 128;
 constexpr int RMS_MAXV = 8;  // float4 per thread: width <= 4096
 
 __global__ void __launch_bounds__(RMS_THREADS) rmsnorm_kernel(RmsArgs a) {
-    pdl_wait();
-    pdl_launch();
     __shared__ float part[RMS_THREADS / 32];
     const int row = blockIdx.x;
     const int n4 = a.width >> 2;
+    // The gains are weights (never written by a kernel): fetched while the previous kernel drains.
+    const uint2* w = reinterpret_cast<const uint2*>(a.w);
+    uint2 wv[RMS_MAXV];
+#pragma unroll
+    for (int i = 0; i < RMS_MAXV; i++) {
+        const int c = threadIdx.x + i * RMS_THREADS;
+        wv[i] = c < n4 ? w[c] : make_uint2(0u, 0u);
+    }
+    pdl_wait();
+    pdl_launch();
     const float4* x = reinterpret_cast<const float4*>(a.x + (size_t)row * a.ldx);
     float4 v[RMS_MAXV];
     float ss = 0.f;
@@ -38,17 +46,15 @@ __global__ void __launch_bounds__(RMS_THREADS) rmsnorm_kernel(RmsArgs a) {
 #pragma unroll
     for (int w = 0; w < RMS_THREADS / 32; w++) tot += part[w];
     const float scale = rsqrtf(tot / (float)a.width + a.eps);
-    const uint2* w = reinterpret_cast<const uint2*>(a.w);
 #pragma unroll
     for (int i = 0; i < RMS_MAXV; i++) {
         const int c = threadIdx.x + i * RMS_THREADS;
         if (c >= n4) break;
-        const uint2 wv = w[c];
         float4 o;
-        o.x = v[i].x * scale * bf16_lo(wv.x);
-        o.y = v[i].y * scale * bf16_hi(wv.x);
-        o.z = v[i].z * scale * bf16_lo(wv.y);
-        o.w = v[i].w * scale * bf16_hi(wv.y);
+        o.x = v[i].x * scale * bf16_lo(wv[i].x);
+        o.y = v[i].y * scale * bf16_hi(wv[i].x);
+        o.z = v[i].z * scale * bf16_lo(wv[i].y);
+        o.w = v[i].w * scale * bf16_hi(wv[i].y);
         if (a.y) reinterpret_cast<float4*>(a.y + (size_t)row * a.ldy)[c] = o;
         if (a.y_hi) {
             uint32_t h01, l01, h23, l23;
