@@ -314,7 +314,7 @@ def run_reference(args, rank, world):
 METRIC = "audio-sec/sec of the Ming-3.0-tts-0.5B step loop (config 5 serving, per-GPU replicas)"
 # DRAM bytes (read + write) of one launch of the roofline GEMM, from the ncu capture summarised in
 # profiles/gemm_tc_flow_ff1_m384_n4096_k1024.md (dram__bytes_read.sum + dram__bytes_write.sum).
-ROOFLINE_TRAFFIC_BYTES = 10_003_712
+ROOFLINE_TRAFFIC_BYTES = 10_003_456
 
 
 def config_block(args):
