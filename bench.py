@@ -229,6 +229,26 @@ def time_gemv_pool(mt, ctx, n, k, m=2, pool_bytes=1 << 30, rounds=3):
 # ------------------------------------------------------------------------------------------------
 # CPU oracle runs (baseline)
 # ------------------------------------------------------------------------------------------------
+def time_to_first_audio(eng, requests, prompt, noise_host, ids_host, steps, world, reps=7):
+    """p50 time to the first non-empty PCM chunk through mt_engine_generate_stream (host ids and noise,
+    prefill, steps 0-2; the first chunk follows step 2). All requests of the batch receive their
+    first chunk in the same callback, so the batch's time is every request's time; the p50 is over
+    repeated calls and the max over ranks."""
+    samples = []
+    for _ in range(reps):
+        t_first = []
+        t0 = time.perf_counter()
+
+        def on_chunk(index, pcm):
+            if not t_first:
+                t_first.append(time.perf_counter())
+            return 0
+
+        eng.generate_stream(requests, prompt, noise_host, steps, on_chunk, ids_host=ids_host)
+        samples.append(t_first[0] - t0)
+    return dist_max(statistics.median(samples), world), reps
+
+
 def host_model(mt, oracle, cfg, seed):
     import numpy as np
     tensors = mt.tensor_table(cfg, seed)
@@ -435,6 +455,7 @@ def main():
     max_chunk = 4 * cfg.hop + (cfg.nfft - cfg.hop) // 2
     h2d = (ids_h.nbytes + noise_e.nbytes) / E
     d2h = (R * max_chunk * 4 * (E + 0.0) + R * 2 * 4 * E) / E
+    ttfa = time_to_first_audio(eng, R, T, noise_e, ids_h, min(E, 12), world)
 
     # ---- kernel roofline: the tcgen05 GEMM at the flow-DiT ff1 shape; decode GEMV (config 1) ----
     hbm_peak, bf16_peak, peak_kind = peaks()
@@ -464,6 +485,9 @@ def main():
                 "e2e": {"value": round(e2e_value, 2), "unit": "audio-s/s", "steps": E,
                         "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                         "includes": "ids+noise H2D, prefill, steps, flush, PCM+stop D2H (mt_engine_generate)"},
+                "ttfa_ms": {"p50": round(ttfa[0] * 1e3, 2), "calls": ttfa[1], "requests_per_call": R,
+                            "includes": "ids+noise H2D, prefill of all requests, steps 0-2, first PCM chunk D2H "
+                                        "(mt_engine_generate_stream callback)"},
                 "roofline": {"kernel": "gemm_tc_kernel (flow DiT ff1, GELU, hi/lo out)",
                              "shape": f"M={M} N={N} K={K}", "bound": "tensor", "achieved": round(achieved, 1),
                              "peak": bf16_peak, "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 4),

@@ -395,11 +395,21 @@ int mt_engine_step_kernels(const mt_engine* engine);
  * (the VAE decode runs concurrently on its own stream). */
 mt_status mt_engine_set_stage_timing(mt_engine* engine, int on);
 mt_status mt_engine_stage_ms(mt_engine* engine, float* ms4);
+/* The reference's stop rule for mt_engine_generate / mt_engine_generate_stream (MingEngine.generate,
+ * Engine.swift:347-355): when on, the host reads step n's stop logits before enqueuing step n + 1,
+ * a request meets the rule at its first step with p = 1/(1+exp(l0-l1)) > 0.5 and n > 3, and the
+ * generation ends after the step at which every request has met it, then flushes. For one request
+ * this is the reference's loop exactly; in a batch, requests that met the rule earlier keep
+ * generating until the last one does (their first such step is visible in stop_prob_host).
+ * mt_engine_steps_done gives the steps run. Off by default (the serving benchmark runs a fixed
+ * number of steps); the per-step host read costs one stream synchronisation per step. */
+mt_status mt_engine_set_stop_rule(mt_engine* engine, int on);
 /* End to end from host memory: copies embeds (or ids) and noise in, runs prefill, `steps` steps
  * and the flush, and copies every PCM chunk and stop probability out. pcm_host is [R, pcm_stride];
  * pcm_count receives the samples written per request (the same for all). The stop head is
- * evaluated every step; generation runs all `steps` (stop not obeyed). Uses staging the engine
- * allocated at creation (no allocation per call); returns when the last sample is in pcm_host. */
+ * evaluated every step; generation runs all `steps` unless mt_engine_set_stop_rule turned the
+ * stop rule on (then stop_prob_host is 0 past the steps run). Uses staging the engine allocated at
+ * creation (no allocation per call); returns when the last sample is in pcm_host. */
 mt_status mt_engine_generate(mt_engine* engine, void* stream, int requests, int prompt_rows, const float* embeds_host,
                              const int32_t* ids_host, const float* noise_host, int steps, float cfg, float* pcm_host,
                              long long pcm_stride, long long* pcm_count, float* stop_prob_host);

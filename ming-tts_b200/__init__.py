@@ -154,6 +154,7 @@ PROTOTYPES = {
     "mt_engine_steps_done": (c_int, [_P]),
     "mt_engine_step_kernels": (c_int, [_P]),
     "mt_engine_set_stage_timing": (c_int, [_P, c_int]),
+    "mt_engine_set_stop_rule": (c_int, [_P, c_int]),
     "mt_engine_stage_ms": (c_int, [_P, _P]),
     "mt_engine_generate": (c_int, [_P, _P, c_int, c_int, _P, _P, _P, c_int, c_float, _P, ctypes.c_longlong,
                                    POINTER(ctypes.c_longlong), _P]),
@@ -630,6 +631,14 @@ class Engine:
 
     def stage_timing(self, on: bool = True):
         self.ctx._check(lib().mt_engine_set_stage_timing(self._e, int(on)), "mt_engine_set_stage_timing")
+
+    def stop_rule(self, on: bool = True):
+        """mt_engine_set_stop_rule: generate/generate_stream end once every request has met
+        p > 0.5 with n > 3 (Engine.swift:347-355); steps_done() then gives the steps run."""
+        self.ctx._check(lib().mt_engine_set_stop_rule(self._e, int(on)), "mt_engine_set_stop_rule")
+
+    def steps_done(self) -> int:
+        return lib().mt_engine_steps_done(self._e)
 
     def stage_ms(self):
         """[llm, flow, agg, vae] GPU milliseconds of the last timed step."""

@@ -136,6 +136,7 @@ struct mt_engine {
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_in = nullptr, ev_out = nullptr;
     int step_kernels = 0;       // kernels of the last step
     bool time_stages = false;   // record per-stage events (eager steps only)
+    bool stop_rule = false;     // generate/generate_stream end once every request met the stop rule
     cudaEvent_t stage_ev[6] = {};  // A: start, after llm, after flow, after agg; B: decode start, end
     bool stage_valid = false;
     int graph_kernels = 0;      // kernels in the captured step graph
@@ -916,6 +917,12 @@ mt_status mt_engine_set_stage_timing(mt_engine* e, int on) {
     return MT_OK;
 }
 
+mt_status mt_engine_set_stop_rule(mt_engine* e, int on) {
+    if (!e) return MT_ERR_ARG;
+    e->stop_rule = on != 0;
+    return MT_OK;
+}
+
 mt_status mt_engine_stage_ms(mt_engine* e, float* ms4) {
     if (!e || !ms4) return MT_ERR_ARG;
     MT_REQUIRE(e->ctx, e->stage_valid, MT_ERR_STATE, "mt_engine_stage_ms: last step was not timed");
@@ -1004,6 +1011,10 @@ mt_status generate_loop(mt_engine* e, void* stream, int requests, int prompt_row
         total += count;
         return drain(counts.size(), false);
     };
+    // With the stop rule (MingEngine.generate, Engine.swift:347-355) the host reads each step's stop
+    // logits before enqueuing the next step, as the reference does; the batch ends after the step
+    // at which the last request has met p > 0.5 with n > 3 (a request keeps its first such step).
+    std::vector<char> met(e->stop_rule ? requests : 0, 0);
     int n = 0;
     for (; st == MT_OK && !cancelled && n < steps; n++) {
         int count = 0;
@@ -1012,7 +1023,24 @@ mt_status generate_loop(mt_engine* e, void* stream, int requests, int prompt_row
         cudaMemcpyAsync(e->stop_host + (size_t)n * requests * 2, e->stop, (size_t)requests * 2 * sizeof(float),
                         cudaMemcpyDeviceToHost, s);
         if (count > 0) st = emit(count);
+        if (st != MT_OK || !e->stop_rule) continue;
+        cudaError_t err = cudaStreamSynchronize(s);
+        if (err != cudaSuccess) {
+            st = fail(ctx, MT_ERR_CUDA, "%s: %s", who, cudaGetErrorString(err));
+            break;
+        }
+        int remaining = 0;
+        for (int r = 0; r < requests; r++) {
+            const float* l = e->stop_host + ((size_t)n * requests + r) * 2;
+            if (1.0f / (1.0f + expf(l[0] - l[1])) > 0.5f && n > 3) met[r] = 1;
+            remaining += !met[r];
+        }
+        if (remaining == 0) {
+            n++;
+            break;
+        }
     }
+    const int ran = n;
     while (st == MT_OK && !cancelled) {
         int count = 0;
         st = mt_engine_flush(e, stream, &count);
@@ -1030,7 +1058,8 @@ mt_status generate_loop(mt_engine* e, void* stream, int requests, int prompt_row
             for (int k = 0; k < steps; k++)
                 for (int r = 0; r < requests; r++) {
                     const float* l = e->stop_host + ((size_t)k * requests + r) * 2;
-                    stop_prob_host[(size_t)r * steps + k] = 1.0f / (1.0f + expf(l[0] - l[1]));  // Engine.swift:349
+                    stop_prob_host[(size_t)r * steps + k] =
+                        k < ran ? 1.0f / (1.0f + expf(l[0] - l[1])) : 0.0f;  // Engine.swift:349
                 }
     }
     return st;

@@ -24,7 +24,7 @@ def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-def oracle_generate(oracle, cfg, w_host, embeds, noise, steps, cfg_scale=2.0):
+def oracle_generate(oracle, cfg, w_host, embeds, noise, steps, cfg_scale=2.0, obey_stop=0):
     L, H, Hv = cfg.latent_dim, cfg.llm.hidden, cfg.vae.hidden
     T = embeds.shape[0]
     out = dict(stop=np.zeros((steps, 2), np.float32), z=np.zeros((steps, H), np.float32),
@@ -32,7 +32,7 @@ def oracle_generate(oracle, cfg, w_host, embeds, noise, steps, cfg_scale=2.0):
                vel0=np.zeros((cfg.flow_steps, 2, L), np.float32), vae_hidden=np.zeros((steps, 4, Hv), np.float32),
                pcm=np.zeros(4 * cfg.hop * (steps + 1), np.float32), chunks=np.zeros(steps + 2, np.int32))
     io = oracle.GenerateIO()
-    io.prompt_rows, io.embeds, io.steps, io.cfg, io.obey_stop = T, embeds.ctypes.data, steps, cfg_scale, 0
+    io.prompt_rows, io.embeds, io.steps, io.cfg, io.obey_stop = T, embeds.ctypes.data, steps, cfg_scale, obey_stop
     io.noise = noise.ctypes.data
     io.stop_logits, io.llm_hidden, io.latents = out["stop"].ctypes.data, out["z"].ctypes.data, out["latents"].ctypes.data
     io.agg_out, io.velocity0, io.vae_hidden = out["agg"].ctypes.data, out["vel0"].ctypes.data, out["vae_hidden"].ctypes.data
@@ -40,6 +40,7 @@ def oracle_generate(oracle, cfg, w_host, embeds, noise, steps, cfg_scale=2.0):
     assert oracle.lib().or_generate(ctypes.addressof(cfg), ctypes.addressof(w_host), ctypes.byref(io)) == 0
     out["pcm"] = out["pcm"][:io.pcm_count]
     out["chunks"] = out["chunks"][:io.chunks]
+    out["steps_run"], out["stopped"] = io.steps_run, io.stopped
     return out
 
 
@@ -202,6 +203,63 @@ def test_generate_stream_delivers_generate_chunks(ctx, mt, oracle):
     pcm2, _ = eng.generate(R, T, noise, steps, embeds_host=embeds)
     for r in range(R):
         assert rel_err(pcm2[r], pcm[r]) < 1e-4
+
+
+def pin_stop_bias(mt, model, l0, l1):
+    """Writes the stop head's bias (bf16 [2], exact for these values) on the device, so that the
+    stop probability 1/(1+exp(l0-l1)) sits far from 0.5 whatever the random stop weights give."""
+    import torch
+    base, _ = model.arena()
+    off = {t.name.decode(): t.offset for t in model.tensors()}["stop_head.bias"]
+    bits = (np.array([l0, l1], np.float32).view(np.uint32) >> 16).astype(np.uint16).view(np.int16)
+    mt.device_view(base + off, (2,), "int16").copy_(torch.from_numpy(bits))
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("R", [1, 2])
+def test_stop_rule_matches_reference_loop(ctx, mt, oracle, R):
+    """mt_engine_set_stop_rule against the oracle's loop with the stop obeyed (Engine.swift:347-367):
+    with p pinned near 1 every request meets the rule at n = 4, so 5 steps run and the flush follows;
+    the waveform, emission counts and steps run match the oracle's, through both host APIs."""
+    cfg = mt.small_config()
+    model = mt.Model(ctx, cfg, seed=13)
+    pin_stop_bias(mt, model, -16.0, 16.0)
+    host = model.arena_to_host()
+    w_host, keep = mt.weights_struct(cfg, host.ctypes.data, model.tensors())
+    T, steps = 4, 9
+    rs = np.random.default_rng(13)
+    embeds = (0.5 * rs.standard_normal((R, T, cfg.llm.hidden))).astype(np.float32)
+    noise = rs.standard_normal((R, steps, cfg.latent_dim)).astype(np.float32)
+    eng = mt.Engine(ctx, model, R, T, steps)
+    eng.stop_rule(True)
+    pcm, stop = eng.generate(R, T, noise, steps, embeds_host=embeds)
+    assert eng.steps_done() == 5
+    assert np.all(stop[:, :5] > 0.5) and np.all(stop[:, 5:] == 0)
+    chunks = []
+    count, _ = eng.generate_stream(R, T, noise, steps, lambda i, b: chunks.append(b), embeds_host=embeds)
+    assert eng.steps_done() == 5 and count == pcm.shape[1]
+    for r in range(R):
+        want = oracle_generate(oracle, cfg, w_host, np.ascontiguousarray(embeds[r]), np.ascontiguousarray(noise[r]),
+                               steps, obey_stop=1)
+        assert want["stopped"] == 1 and want["steps_run"] == 5
+        assert [b.shape[1] for b in chunks] == list(want["chunks"])
+        assert pcm[r].shape == want["pcm"].shape and cosine(pcm[r], want["pcm"]) >= 0.999
+        streamed = np.concatenate([b[r] for b in chunks])
+        assert rel_err(streamed, pcm[r]) < 1e-4
+    # p pinned near 0: the rule never holds and every step runs, as without the rule
+    eng.close()
+    pin_stop_bias(mt, model, 16.0, -16.0)
+    eng = mt.Engine(ctx, model, R, T, steps)
+    eng.stop_rule(True)
+    pcm_all, stop_all = eng.generate(R, T, noise, steps, embeds_host=embeds)
+    assert eng.steps_done() == steps and np.all(stop_all < 0.5)
+    eng.stop_rule(False)
+    pcm_off, _ = eng.generate(R, T, noise, steps, embeds_host=embeds)
+    assert pcm_all.shape == pcm_off.shape == (R, 4 * cfg.hop * steps)
+    for r in range(R):
+        assert rel_err(pcm_all[r], pcm_off[r]) < 1e-4
+    eng.close()
+    model.close()
 
 
 def test_full_model_parity(ctx, mt, oracle):

@@ -66,3 +66,27 @@ def test_oracle_generation_bookkeeping(mt, oracle):
     c = oracle_generate(oracle, cfg, w, embeds, noise2, steps)
     np.testing.assert_array_equal(a["latents"][0], c["latents"][0])
     assert not np.allclose(a["latents"][1], c["latents"][1])
+
+
+def test_oracle_stop_rule(mt, oracle):
+    """obey_stop (Engine.swift:347-367): with the stop bias pinned so p ~ 1 the loop ends after step
+    n = 4 (the rule needs n > 3) and flushes, which is exactly a 5-step run on the same noise; with
+    p ~ 0 every step runs."""
+    cfg = mt.small_config()
+    arena, tensors = host_arena(mt, oracle, cfg, seed=5)
+    off = {t.name.decode(): t.offset for t in tensors}["stop_head.bias"]
+    bias = arena[off:off + 4].view(np.uint16)
+    w, keep = mt.weights_struct(cfg, arena.ctypes.data, tensors)
+    steps, T = 9, 3
+    rs = np.random.default_rng(5)
+    embeds = (0.5 * rs.standard_normal((T, cfg.llm.hidden))).astype(np.float32)
+    noise = oracle.gaussian_noise(steps * cfg.latent_dim, 11).reshape(steps, cfg.latent_dim)
+    bias[:] = [0xC180, 0x4180]  # bf16 -16, +16
+    stopped = oracle_generate(oracle, cfg, w, embeds, noise, steps, obey_stop=1)
+    fixed = oracle_generate(oracle, cfg, w, embeds, np.ascontiguousarray(noise[:5]), 5)
+    assert stopped["stopped"] == 1 and stopped["steps_run"] == 5
+    assert list(stopped["chunks"]) == list(fixed["chunks"])
+    np.testing.assert_array_equal(stopped["pcm"], fixed["pcm"])
+    bias[:] = [0x4180, 0xC180]
+    never = oracle_generate(oracle, cfg, w, embeds, noise, steps, obey_stop=1)
+    assert never["stopped"] == 0 and never["steps_run"] == steps and never["pcm"].size == 4 * cfg.hop * steps
