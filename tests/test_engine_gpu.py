@@ -24,7 +24,7 @@ def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-def oracle_generate(oracle, cfg, w_host, embeds, noise, steps, cfg_scale=2.0, obey_stop=0):
+def oracle_generate(oracle, cfg, w_host, embeds, noise, steps, cfg_scale=2.0, obey_stop=0, initial_history=None):
     L, H, Hv = cfg.latent_dim, cfg.llm.hidden, cfg.vae.hidden
     T = embeds.shape[0]
     out = dict(stop=np.zeros((steps, 2), np.float32), z=np.zeros((steps, H), np.float32),
@@ -34,6 +34,7 @@ def oracle_generate(oracle, cfg, w_host, embeds, noise, steps, cfg_scale=2.0, ob
     io = oracle.GenerateIO()
     io.prompt_rows, io.embeds, io.steps, io.cfg, io.obey_stop = T, embeds.ctypes.data, steps, cfg_scale, obey_stop
     io.noise = noise.ctypes.data
+    io.initial_history = None if initial_history is None else initial_history.ctypes.data
     io.stop_logits, io.llm_hidden, io.latents = out["stop"].ctypes.data, out["z"].ctypes.data, out["latents"].ctypes.data
     io.agg_out, io.velocity0, io.vae_hidden = out["agg"].ctypes.data, out["vel0"].ctypes.data, out["vae_hidden"].ctypes.data
     io.pcm, io.pcm_cap, io.chunk_counts = out["pcm"].ctypes.data, out["pcm"].size, out["chunks"].ctypes.data
@@ -44,12 +45,13 @@ def oracle_generate(oracle, cfg, w_host, embeds, noise, steps, cfg_scale=2.0, ob
     return out
 
 
-def engine_generate(mt, eng, cfg, embeds=None, ids=None, noise=None, steps=1, cfg_scale=2.0):
+def engine_generate(mt, eng, cfg, embeds=None, ids=None, noise=None, steps=1, cfg_scale=2.0, initial_history=None):
     import torch
     R, T = (embeds.shape[0], embeds.shape[1]) if embeds is not None else ids.shape
     H, L = cfg.llm.hidden, cfg.latent_dim
     eng.begin(R, T, embeds=dev(embeds) if embeds is not None else None,
-              token_ids=dev(ids) if ids is not None else None, noise=dev(noise), steps=steps, cfg=cfg_scale)
+              token_ids=dev(ids) if ids is not None else None, noise=dev(noise),
+              initial_history=dev(initial_history) if initial_history is not None else None, steps=steps, cfg=cfg_scale)
     eng.prefill()
     res = dict(stop=[], z=[], agg=[], pcm=[[] for _ in range(R)], chunks=[], vae_hidden=[])
     for n in range(steps):
@@ -84,7 +86,8 @@ def engine_generate(mt, eng, cfg, embeds=None, ids=None, noise=None, steps=1, cf
     return res
 
 
-def compare(mt, oracle, ctx, cfg, R, T, steps, seed, use_graphs=True, use_ids=False, lat_rel=1e-3, groups=0):
+def compare(mt, oracle, ctx, cfg, R, T, steps, seed, use_graphs=True, use_ids=False, lat_rel=1e-3, groups=0,
+            with_history=False):
     model = mt.Model(ctx, cfg, seed=seed)
     host = model.arena_to_host()
     tensors = model.tensors()
@@ -100,10 +103,14 @@ def compare(mt, oracle, ctx, cfg, R, T, steps, seed, use_graphs=True, use_ids=Fa
     else:
         ids = None
         embeds = (0.5 * rs.standard_normal((R, T, H))).astype(np.float32)
+    # a cloned voice's starting history: the reference clip's last latent (MingTTS.swift:105, 112-114)
+    hist = rs.standard_normal((R, L)).astype(np.float32) if with_history else None
     eng = mt.Engine(ctx, model, R, T, steps, use_graphs=use_graphs, groups=groups)
-    got = engine_generate(mt, eng, cfg, embeds=None if use_ids else embeds, ids=ids, noise=noise, steps=steps)
+    got = engine_generate(mt, eng, cfg, embeds=None if use_ids else embeds, ids=ids, noise=noise, steps=steps,
+                          initial_history=hist)
     for r in range(R):
-        want = oracle_generate(oracle, cfg, w_host, np.ascontiguousarray(embeds[r]), np.ascontiguousarray(noise[r]), steps)
+        want = oracle_generate(oracle, cfg, w_host, np.ascontiguousarray(embeds[r]), np.ascontiguousarray(noise[r]), steps,
+                               initial_history=None if hist is None else np.ascontiguousarray(hist[r]))
         tag = f"R{R} request {r}"
         assert list(got["chunks"]) == list(want["chunks"]), f"{tag}: emission counts"
         assert rel_err(got["z"][r], want["z"]) < 1e-3, f"{tag}: llm hidden rel {rel_err(got['z'][r], want['z'])}"
@@ -135,6 +142,14 @@ def test_small_model_all_tensor_core(ctx, mt, oracle):
 def test_small_model_request_groups(ctx, mt, oracle, R, groups):
     # Requests split into groups stepped on their own streams (11 = 6 + 5: uneven groups).
     compare(mt, oracle, ctx, mt.small_config(), R=R, T=5, steps=6, seed=7, groups=groups)
+
+
+def test_initial_history_matches_oracle(ctx, mt, oracle):
+    """mt_engine_begin's initial_history (Options.initialHistory, Engine.swift:315): per-request
+    starting latent history of the flow head, as a cloned voice sets it."""
+    got = compare(mt, oracle, ctx, mt.small_config(), R=3, T=4, steps=4, seed=21, with_history=True)
+    plain = compare(mt, oracle, ctx, mt.small_config(), R=3, T=4, steps=4, seed=21)
+    assert rel_err(got["latents"], plain["latents"]) > 1e-2  # the history reaches the flow head
 
 
 def test_graph_replay_matches_eager(ctx, mt, oracle):
