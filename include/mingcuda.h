@@ -178,7 +178,7 @@ int mt_linear_route(int m, int n, int k);
  *
  * Every kernel is launched with programmatic dependent launch: it may start while the previous
  * kernel on the stream drains, and waits for that kernel before it reads activations or writes
- * outputs. The tensor-core linear reads its weights (w, w2) before that wait, so the weights must
+ * outputs. mt_linear reads its weights (w, w2) before that wait on every route, so the weights must
  * not be written by the kernel directly before it on the same stream if that kernel triggers
  * programmatic completion early (kernels of other libraries normally do not; model creation in
  * this library synchronises).

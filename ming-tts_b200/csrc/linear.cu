@@ -6,9 +6,9 @@
 // epilogue order +bias -> silu gate -> gelu -> silu -> accumulate.
 //
 // GEMV design: the weight matrix is streamed exactly once with 16-byte non-caching loads; a group
-// of G threads (8..256, a power of two) owns one output column for all MR rows, G sized so each
-// thread keeps about four 16-byte loads in flight; partial sums meet through warp shuffles (and
-// shared memory when G spans warps).
+// of G threads (8..128, a power of two) owns one output column for all MR rows, G sized so each
+// thread has at most eight 16-byte loads, all issued together before the programmatic-launch
+// dependency wait; partial sums meet through warp shuffles (and shared memory when G spans warps).
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -16,74 +16,71 @@ namespace mt {
 
 constexpr int GEMV_THREADS = 256;
 
+// acc[r] (+ acc2[r] for the gated up projection) += x[r, k0:k0+8] . w[k0:k0+8] for the rows present.
+template <int MR, bool GATED>
+__device__ __forceinline__ void gemv_chunk(float (&acc)[MR], float (&acc2)[MR], const uint4& w, const uint4& w2,
+                                           const float* x, int ldx, int rows, int k0) {
+#pragma unroll
+    for (int r = 0; r < MR; r++) {
+        if (r < rows) {
+            const float4 x0 = *reinterpret_cast<const float4*>(x + (size_t)r * ldx + k0);
+            const float4 x1 = *reinterpret_cast<const float4*>(x + (size_t)r * ldx + k0 + 4);
+            acc[r] += x0.x * bf16_lo(w.x) + x0.y * bf16_hi(w.x) + x0.z * bf16_lo(w.y) + x0.w * bf16_hi(w.y) +
+                      x1.x * bf16_lo(w.z) + x1.y * bf16_hi(w.z) + x1.z * bf16_lo(w.w) + x1.w * bf16_hi(w.w);
+            if (GATED)
+                acc2[r] += x0.x * bf16_lo(w2.x) + x0.y * bf16_hi(w2.x) + x0.z * bf16_lo(w2.y) + x0.w * bf16_hi(w2.y) +
+                           x1.x * bf16_lo(w2.z) + x1.y * bf16_hi(w2.z) + x1.z * bf16_lo(w2.w) + x1.w * bf16_hi(w2.w);
+        }
+    }
+}
+
 template <int MR, int G, bool GATED>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(LinearArgs a) {
-    pdl_wait();
-    pdl_launch();
     constexpr int C = GEMV_THREADS / G;  // columns per block
+    constexpr int U = G >= 128 ? 8 : 4;  // chunks per thread loaded ahead of the dependency wait
     __shared__ float red[GATED ? 2 : 1][GEMV_THREADS / 32][MR];
     const int tid = threadIdx.x;
     const int group = tid / G, gl = tid % G;
     const int n = blockIdx.x * C + group;
     const int row0 = blockIdx.y * MR;
-    const int rows = min(MR, a.m - row0);
     const bool live = n < a.n;
     const int chunks = a.k >> 3;
+    const uint16_t* wrow = a.w + (size_t)(live ? n : 0) * a.k;
+    const uint16_t* w2row = GATED ? a.w2 + (size_t)(live ? n : 0) * a.k : nullptr;
+
+    // The weights do not depend on the previous kernel: all of this thread's first U 16-byte loads
+    // (every load when k <= 8 U G, which the group size ensures up to k = 8192) are issued before
+    // the dependency wait, so they stream while the previous kernel drains.
+    uint4 wv[U], wv2[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        const int c = gl + u * G;
+        wv[u] = wv2[u] = make_uint4(0, 0, 0, 0);
+        if (live && c < chunks) {
+            wv[u] = ld_stream_u4(wrow + (size_t)c * 8);
+            if (GATED) wv2[u] = ld_stream_u4(w2row + (size_t)c * 8);
+        }
+    }
+    pdl_wait();
+    pdl_launch();
+    const int rows = min(MR, a.m - row0);
 
     float acc[MR], acc2[MR];
 #pragma unroll
     for (int r = 0; r < MR; r++) { acc[r] = 0.f; acc2[r] = 0.f; }
 
     if (live) {
-        const uint16_t* wrow = a.w + (size_t)n * a.k;
-        const uint16_t* w2row = GATED ? a.w2 + (size_t)n * a.k : nullptr;
         const float* x = a.x + (size_t)row0 * a.ldx;
-        int c = gl;
-        // Four chunks per iteration keep four independent 16-byte weight loads in flight.
-        for (; c + 3 * G < chunks; c += 4 * G) {
-            uint4 wv[4], wv2[4];
+        // Chunks in ascending order (gl, gl + G, ...), one add per chunk into the row's sum.
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                wv[u] = ld_stream_u4(wrow + (size_t)(c + u * G) * 8);
-                if (GATED) wv2[u] = ld_stream_u4(w2row + (size_t)(c + u * G) * 8);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int k0 = (c + u * G) * 8;
-#pragma unroll
-                for (int r = 0; r < MR; r++) {
-                    if (r < rows) {
-                        const float4 x0 = *reinterpret_cast<const float4*>(x + (size_t)r * a.ldx + k0);
-                        const float4 x1 = *reinterpret_cast<const float4*>(x + (size_t)r * a.ldx + k0 + 4);
-                        acc[r] += x0.x * bf16_lo(wv[u].x) + x0.y * bf16_hi(wv[u].x) + x0.z * bf16_lo(wv[u].y) +
-                                  x0.w * bf16_hi(wv[u].y) + x1.x * bf16_lo(wv[u].z) + x1.y * bf16_hi(wv[u].z) +
-                                  x1.z * bf16_lo(wv[u].w) + x1.w * bf16_hi(wv[u].w);
-                        if (GATED)
-                            acc2[r] += x0.x * bf16_lo(wv2[u].x) + x0.y * bf16_hi(wv2[u].x) + x0.z * bf16_lo(wv2[u].y) +
-                                       x0.w * bf16_hi(wv2[u].y) + x1.x * bf16_lo(wv2[u].z) + x1.y * bf16_hi(wv2[u].z) +
-                                       x1.z * bf16_lo(wv2[u].w) + x1.w * bf16_hi(wv2[u].w);
-                    }
-                }
-            }
+        for (int u = 0; u < U; u++) {
+            const int c = gl + u * G;
+            if (c < chunks) gemv_chunk<MR, GATED>(acc, acc2, wv[u], wv2[u], x, a.ldx, rows, c * 8);
         }
-        for (; c < chunks; c += G) {
-            const uint4 wv = ld_stream_u4(wrow + (size_t)c * 8);
-            uint4 wv2 = make_uint4(0, 0, 0, 0);
-            if (GATED) wv2 = ld_stream_u4(w2row + (size_t)c * 8);
-            const int k0 = c * 8;
-#pragma unroll
-            for (int r = 0; r < MR; r++) {
-                if (r < rows) {
-                    const float4 x0 = *reinterpret_cast<const float4*>(x + (size_t)r * a.ldx + k0);
-                    const float4 x1 = *reinterpret_cast<const float4*>(x + (size_t)r * a.ldx + k0 + 4);
-                    acc[r] += x0.x * bf16_lo(wv.x) + x0.y * bf16_hi(wv.x) + x0.z * bf16_lo(wv.y) + x0.w * bf16_hi(wv.y) +
-                              x1.x * bf16_lo(wv.z) + x1.y * bf16_hi(wv.z) + x1.z * bf16_lo(wv.w) + x1.w * bf16_hi(wv.w);
-                    if (GATED)
-                        acc2[r] += x0.x * bf16_lo(wv2.x) + x0.y * bf16_hi(wv2.x) + x0.z * bf16_lo(wv2.y) +
-                                   x0.w * bf16_hi(wv2.y) + x1.x * bf16_lo(wv2.z) + x1.y * bf16_hi(wv2.z) +
-                                   x1.z * bf16_lo(wv2.w) + x1.w * bf16_hi(wv2.w);
-                }
-            }
+        for (int c = gl + U * G; c < chunks; c += G) {
+            const uint4 w = ld_stream_u4(wrow + (size_t)c * 8);
+            const uint4 w2 = GATED ? ld_stream_u4(w2row + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
+            gemv_chunk<MR, GATED>(acc, acc2, w, w2, x, a.ldx, rows, c * 8);
         }
     }
 
@@ -148,16 +145,17 @@ static void launch_gemv_g(const LinearArgs& a, int G, cudaStream_t s) {
         case 16: launch_k(gemv_kernel<MR, 16, GATED>, grid, GEMV_THREADS, 0, s, a); break;
         case 32: launch_k(gemv_kernel<MR, 32, GATED>, grid, GEMV_THREADS, 0, s, a); break;
         case 64: launch_k(gemv_kernel<MR, 64, GATED>, grid, GEMV_THREADS, 0, s, a); break;
-        case 128: launch_k(gemv_kernel<MR, 128, GATED>, grid, GEMV_THREADS, 0, s, a); break;
-        default: launch_k(gemv_kernel<MR, 256, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        default: launch_k(gemv_kernel<MR, 128, GATED>, grid, GEMV_THREADS, 0, s, a); break;
     }
 }
 
-// Threads per column: about four 16-byte chunks per thread, 8..256.
+// Threads per column: about four 16-byte chunks per thread, 8..128 (up to eight at 128, k <= 8192).
+// Measured in graph replay over a weight pool larger than L2: W[4864x896] streams fastest with 32
+// threads per column (608 blocks), W[896x4864] with 128 (448 blocks) rather than 256 (896 blocks).
 static int gemv_group(int k) {
     const int chunks = k / 8;
     int g = 8;
-    while (g < 256 && g * 4 < chunks) g *= 2;
+    while (g < 128 && g * 4 < chunks) g *= 2;
     return g;
 }
 
