@@ -364,6 +364,8 @@ def main():
                     help="request groups stepped concurrently (0 = the engine's automatic choice)")
     ap.add_argument("--gemm", type=str, default="",
                     help="M,N,K[,flags]: time one tensor-core GEMM shape alone and exit (for focused profiling)")
+    ap.add_argument("--gemv", type=str, default="",
+                    help="N,K[,M]: time the CUDA-core GEMV over a >= 1 GiB weight pool alone and exit (for focused profiling)")
     ap.add_argument("--profile", action="store_true",
                     help="prefill, warm-up and timed steps only (for a profiler's launch list); prints ms/step")
     args = ap.parse_args()
@@ -381,6 +383,16 @@ def main():
         t = time_gemm(mt, ctx, m, n, k, flags, iters=20, rounds=1)
         print(json.dumps({"gemm": [m, n, k, flags], "us": round(t * 1e6, 2),
                           "tflops": round(2.0 * m * n * k / t / 1e12, 1)}), flush=True)
+        return
+    if args.gemv:
+        mt = load_package()
+        ctx = mt.Context(local)
+        f = [int(v) for v in args.gemv.split(",")]
+        n, k, m = f[0], f[1], (f[2] if len(f) > 2 else 2)
+        t, copies = time_gemv_pool(mt, ctx, n, k, m=m)
+        nbytes = n * k * 2 + m * k * 4 + m * n * 4
+        print(json.dumps({"gemv": [m, n, k], "us": round(t * 1e6, 3), "gbs": round(nbytes / t / 1e9, 1),
+                          "pool_copies": copies}), flush=True)
         return
 
     import numpy as np
