@@ -14,6 +14,8 @@ the aggregator DiT (2R rows), VAE fc1, and the VAE decode of latent n-2 (24-laye
             chunk and stop logit D2H), wall time of the call, max over ranks.
   roofline  the dominant kernel (tcgen05 GEMM at the flow-DiT ff1 shape) timed alone with events.
   gemv      BASELINE config 1: decode GEMV W[4864x896] (and the down proj) over a >= 1 GiB pool.
+  single_request  the reference's published shape (one request, 174-token prompt): prefill ms,
+            ms per step, audio-s/s and p50 time to first audio.
   cpu_baseline / --impl reference: the CPU oracle (C restatement of the reference's kernels and
             loop, OpenMP) on a bounded sample: one request, full model, timed per step.
 
@@ -249,6 +251,49 @@ def time_to_first_audio(eng, requests, prompt, noise_host, ids_host, steps, worl
     return dist_max(statistics.median(samples), world), reps
 
 
+def single_request(mt, ctx, model, cfg, first_request, world, prompt=174, steps=50, warmup=5, reps=5):
+    """The reference's own benchmark shape (.claude/skills/verify/features/bench.md:25: one request, a
+    174-token prompt):
+    prefill time and step time with device-resident inputs (CUDA events on the launching stream,
+    medians over `reps`), audio-s/s of the steps, and the p50 time to first audio through the
+    streaming host API. One request runs its LLM and aggregator rows on the CUDA-core GEMV."""
+    import numpy as np
+    import torch
+    ids, noise = request_inputs(mt, cfg, 1, prompt, warmup + steps, first_request)
+    eng = mt.Engine(ctx, model, 1, prompt, warmup + steps)
+    ids_d, noise_d = torch.from_numpy(ids).cuda(), torch.from_numpy(noise).cuda()
+    stream = torch.cuda.current_stream()
+    pre, per_step = [], []
+    for _ in range(reps):
+        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        eng.begin(1, prompt, token_ids=ids_d, noise=noise_d, steps=warmup + steps)
+        a.record(stream)
+        eng.prefill()
+        b.record(stream)
+        for _ in range(warmup):
+            eng.step()
+        b2 = torch.cuda.Event(enable_timing=True)
+        b2.record(stream)
+        for _ in range(steps):
+            eng.step()
+        c.record(stream)
+        c.synchronize()
+        pre.append(a.elapsed_time(b))
+        per_step.append(b2.elapsed_time(c) / steps)
+    ctx.check()
+    ids_h = torch.from_numpy(ids).pin_memory().numpy()
+    noise_h = torch.from_numpy(np.ascontiguousarray(noise)).pin_memory().numpy()
+    ttfa, calls = time_to_first_audio(eng, 1, prompt, noise_h, ids_h, 12, world)
+    eng.close()
+    prefill_ms = dist_max(statistics.median(pre), world)
+    step_ms = dist_max(statistics.median(per_step), world)
+    return {"prompt_tokens": prompt, "requests": 1, "prefill_ms": round(prefill_ms, 3),
+            "ms_per_step": round(step_ms, 3), "audio_s_per_s": round(AUDIO_PER_STEP / (step_ms * 1e-3), 2),
+            "ttfa_ms_p50": round(ttfa * 1e3, 2), "ttfa_calls": calls,
+            "reference_published": {"prefill_ms": 26.0, "ms_per_step_gpu": 15.01, "ttfa_ms": 65,
+                                    "hardware": "Apple M-series GPU (.claude/skills/verify/features/bench.md:25)"}}
+
+
 def host_model(mt, oracle, cfg, seed):
     import numpy as np
     tensors = mt.tensor_table(cfg, seed)
@@ -468,6 +513,7 @@ def main():
     h2d = (ids_h.nbytes + noise_e.nbytes) / E
     d2h = (R * max_chunk * 4 * (E + 0.0) + R * 2 * 4 * E) / E
     ttfa = time_to_first_audio(eng, R, T, noise_e, ids_h, min(E, 12), world)
+    single = single_request(mt, ctx, model, cfg, first + R, world)
 
     # ---- kernel roofline: the tcgen05 GEMM at the flow-DiT ff1 shape; decode GEMV (config 1) ----
     hbm_peak, bf16_peak, peak_kind = peaks()
@@ -512,6 +558,7 @@ def main():
                          "down_proj_gbs": round(gv_down_bytes / t_gv_down / 1e9, 1),
                          "pool": f"{copies} distinct weight copies (>= 1 GiB), graph replay",
                          "peak_gbs": hbm_peak, "peak_kind": peak_kind},
+                "single_request": single,
                 "stages_ms": {"llm": stage_ms[0], "flow": stage_ms[1], "agg": stage_ms[2], "vae_concurrent": stage_ms[3],
                               "note": "one eager step, events per stage; the VAE decode runs on a second stream"},
                 "gpu_launches": kernels, "clocks": clocks.summary()}
