@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """bench.py -- audio-seconds per second of the Ming-3.0-tts-0.5B per-step loop on B200.
 
-Workload (per GPU): R = 64 concurrent requests, each a 128-token prompt of
+Workload (the serving configuration, per GPU): R = 64 concurrent requests, each a 128-token prompt of
 uniform random ids in [0, 151936) (per-request seeds), prefill, then generation steps with CFG 2.0
 and N(0,1) noise; random-init weights (seed 1). One bench step = one engine step over all R
 requests: LLM token (24 layers, R rows), stop head, 10 Euler steps of the CFG flow DiT (6R rows),
@@ -13,7 +13,7 @@ the aggregator DiT (2R rows), VAE fc1, and the VAE decode of latent n-2 (24-laye
   e2e       mt_engine_generate from host memory (ids + noise H2D, prefill, steps, flush, every PCM
             chunk and stop logit D2H), wall time of the call, max over ranks.
   roofline  the dominant kernel (tcgen05 GEMM at the flow-DiT ff1 shape) timed alone with events.
-  gemv      BASELINE config 1: decode GEMV W[4864x896] (and the down proj) over a >= 1 GiB pool.
+  gemv      the decode GEMV alone: M=2, W[4864x896] (and the down proj) over a >= 1 GiB pool.
   single_request  the reference's published shape (one request, 174-token prompt): prefill ms,
             ms per step, audio-s/s and p50 time to first audio.
   cpu_baseline / --impl reference: the CPU oracle (C restatement of the reference's kernels and
