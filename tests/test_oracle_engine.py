@@ -90,3 +90,24 @@ def test_oracle_stop_rule(mt, oracle):
     bias[:] = [0x4180, 0xC180]
     never = oracle_generate(oracle, cfg, w, embeds, noise, steps, obey_stop=1)
     assert never["stopped"] == 0 and never["steps_run"] == steps and never["pcm"].size == 4 * cfg.hop * steps
+
+
+def test_oracle_initial_history(mt, oracle):
+    """The history buffer is zeroed and then overwritten by initialHistory when one is given
+    (Engine.swift:314-315): an all-zero history gives exactly the run without one, a reference
+    voice's latent changes the generation from step 0 on."""
+    cfg = mt.small_config()
+    arena, tensors = host_arena(mt, oracle, cfg, seed=8)
+    w, keep = mt.weights_struct(cfg, arena.ctypes.data, tensors)
+    steps, T = 4, 3
+    rs = np.random.default_rng(8)
+    embeds = (0.5 * rs.standard_normal((T, cfg.llm.hidden))).astype(np.float32)
+    noise = oracle.gaussian_noise(steps * cfg.latent_dim, 13).reshape(steps, cfg.latent_dim)
+    plain = oracle_generate(oracle, cfg, w, embeds, noise, steps)
+    zeros = oracle_generate(oracle, cfg, w, embeds, noise, steps,
+                            initial_history=np.zeros(cfg.latent_dim, np.float32))
+    voice = oracle_generate(oracle, cfg, w, embeds, noise, steps,
+                            initial_history=rs.standard_normal(cfg.latent_dim).astype(np.float32))
+    np.testing.assert_array_equal(zeros["latents"], plain["latents"])
+    np.testing.assert_array_equal(zeros["pcm"], plain["pcm"])
+    assert np.abs(voice["latents"][0] - plain["latents"][0]).max() > 1e-3
