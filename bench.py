@@ -1,23 +1,32 @@
 #!/usr/bin/env python
 """bench.py -- audio-seconds per second of the Ming-3.0-tts-0.5B per-step loop on B200.
 
-Workload (the serving configuration, per GPU): R = 64 concurrent requests, each a 128-token prompt of
-uniform random ids in [0, 151936) (per-request seeds), prefill, then generation steps with CFG 2.0
-and N(0,1) noise; random-init weights (seed 1). One bench step = one engine step over all R
-requests: LLM token (24 layers, R rows), stop head, 10 Euler steps of the CFG flow DiT (6R rows),
-the aggregator DiT (2R rows), VAE fc1, and the VAE decode of latent n-2 (24-layer windowed Qwen,
-4R rows, head, ISTFT, overlap-add). Each step yields 0.08 s of audio per request.
+Workload (per GPU): R = 64 concurrent requests, each a 128-token prompt of uniform
+random ids in [0, 151936) (per-request seeds), prefill, then a 256-step generation with CFG 2.0 and
+N(0,1) noise; random-init weights (seed 1). One bench step = one engine step over all R requests:
+LLM token (24 layers, R rows), stop head, 10 Euler steps of the CFG flow DiT (6R rows), the
+aggregator DiT (2R rows), VAE fc1, and the VAE decode of latent n-2 (24-layer windowed Qwen, 4R rows,
+head, ISTFT, overlap-add). Each step yields 0.08 s of audio per request.
 
-  value     device-timed throughput of K steps (CUDA events on the engine stream, inputs resident),
-            whole job = all ranks' requests / max-over-ranks time (weak scaling: R per GPU).
-  e2e       mt_engine_generate from host memory (ids + noise H2D, prefill, steps, flush, every PCM
-            chunk and stop logit D2H), wall time of the call, max over ranks.
-  roofline  the dominant kernel (tcgen05 GEMM at the flow-DiT ff1 shape) timed alone with events.
-  gemv      the decode GEMV alone: M=2, W[4864x896] (and the down proj) over a >= 1 GiB pool.
-  single_request  the reference's published shape (one request, 174-token prompt): prefill ms,
-            ms per step, audio-s/s and p50 time to first audio.
-  cpu_baseline / --impl reference: the CPU oracle (C restatement of the reference's kernels and
-            loop, OpenMP) on a bounded sample: one request, full model, timed per step.
+  value       device-timed throughput of K steps after W warm-up steps of one generation (CUDA events on
+              the engine stream, inputs resident), whole job = all ranks' requests / max-over-ranks time
+              (weak scaling: R requests per GPU).
+  full_run    the whole config-5 generation (prefill, 256 steps, flush) device-timed, same units.
+  e2e         mt_engine_generate from host memory over the full 256-step run (ids + noise H2D, prefill,
+              steps, flush, every PCM chunk and stop logit D2H), wall time of the call, max over ranks.
+  strong      config 5's partitioning: 64 requests in all, 64 / N per GPU (N = 1: the value itself).
+  roofline    the dominant kernel (tcgen05 GEMM at the flow-DiT ff1 shape), graph-replayed over a pool
+              of weight copies larger than L2, CUDA events.
+  gemv        config 1: the decode GEMV alone, M = 2, W[4864x896] (and the down projection), >= 1 GiB pool.
+  decode      config 2: the 24-layer LLM decode step (mt_qwen_decode) + stop head, M = 1 and 2, KV cache
+              filled to 256 of 512 positions, GB/s of algorithmic bytes per step.
+  configs_cpu configs 1-4 on the host cores through the CPU oracle (C restatement of the reference's
+              kernels, fp64 dot products, OpenMP), each on a bounded sample.
+  single_request  the reference's published shape (one request, 174-token prompt): prefill ms, ms per
+              step, audio-s/s, p50 time to first audio; with flow patch (config 3) and VAE clip (config 4)
+              GPU times of one request.
+  cpu_baseline / --impl reference: the CPU oracle's generation loop (one request, 128-token prompt)
+              on all host cores; it loads liboracle.so only.
 
 Multi-GPU: launched by torchrun, one rank per GPU, independent replicas (no collective on the data
 path); torch.distributed is used only for barriers and the max-over-ranks of the timings.
@@ -36,6 +45,11 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 AUDIO_PER_STEP = 0.08  # 3528 samples at 44.1 kHz (Text/MingRequest.swift:104)
+RUN_STEPS = 256        # config 5: prefill then 256 autoregressive steps
+METRIC = "audio-sec/sec of the Ming-3.0-tts-0.5B step loop (config 5 serving, per-GPU replicas)"
+# DRAM bytes (read + write) of one launch of the roofline GEMM at the flow ff1 shape, from an ncu
+# capture of that kernel (dram__bytes_read.sum + dram__bytes_write.sum); reported, not measured here.
+ROOFLINE_TRAFFIC_BYTES = 10_003_456
 
 
 def load_package():
@@ -48,6 +62,14 @@ def load_package():
     sys.modules[name] = mod
     spec.loader.exec_module(mod)
     return mod
+
+
+def load_oracle():
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
+    import oracle
+    import oracle.model
+    return oracle
 
 
 def peaks():
@@ -145,41 +167,57 @@ def rank_requests(rank: int, per_rank: int):
     return rank * per_rank, per_rank
 
 
-def request_inputs(mt, cfg, requests, prompt, steps, first_request):
-    """Per-request prompt ids (uniform over the vocabulary) and N(0,1) noise, seeded by request index."""
+def request_inputs(noise_fn, vocab, latent, requests, prompt, steps, first_request):
+    """Per-request prompt ids (uniform over the vocabulary) and N(0,1) noise, seeded by request index.
+    noise_fn(out_float32_array, seed) fills one request's noise (SplitMix64 + Box-Muller)."""
     import numpy as np
-    ids = np.stack([np.random.default_rng(1000 + first_request + r).integers(0, cfg.vocab, prompt, dtype=np.int32)
+    ids = np.stack([np.random.default_rng(1000 + first_request + r).integers(0, vocab, prompt, dtype=np.int32)
                     for r in range(requests)])
-    noise = np.empty((requests, steps, cfg.latent_dim), np.float32)
+    noise = np.empty((requests, steps, latent), np.float32)
     for r in range(requests):
-        mt.lib().mt_gaussian_noise_host(noise[r].ctypes.data, noise[r].size, 3 + first_request + r)
+        noise_fn(noise[r], 3 + first_request + r)
     return ids, noise
+
+
+def product_noise(mt):
+    return lambda out, seed: mt.lib().mt_gaussian_noise_host(out.ctypes.data, out.size, seed)
+
+
+def oracle_noise(oracle):
+    def fill(out, seed):
+        out[...] = oracle.gaussian_noise(out.size, seed).reshape(out.shape)
+    return fill
 
 
 # ------------------------------------------------------------------------------------------------
 # Kernel-level measurements
 # ------------------------------------------------------------------------------------------------
-def time_gemm(mt, ctx, m, n, k, flags, iters=100, rounds=3):
-    """Average duration of the tcgen05 GEMM at one shape: `iters` launches replayed from a CUDA
-    graph (so host launch cost is not measured), CUDA events, best of `rounds`."""
+def time_gemm(mt, ctx, m, n, k, flags, pool_bytes=256 << 20, rounds=3):
+    """Average duration of the tcgen05 GEMM at one shape with its weights streamed from DRAM: the
+    launches walk a pool of distinct weight copies larger than L2 (126 MB), replayed from a CUDA
+    graph (host launch cost not measured), CUDA events on the launching stream, best of `rounds`."""
     import torch
     g = torch.Generator(device="cuda").manual_seed(0)
+    copies = max(2, pool_bytes // (n * k * 2))
     xh = (torch.randn(m, k, device="cuda", generator=g)).to(torch.bfloat16)
     xl = (torch.randn(m, k, device="cuda", generator=g) * 2 ** -9).to(torch.bfloat16)
-    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    pool = (torch.randn(copies, n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
     b = (torch.randn(n, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
     yh = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
     yl = torch.empty_like(yh)
-    args = (xh, xl, k, m, w, None, b, n, k, None, 0, yh, yl, n, flags | mt.BIAS)
+
+    def call(i):
+        ctx.call("linear_split", xh, xl, k, m, pool[i], None, b, n, k, None, 0, yh, yl, n, flags | mt.BIAS)
+
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
-        for _ in range(3):
-            ctx.call("linear_split", *args)
+        for i in range(3):
+            call(i)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
-            for _ in range(iters):
-                ctx.call("linear_split", *args)
+            for i in range(copies):
+                call(i)
         graph.replay()
         torch.cuda.synchronize()
         best = None
@@ -189,10 +227,12 @@ def time_gemm(mt, ctx, m, n, k, flags, iters=100, rounds=3):
             graph.replay()
             e.record(stream)
             e.synchronize()
-            t = s.elapsed_time(e) * 1e-3 / iters
+            t = s.elapsed_time(e) * 1e-3 / copies
             best = t if best is None else min(best, t)
     ctx.check()
-    return best
+    del graph, pool
+    torch.cuda.empty_cache()
+    return best, copies
 
 
 def time_gemv_pool(mt, ctx, n, k, m=2, pool_bytes=1 << 30, rounds=3):
@@ -228,8 +268,64 @@ def time_gemv_pool(mt, ctx, n, k, m=2, pool_bytes=1 << 30, rounds=3):
     return best, copies
 
 
+def decode_step_bytes(cfg, requests, length):
+    """Algorithmic bytes of one config-2 step: every LLM weight once (bf16), the stop head, each
+    request's cached keys and values over length + 1 positions (fp32 reads) and its new row (writes)."""
+    c = cfg.llm
+    qkvw = (c.heads + 2 * c.kv_heads) * 64
+    layer = 2 * (c.hidden * qkvw + qkvw + c.hidden * c.heads * 64 + 2 * c.intermediate * c.hidden +
+                 c.hidden * c.intermediate + 2 * c.hidden)
+    weights = c.layers * layer + 2 * c.hidden + 2 * (2 * c.hidden + 2)
+    kv = requests * c.layers * 2 * c.kv_heads * 64 * 4 * ((length + 1) + 1)
+    acts = requests * c.hidden * 4 * 3
+    return weights + kv + acts
+
+
+def time_decode(mt, ctx, model, cfg, requests, length=256, iters=20, rounds=3):
+    """Config 2: mt_qwen_decode over `requests` sequences (one row each) at cache length `length` of
+    512, plus the stop head, replayed from a CUDA graph; seconds per step."""
+    import torch
+    c, H, cap = cfg.llm, cfg.llm.hidden, cfg.llm_capacity
+    w = ctypes.cast(mt.lib().mt_model_get_weights(model.handle), ctypes.POINTER(mt.ModelWeights)).contents
+    stride = c.layers * 2 * c.kv_heads * cap * 64
+    kv = torch.randn(requests * stride, device="cuda").to(torch.bfloat16).float()
+    x = torch.randn(requests, H, device="cuda") * 0.5
+    z = torch.empty(requests, H, device="cuda")
+    logits = torch.empty(requests, 2, device="cuda")
+    pos = torch.full((requests,), length, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def step():
+        ctx.call("qwen_decode", ctypes.byref(w.llm), requests, 1, x, kv, stride, cap, pos, z)
+        ctx.call("linear", z, H, requests, w.stop_w, None, w.stop_b, 2, H, logits, 2, mt.BIAS)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(iters):
+                step()
+        graph.replay()
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(rounds):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            graph.replay()
+            e.record(stream)
+            e.synchronize()
+            t = s.elapsed_time(e) * 1e-3 / iters
+            best = t if best is None else min(best, t)
+    ctx.check()
+    del graph, kv
+    torch.cuda.empty_cache()
+    return best
+
+
 # ------------------------------------------------------------------------------------------------
-# CPU oracle runs (baseline)
+# Serving measurements
 # ------------------------------------------------------------------------------------------------
 def time_to_first_audio(eng, requests, prompt, noise_host, ids_host, steps, world, reps=7):
     """p50 time to the first non-empty PCM chunk through mt_engine_generate_stream (host ids and noise,
@@ -251,15 +347,31 @@ def time_to_first_audio(eng, requests, prompt, noise_host, ids_host, steps, worl
     return dist_max(statistics.median(samples), world), reps
 
 
+def stage_split(eng, R, T, ids_d, noise_d, steps=8):
+    """Per-stage GPU milliseconds [llm, flow, agg, vae] of eager steps 3..steps-1 (medians)."""
+    import torch
+    eng.stage_timing(True)
+    eng.begin(R, T, token_ids=ids_d, noise=noise_d, steps=steps)
+    eng.prefill()
+    samples = []
+    for n in range(steps):
+        eng.step()
+        if n >= 3:
+            torch.cuda.synchronize()
+            samples.append(eng.stage_ms())
+    eng.stage_timing(False)
+    return [round(statistics.median(x[i] for x in samples), 4) for i in range(4)]
+
+
 def single_request(mt, ctx, model, cfg, first_request, world, prompt=174, steps=50, warmup=5, reps=5):
     """The reference's own benchmark shape (.claude/skills/verify/features/bench.md:25: one request, a
-    174-token prompt):
-    prefill time and step time with device-resident inputs (CUDA events on the launching stream,
-    medians over `reps`), audio-s/s of the steps, and the p50 time to first audio through the
-    streaming host API. One request runs its LLM and aggregator rows on the CUDA-core GEMV."""
+    174-token prompt): prefill time and step time with device-resident inputs (CUDA events on the
+    launching stream, medians over `reps`), audio-s/s of the steps, and the p50 time to first audio
+    through the streaming host API. With it, one request's flow patch (config 3: the flow stage of a
+    step) and 10-s VAE clip (config 4: 125 latent decodes) on the GPU, from the per-stage split."""
     import numpy as np
     import torch
-    ids, noise = request_inputs(mt, cfg, 1, prompt, warmup + steps, first_request)
+    ids, noise = request_inputs(product_noise(mt), cfg.vocab, cfg.latent_dim, 1, prompt, warmup + steps, first_request)
     eng = mt.Engine(ctx, model, 1, prompt, warmup + steps)
     ids_d, noise_d = torch.from_numpy(ids).cuda(), torch.from_numpy(noise).cuda()
     stream = torch.cuda.current_stream()
@@ -281,6 +393,7 @@ def single_request(mt, ctx, model, cfg, first_request, world, prompt=174, steps=
         pre.append(a.elapsed_time(b))
         per_step.append(b2.elapsed_time(c) / steps)
     ctx.check()
+    stages = stage_split(eng, 1, prompt, ids_d, noise_d)
     ids_h = torch.from_numpy(ids).pin_memory().numpy()
     noise_h = torch.from_numpy(np.ascontiguousarray(noise)).pin_memory().numpy()
     ttfa, calls = time_to_first_audio(eng, 1, prompt, noise_h, ids_h, 12, world)
@@ -290,30 +403,32 @@ def single_request(mt, ctx, model, cfg, first_request, world, prompt=174, steps=
     return {"prompt_tokens": prompt, "requests": 1, "prefill_ms": round(prefill_ms, 3),
             "ms_per_step": round(step_ms, 3), "audio_s_per_s": round(AUDIO_PER_STEP / (step_ms * 1e-3), 2),
             "ttfa_ms_p50": round(ttfa * 1e3, 2), "ttfa_calls": calls,
+            "stages_ms": {"llm": stages[0], "flow": stages[1], "agg": stages[2], "vae_concurrent": stages[3]},
+            "config3_flow_patch_ms": stages[1],
+            "config4_clip_ms": round(stages[3] * 125, 2),
+            "config4_note": "10-s clip = 125 latent decodes of one request (per-latent VAE stage x 125)",
             "reference_published": {"prefill_ms": 26.0, "ms_per_step_gpu": 15.01, "ttfa_ms": 65,
                                     "hardware": "Apple M-series GPU (.claude/skills/verify/features/bench.md:25)"}}
 
 
-def host_model(mt, oracle, cfg, seed):
-    import numpy as np
-    tensors = mt.tensor_table(cfg, seed)
-    arena = np.zeros(mt.lib().mt_model_arena_bytes(ctypes.byref(cfg), 1), np.uint8)
-    for t in tensors:
-        if t.dtype == mt.MT_DTYPE_BF16:
-            v = arena[t.offset:t.offset + 2 * t.numel].view(np.uint16)
-            v[:] = 0x3F80 if t.init == 1 else oracle.randn_bf16(t.numel, t.seed, t.std)
-        else:
-            v = arena[t.offset:t.offset + 4 * t.numel].view(np.float32)
-            if t.init == 0:
-                v[:] = oracle.bf16_to_f32(oracle.randn_bf16(t.numel, t.seed, t.std))
-            elif t.init == 2:
-                v[:] = (1.0 / np.power(10000.0, 2 * np.arange(t.numel) / 64.0)).astype(np.float32)
-            elif t.init == 3:
-                v[:] = (0.5 - 0.5 * np.cos(2 * np.pi * np.arange(t.numel) / t.numel)).astype(np.float32)
-    w, keep = mt.weights_struct(cfg, arena.ctypes.data, tensors)
-    return arena, tensors, w, keep
+def alt_dit_patch(mt, ctx, cfg, first_request, world):
+    """Config 3 at its own DiT dimensions (hidden 512, 8 heads, 6 blocks, MLP 2048; the reference's
+    block structure): one request's flow stage per step, from the per-stage split."""
+    import torch
+    alt = mt.default_config()
+    alt.flow.hidden, alt.flow.heads, alt.flow.depth, alt.flow.ff = 512, 8, 6, 2048
+    model = mt.Model(ctx, alt, seed=2, with_embeddings=True)
+    ids, noise = request_inputs(product_noise(mt), alt.vocab, alt.latent_dim, 1, 16, 8, first_request)
+    eng = mt.Engine(ctx, model, 1, 16, 8)
+    stages = stage_split(eng, 1, 16, torch.from_numpy(ids).cuda(), torch.from_numpy(noise).cuda())
+    eng.close()
+    model.close()
+    return round(dist_max(stages[1], world), 4)
 
 
+# ------------------------------------------------------------------------------------------------
+# CPU oracle (the reference's semantics on the host cores)
+# ------------------------------------------------------------------------------------------------
 def use_all_host_threads() -> int:
     """The CPU legs use every host core. torchrun sets OMP_NUM_THREADS=1 for its workers, and the
     OpenMP runtime may already be initialised by the time the oracle runs, so set both the
@@ -327,17 +442,14 @@ def use_all_host_threads() -> int:
     return n
 
 
-def cpu_oracle_rate(mt, cfg, prompt, warm_steps, timed_steps):
-    """Times the oracle's generation loop (one request) per step; returns (audio-s/s, seconds, threads)."""
+def cpu_generation_rate(oracle, hm, prompt, warm_steps, timed_steps):
+    """The oracle's generation loop for one request (128-token prompt as config 5), timed per step;
+    returns (audio-s/s, seconds of the timed steps, threads)."""
     import numpy as np
-    sys.path.insert(0, ROOT)
-    import oracle
-    arena, tensors, w, keep = host_model(mt, oracle, cfg, seed=1)
+    cfg = hm.cfg
     steps = warm_steps + timed_steps
-    ids, noise = request_inputs(mt, cfg, 1, prompt, steps, 0)
-    off = {t.name.decode(): t.offset for t in tensors}["model.model.embed_tokens.weight"]
-    table = arena[off:off + cfg.vocab * cfg.llm.hidden * 2].view(np.uint16).reshape(cfg.vocab, cfg.llm.hidden)
-    embeds = np.ascontiguousarray(oracle.bf16_to_f32(table[ids[0]]))
+    ids, noise = request_inputs(oracle_noise(oracle), cfg.vocab, cfg.latent_dim, 1, prompt, steps, 0)
+    embeds = hm.embed(ids[0])
     io = oracle.GenerateIO()
     stamps = np.zeros(steps, np.float64)
     io.prompt_rows, io.embeds, io.steps, io.cfg, io.obey_stop = prompt, embeds.ctypes.data, steps, 2.0, 0
@@ -345,51 +457,143 @@ def cpu_oracle_rate(mt, cfg, prompt, warm_steps, timed_steps):
     io.noise = n0.ctypes.data
     io.step_seconds = stamps.ctypes.data
     threads = use_all_host_threads()
-    oracle.lib().or_generate(ctypes.addressof(cfg), ctypes.addressof(w), ctypes.byref(io))
+    oracle.lib().or_generate(ctypes.addressof(cfg), ctypes.addressof(hm.weights), ctypes.byref(io))
     secs = stamps[steps - 1] - stamps[warm_steps - 1]
     return timed_steps * AUDIO_PER_STEP / secs, secs, threads
 
 
+def cpu_configs(oracle, hm):
+    """Configs 1-4 on the host cores (BASELINE's CPU plan), each a bounded sample."""
+    import numpy as np
+    threads = use_all_host_threads()
+    cfg = hm.cfg
+    out = {"cores": threads, "kind": "port",
+           "note": "CPU oracle: C restatement of the reference kernels, fp64 dot products, OpenMP over outputs"}
+    # Config 1: one decode GEMV, M = 2, W[4864x896] N(0,0.02) seed 0, X N(0,1); median of 50.
+    w = oracle.randn_bf16(4864 * 896, 0, 0.02)
+    x = oracle.gaussian_noise(2 * 896, 0)
+    y = np.zeros(2 * 4864, np.float32)
+    ts = []
+    for _ in range(50):
+        t0 = time.perf_counter()
+        oracle.linear(x, 896, 2, w, None, None, 4864, 896, y, 4864, 0)
+        ts.append(time.perf_counter() - t0)
+    t1 = statistics.median(ts)
+    out["config1"] = {"us": round(t1 * 1e6, 1), "gbs": round(8_762_368 / t1 / 1e9, 2), "sample": "median of 50 launches"}
+    # Config 2: one 24-layer LLM decode step per sequence, cache filled to 256 of 512, M = 1 and 2.
+    c = cfg.llm
+    cache = oracle.bf16_to_f32(oracle.randn_bf16(c.layers * 2 * c.kv_heads * cfg.llm_capacity * 64, 5, 1.0))
+    xin = (0.5 * oracle.gaussian_noise(c.hidden, 6)).astype(np.float32)
+    z = np.zeros(c.hidden, np.float32)
+    ts = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        oracle.lib().or_llm_decode(ctypes.addressof(hm.weights.llm), cache.ctypes.data, cfg.llm_capacity, 256,
+                                   xin.ctypes.data, 1, z.ctypes.data)
+        ts.append(time.perf_counter() - t0)
+    t2 = statistics.median(ts)
+    out["config2"] = {"ms_per_step_m1": round(t2 * 1e3, 2), "ms_per_step_m2": round(2 * t2 * 1e3, 2),
+                      "sample": "median of 3 decode steps of one sequence; M = 2 is two sequences in turn"}
+    # Config 3: one flow patch (10 CFG Euler steps of the DiT over 6 rows) at the reference dimensions.
+    zc = (0.5 * oracle.gaussian_noise(c.hidden, 7)).astype(np.float32)
+    hist = np.zeros(cfg.latent_dim, np.float32)
+    nz = oracle.gaussian_noise(cfg.latent_dim, 3)
+    yl = np.zeros(cfg.latent_dim, np.float32)
+    t0 = time.perf_counter()
+    oracle.lib().or_flow_patch(ctypes.addressof(cfg), ctypes.addressof(hm.weights), zc.ctypes.data, hist.ctypes.data,
+                               nz.ctypes.data, 2.0, yl.ctypes.data)
+    out["config3"] = {"ms_per_patch": round((time.perf_counter() - t0) * 1e3, 1), "sample": "one patch, reference dims"}
+    # Config 4: the streaming VAE decoder; 8 latents timed and scaled to the 10-s clip (125 latents).
+    sample = 8
+    lat = oracle.gaussian_noise(sample * cfg.latent_dim, 4)
+    pcm = np.zeros(sample * 4 * cfg.hop + cfg.nfft, np.float32)
+    t0 = time.perf_counter()
+    oracle.lib().or_vae_decode_clip(ctypes.addressof(cfg), ctypes.addressof(hm.weights), lat.ctypes.data, sample,
+                                    pcm.ctypes.data, pcm.size)
+    t4 = (time.perf_counter() - t0) * 125 / sample
+    out["config4"] = {"ms_per_10s_clip": round(t4 * 1e3, 1), "audio_s_per_s": round(10.0 / t4, 3),
+                      "sample": f"{sample} latents decoded (flush included), scaled to 125"}
+    return out
+
+
+def config_block(args, requests, prompt, what=None):
+    return {"workload": what or (f"config5 serving step: {requests} requests/GPU, {prompt}-token prompts, "
+                                 "1 step = LLM token + stop head + 10-step CFG flow DiT + aggregator + VAE decode of "
+                                 "one latent per request (0.08 s audio each)"),
+            "model": "Ming-3.0-tts-0.5B dims (LLM 896x24, flow/agg DiT 1024x8, VAE decoder 896x24 window 65)",
+            "requests_per_gpu": requests, "prompt_tokens": prompt, "global_batch": requests * args.gpus,
+            "parallelism": f"replicas x{args.gpus} (no data-path collective)",
+            "l2": "inputs larger than L2: ~3.6 GB of weights streamed per step"}
+
+
 # ------------------------------------------------------------------------------------------------
 def run_reference(args, rank, world):
+    """The reference arm: the reference's semantics (the CPU oracle, a C restatement of its Metal
+    kernels and generation loop) on the host cores. Loads liboracle.so only."""
     if rank != 0:
         return
-    use_all_host_threads()
-    mt = load_package()
-    cfg = mt.default_config()
-    # One step of this arm = one generation step of one request on the host cores (a bounded sample
-    # of the per-GPU workload: ~0.3 s on 16 cores); W untimed and K timed steps, K capped so the
-    # positions fit the 512-entry cache.
+    threads = use_all_host_threads()
+    oracle = load_oracle()
+    hm = oracle.model.HostModel(oracle.model.default_config(), seed=1, with_embeddings=True)
+    prompt = args.prompt
     warm = max(1, args.warmup)
-    timed = max(1, min(args.steps, cfg.llm_capacity - args.cpu_prompt - warm - 1))
-    rate, secs, threads = cpu_oracle_rate(mt, cfg, args.cpu_prompt, warm, timed)
-    sample = (f"1 request, {args.cpu_prompt}-token prompt, {warm} untimed + {timed} timed steps of the full "
-              f"model (CPU oracle: C restatement of the reference kernels, fp64 dot products, OpenMP)")
+    timed = max(1, min(args.steps, hm.cfg.llm_capacity - prompt - warm - 1))
+    rate, secs, threads = cpu_generation_rate(oracle, hm, prompt, warm, timed)
+    sample = (f"1 request with a {prompt}-token prompt (config 5's shape), prefill + {warm} untimed + {timed} timed "
+              f"steps of the full model; requests run one after another on the host, so the rate of the "
+              f"{args.requests}-request workload is the per-request rate")
     line = {"impl": "reference", "metric": METRIC, "value": round(rate, 5), "unit": "audio-s/s", "n_gpus": args.gpus,
             "steps": timed, "warmup": warm, "ms_per_step": round(secs / timed * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: random-init weights seed 1, uniform prompt ids, N(0,1) noise",
-            "config": config_block(args),
+            "config": config_block(args, args.requests, prompt,
+                                   what=f"config5 step loop on the host cores: 1 request at a time ({prompt}-token "
+                                        f"prompt), extrapolated to {args.requests} requests by the per-request rate"),
             "cpu_baseline": {"value": round(rate, 5), "unit": "audio-s/s", "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(rate, 5), "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-METRIC = "audio-sec/sec of the Ming-3.0-tts-0.5B step loop (config 5 serving, per-GPU replicas)"
-# DRAM bytes (read + write) of one launch of the roofline GEMM, from the ncu capture summarised in
-# profiles/gemm_tc_flow_ff1_m384_n4096_k1024.md (dram__bytes_read.sum + dram__bytes_write.sum).
-ROOFLINE_TRAFFIC_BYTES = 10_003_456
+def timed_steps(mt, eng, R, T, ids_d, noise_d, total, warmup, steps, local, world):
+    """W untimed steps, then K steps between CUDA events on the engine stream (barrier and
+    synchronisation on both sides); returns (max-over-ranks seconds, kernels launched, clocks)."""
+    import torch
+    stream = torch.cuda.current_stream()
+    eng.begin(R, T, token_ids=ids_d, noise=noise_d, steps=total)
+    eng.prefill()
+    for _ in range(warmup):
+        eng.step()
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kernels = 0
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(steps):
+            eng.step()
+            kernels += mt.lib().mt_engine_step_kernels(eng.handle)
+        end.record(stream)
+        end.synchronize()
+    barrier(world)
+    return dist_max(start.elapsed_time(end) * 1e-3, world), kernels, clocks
 
 
-def config_block(args):
-    return {"workload": (f"config5 serving step: {args.requests} requests/GPU, {args.prompt}-token prompts, "
-                         "1 step = LLM token + stop head + 10-step CFG flow DiT + aggregator + VAE decode of one "
-                         "latent per request (0.08 s audio each)"),
-            "model": "Ming-3.0-tts-0.5B dims (LLM 896x24, flow/agg DiT 1024x8, VAE decoder 896x24 window 65)",
-            "requests_per_gpu": args.requests, "prompt_tokens": args.prompt, "global_batch": args.requests * args.gpus,
-            "parallelism": f"replicas x{args.gpus} (no data-path collective)",
-            "l2": "inputs larger than L2: ~3.6 GB of weights streamed per step"}
+def full_run(eng, R, T, ids_d, noise_d, world):
+    """The whole config-5 generation device-timed: prefill, RUN_STEPS steps and the flush."""
+    import torch
+    stream = torch.cuda.current_stream()
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    eng.begin(R, T, token_ids=ids_d, noise=noise_d, steps=RUN_STEPS)
+    eng.prefill()
+    for _ in range(RUN_STEPS):
+        eng.step()
+    while eng.flush():
+        pass
+    end.record(stream)
+    end.synchronize()
+    return dist_max(start.elapsed_time(end) * 1e-3, world)
 
 
 def main():
@@ -398,19 +602,23 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--requests", type=int, default=64)
+    ap.add_argument("--requests", type=int, default=64, help="requests per GPU (weak scaling, the headline)")
+    ap.add_argument("--global-requests", type=int, default=64,
+                    help="requests in all for the strong-scaling leg (config 5's partitioning: this many / N per GPU)")
     ap.add_argument("--prompt", type=int, default=128)
-    ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--e2e-steps", type=int, default=RUN_STEPS)
     ap.add_argument("--cpu-steps", type=int, default=3)
-    ap.add_argument("--cpu-prompt", type=int, default=16)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="headline, full run, e2e and roofline only")
     ap.add_argument("--groups", type=int, default=0,
                     help="request groups stepped concurrently (0 = the engine's automatic choice)")
     ap.add_argument("--gemm", type=str, default="",
                     help="M,N,K[,flags]: time one tensor-core GEMM shape alone and exit (for focused profiling)")
     ap.add_argument("--gemv", type=str, default="",
                     help="N,K[,M]: time the CUDA-core GEMV over a >= 1 GiB weight pool alone and exit (for focused profiling)")
+    ap.add_argument("--decode", type=int, default=0,
+                    help="M: time the config-2 decode step at M sequences alone and exit (for focused profiling)")
     ap.add_argument("--profile", action="store_true",
                     help="prefill, warm-up and timed steps only (for a profiler's launch list); prints ms/step")
     args = ap.parse_args()
@@ -420,18 +628,16 @@ def main():
         run_reference(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
         return
     rank, world, local = dist_setup(args)
+    mt = load_package()
+    ctx = mt.Context(local)
     if args.gemm:
-        mt = load_package()
-        ctx = mt.Context(local)
         f = [int(v) for v in args.gemm.split(",")]
         m, n, k, flags = f[0], f[1], f[2], (f[3] if len(f) > 3 else 0)
-        t = time_gemm(mt, ctx, m, n, k, flags, iters=20, rounds=1)
-        print(json.dumps({"gemm": [m, n, k, flags], "us": round(t * 1e6, 2),
+        t, copies = time_gemm(mt, ctx, m, n, k, flags, rounds=1)
+        print(json.dumps({"gemm": [m, n, k, flags], "us": round(t * 1e6, 2), "pool_copies": copies,
                           "tflops": round(2.0 * m * n * k / t / 1e12, 1)}), flush=True)
         return
     if args.gemv:
-        mt = load_package()
-        ctx = mt.Context(local)
         f = [int(v) for v in args.gemv.split(",")]
         n, k, m = f[0], f[1], (f[2] if len(f) > 2 else 2)
         t, copies = time_gemv_pool(mt, ctx, n, k, m=m)
@@ -439,70 +645,47 @@ def main():
         print(json.dumps({"gemv": [m, n, k], "us": round(t * 1e6, 3), "gbs": round(nbytes / t / 1e9, 1),
                           "pool_copies": copies}), flush=True)
         return
+    cfg = mt.default_config()
+    model = mt.Model(ctx, cfg, seed=1, with_embeddings=True)
+    if args.decode:
+        t = time_decode(mt, ctx, model, cfg, args.decode)
+        print(json.dumps({"decode": args.decode, "us": round(t * 1e6, 2),
+                          "gbs": round(decode_step_bytes(cfg, args.decode, 256) / t / 1e9, 1)}), flush=True)
+        return
 
     import numpy as np
     import torch
-    mt = load_package()
-    ctx = mt.Context(local)
-    cfg = mt.default_config()
-    model = mt.Model(ctx, cfg, seed=1, with_embeddings=True)
     R, T = args.requests, args.prompt
     total_steps = args.warmup + args.steps
     assert T + total_steps <= cfg.llm_capacity, f"prompt + steps must fit the {cfg.llm_capacity}-position cache"
-    eng = mt.Engine(ctx, model, R, T, max(total_steps, args.e2e_steps), use_graphs=not args.no_graphs,
+    eng = mt.Engine(ctx, model, R, T, max(total_steps, args.e2e_steps, RUN_STEPS), use_graphs=not args.no_graphs,
                     groups=args.groups)
     first, _ = rank_requests(rank, R)
-    ids, noise = request_inputs(mt, cfg, R, T, total_steps, first)
+    ids, noise = request_inputs(product_noise(mt), cfg.vocab, cfg.latent_dim, R, T, max(total_steps, RUN_STEPS), first)
     ids_d, noise_d = torch.from_numpy(ids).cuda(), torch.from_numpy(noise).cuda()
-    stream = torch.cuda.current_stream()
 
     # ---- device-timed steps (inputs resident) ----
-    eng.begin(R, T, token_ids=ids_d, noise=noise_d, steps=total_steps)
-    eng.prefill()
-    for _ in range(args.warmup):
-        eng.step()
-    barrier(world)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    kernels = 0
     if args.profile:
         torch.cuda.cudart().cudaProfilerStart()  # a profiler started with --profile-from-start off sees only these steps
-    with ClockSampler(local) as clocks:
-        start.record(stream)
-        for _ in range(args.steps):
-            eng.step()
-            kernels += mt.lib().mt_engine_step_kernels(eng.handle)
-        end.record(stream)
-        end.synchronize()
+    t_max, kernels, clocks = timed_steps(mt, eng, R, T, ids_d, noise_d, total_steps, args.warmup, args.steps, local,
+                                         world)
     if args.profile:
         torch.cuda.cudart().cudaProfilerStop()
-    ctx.check()
-    t_local = start.elapsed_time(end) * 1e-3
-    t_max = dist_max(t_local, world)
-    value = world * R * args.steps * AUDIO_PER_STEP / t_max
-    if args.profile:
         if rank == 0:
             print(json.dumps({"profile": True, "ms_per_step": round(t_max / args.steps * 1e3, 3),
                               "kernels_per_step": kernels // max(args.steps, 1)}), flush=True)
         return
+    ctx.check()
+    value = world * R * args.steps * AUDIO_PER_STEP / t_max
 
-    # ---- per-stage split of one eager step (reference StepRecorder semantics) ----
-    eng.stage_timing(True)
-    eng.begin(R, T, token_ids=ids_d, noise=noise_d, steps=min(total_steps, 8))
-    eng.prefill()
-    stage_samples = []
-    for n in range(min(total_steps, 8)):
-        eng.step()
-        if n >= 3:
-            torch.cuda.synchronize()
-            stage_samples.append(eng.stage_ms())
-    eng.stage_timing(False)
-    stage_ms = [round(statistics.median(x[i] for x in stage_samples), 3) for i in range(4)]
+    # ---- the whole 256-step generation, device-timed ----
+    t_run = full_run(eng, R, T, ids_d, noise_d, world)
+    run_value = world * R * RUN_STEPS * AUDIO_PER_STEP / t_run
 
-    # ---- end to end through the host API ----
+    # ---- end to end through the host API, the full run ----
     E = args.e2e_steps
     ids_h = torch.from_numpy(ids).pin_memory().numpy()
-    noise_e = torch.from_numpy(np.ascontiguousarray(noise[:, :E] if E <= total_steps else
-                                                    np.resize(noise, (R, E, cfg.latent_dim)))).pin_memory().numpy()
+    noise_e = torch.from_numpy(np.ascontiguousarray(noise[:, :E])).pin_memory().numpy()
     eng.generate(R, T, noise_e, min(E, 8), ids_host=ids_h)  # warm the host path
     barrier(world)
     t0 = time.perf_counter()
@@ -512,26 +695,73 @@ def main():
     max_chunk = 4 * cfg.hop + (cfg.nfft - cfg.hop) // 2
     h2d = (ids_h.nbytes + noise_e.nbytes) / E
     d2h = (R * max_chunk * 4 * (E + 0.0) + R * 2 * 4 * E) / E
-    ttfa = time_to_first_audio(eng, R, T, noise_e, ids_h, min(E, 12), world)
-    single = single_request(mt, ctx, model, cfg, first + R, world)
 
-    # ---- kernel roofline: the tcgen05 GEMM at the flow-DiT ff1 shape; decode GEMV (config 1) ----
+    # ---- strong scaling: config 5's 64 requests partitioned over the N GPUs ----
+    strong = None
+    if world > 1 and args.global_requests % world == 0:
+        Rs = args.global_requests // world
+        first_s, _ = rank_requests(rank, Rs)
+        ids_s, noise_s = request_inputs(product_noise(mt), cfg.vocab, cfg.latent_dim, Rs, T, total_steps, first_s)
+        t_s, _, _ = timed_steps(mt, eng, Rs, T, torch.from_numpy(ids_s).cuda(), torch.from_numpy(noise_s).cuda(),
+                                total_steps, args.warmup, args.steps, local, world)
+        strong = {"global_requests": args.global_requests, "requests_per_gpu": Rs,
+                  "value": round(args.global_requests * args.steps * AUDIO_PER_STEP / t_s, 2),
+                  "ms_per_step": round(t_s / args.steps * 1e3, 3), "unit": "audio-s/s"}
+    elif world == 1 and args.global_requests == R:
+        strong = {"global_requests": R, "requests_per_gpu": R, "value": round(value, 2),
+                  "ms_per_step": round(t_max / args.steps * 1e3, 3), "unit": "audio-s/s",
+                  "note": "one GPU: the headline run itself"}
+
+    # ---- kernel roofline: the tcgen05 GEMM at the flow-DiT ff1 shape ----
     hbm_peak, bf16_peak, peak_kind = peaks()
     M, N, K = 6 * R, cfg.flow.ff, cfg.flow.hidden
-    t_gemm = time_gemm(mt, ctx, M, N, K, mt.GELU)
-    flops = 2.0 * M * N * K
-    achieved = flops / t_gemm / 1e12
-    t_gv, copies = time_gemv_pool(mt, ctx, 4864, 896)
-    gv_bytes = 4864 * 896 * 2 + 2 * 896 * 4 + 2 * 4864 * 4
-    t_gv_down, _ = time_gemv_pool(mt, ctx, 896, 4864)
-    gv_down_bytes = 896 * 4864 * 2 + 2 * 4864 * 4 + 2 * 896 * 4
+    t_gemm, gemm_copies = time_gemm(mt, ctx, M, N, K, mt.GELU)
+    achieved = 2.0 * M * N * K / t_gemm / 1e12
 
-    cpu = None
+    extra = {}
+    if not args.quick:
+        stage_ms = stage_split(eng, R, T, ids_d, noise_d)
+        ttfa = time_to_first_audio(eng, R, T, noise_e, ids_h, 12, world)
+        single = single_request(mt, ctx, model, cfg, first + R, world)
+        single["config3_alt_dims_flow_patch_ms"] = alt_dit_patch(mt, ctx, cfg, first + R + 1, world)
+        t_gv, copies = time_gemv_pool(mt, ctx, 4864, 896)
+        gv_bytes = 4864 * 896 * 2 + 2 * 896 * 4 + 2 * 4864 * 4
+        t_gv_down, _ = time_gemv_pool(mt, ctx, 896, 4864)
+        gv_down_bytes = 896 * 4864 * 2 + 2 * 4864 * 4 + 2 * 896 * 4
+        decode = {}
+        for m in (1, 2):
+            t_d = dist_max(time_decode(mt, ctx, model, cfg, m), world)
+            nb = decode_step_bytes(cfg, m, 256)
+            decode[f"m{m}"] = {"us_per_step": round(t_d * 1e6, 2), "bytes_per_step": nb,
+                               "gbs": round(nb / t_d / 1e9, 1), "frac": round(nb / t_d / 1e9 / hbm_peak, 4)}
+        decode["shape"] = "config 2: 24-layer LLM decode + stop head, KV cache 256 of 512 positions, M sequences"
+        decode["peak_gbs"] = hbm_peak
+        extra = {
+            "ttfa_ms": {"p50": round(ttfa[0] * 1e3, 2), "calls": ttfa[1], "requests_per_call": R,
+                        "includes": "ids+noise H2D, prefill of all requests, steps 0-2, first PCM chunk D2H "
+                                    "(mt_engine_generate_stream callback)"},
+            "gemv": {"shape": "config 1: M=2 W[4864x896] bf16, fp32 x/y", "gbs": round(gv_bytes / t_gv / 1e9, 1),
+                     "frac": round(gv_bytes / t_gv / 1e9 / hbm_peak, 4), "us": round(t_gv * 1e6, 3),
+                     "down_proj_gbs": round(gv_down_bytes / t_gv_down / 1e9, 1),
+                     "pool": f"{copies} distinct weight copies (>= 1 GiB), graph replay",
+                     "peak_gbs": hbm_peak, "peak_kind": peak_kind},
+            "decode": decode,
+            "single_request": single,
+            "stages_ms": {"llm": stage_ms[0], "flow": stage_ms[1], "agg": stage_ms[2], "vae_concurrent": stage_ms[3],
+                          "note": "one eager step, events per stage; the VAE decode runs on a second stream"},
+        }
+
+    cpu, cpu_cfgs = None, None
     if rank == 0 and world == 1 and not args.no_cpu:
-        rate, secs, threads = cpu_oracle_rate(mt, cfg, args.cpu_prompt, 1, args.cpu_steps)
+        oracle = load_oracle()
+        hm = oracle.model.HostModel(oracle.model.default_config(), seed=1, with_embeddings=True)
+        rate, secs, threads = cpu_generation_rate(oracle, hm, T, 1, args.cpu_steps)
         cpu = {"value": round(rate, 5), "unit": "audio-s/s", "cores": threads, "kind": "port",
-               "sample": f"1 request, {args.cpu_prompt}-token prompt, 1 untimed + {args.cpu_steps} timed steps of the "
-                         "full model on the CPU oracle (C restatement, fp64 dot products, OpenMP)"}
+               "sample": f"1 request, {T}-token prompt, prefill + 1 untimed + {args.cpu_steps} timed steps of the full "
+                         "model on the CPU oracle (C restatement, fp64 dot products, OpenMP); the per-request rate "
+                         "is the rate of the 64-request workload on the host"}
+        if not args.quick:
+            cpu_cfgs = cpu_configs(oracle, hm)
 
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "audio-s/s", "n_gpus": world, "steps": args.steps,
@@ -539,31 +769,28 @@ def main():
                 "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32 (bf16 weights; tensor-core GEMMs on bf16 hi+lo activation pairs, fp32 accumulate)",
                 "data": "synthetic: random-init weights seed 1, uniform prompt ids per request seed, N(0,1) noise",
-                "config": config_block(args),
+                "config": config_block(args, R, T),
+                "full_run": {"value": round(run_value, 2), "unit": "audio-s/s", "steps": RUN_STEPS,
+                             "ms": round(t_run * 1e3, 2),
+                             "includes": "prefill, 256 steps (positions 128-383), flush; device-timed, inputs resident"},
                 "e2e": {"value": round(e2e_value, 2), "unit": "audio-s/s", "steps": E,
                         "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                         "includes": "ids+noise H2D, prefill, steps, flush, PCM+stop D2H (mt_engine_generate)"},
-                "ttfa_ms": {"p50": round(ttfa[0] * 1e3, 2), "calls": ttfa[1], "requests_per_call": R,
-                            "includes": "ids+noise H2D, prefill of all requests, steps 0-2, first PCM chunk D2H "
-                                        "(mt_engine_generate_stream callback)"},
+                "strong": strong,
                 "roofline": {"kernel": "gemm_tc_kernel (flow DiT ff1, GELU, hi/lo out)",
                              "shape": f"M={M} N={N} K={K}", "bound": "tensor", "achieved": round(achieved, 1),
                              "peak": bf16_peak, "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 4),
                              "peak_kind": f"{peak_kind} bf16 dense (burst)",
-                             "note": "algorithmic 2MNK; the fp32-faithful hi+lo split issues 2 bf16 MMAs per product",
+                             "note": "algorithmic 2MNK; the fp32-faithful hi+lo split issues 2 bf16 MMAs per product, "
+                                     f"so 0.5 of peak is the cap; weights from a pool of {gemm_copies} copies (> L2)",
                              "ms_per_launch": round(t_gemm * 1e3, 4), "traffic": ROOFLINE_TRAFFIC_BYTES,
-                             "traffic_unit": "bytes per launch (ncu dram read+write)"},
-                "gemv": {"shape": "config 1: M=2 W[4864x896] bf16, fp32 x/y", "gbs": round(gv_bytes / t_gv / 1e9, 1),
-                         "frac": round(gv_bytes / t_gv / 1e9 / hbm_peak, 4), "us": round(t_gv * 1e6, 3),
-                         "down_proj_gbs": round(gv_down_bytes / t_gv_down / 1e9, 1),
-                         "pool": f"{copies} distinct weight copies (>= 1 GiB), graph replay",
-                         "peak_gbs": hbm_peak, "peak_kind": peak_kind},
-                "single_request": single,
-                "stages_ms": {"llm": stage_ms[0], "flow": stage_ms[1], "agg": stage_ms[2], "vae_concurrent": stage_ms[3],
-                              "note": "one eager step, events per stage; the VAE decode runs on a second stream"},
+                             "traffic_source": "ncu capture of one launch at this shape (dram read+write bytes)"},
                 "gpu_launches": kernels, "clocks": clocks.summary()}
+        line.update(extra)
         if cpu:
             line["cpu_baseline"] = cpu
+        if cpu_cfgs:
+            line["configs_cpu"] = cpu_cfgs
         print(json.dumps(line), flush=True)
     eng.close()
     model.close()

@@ -163,6 +163,17 @@ const char* mt_version(void);
  * Returns MT_ERR_TIMEOUT if a kernel gave up a wait, MT_ERR_CUDA on a CUDA error.
  * Replaces the command-buffer error check of StepRecorder.finish (Engine.swift:70-85). */
 mt_status mt_ctx_check(mt_ctx* ctx, void* stream);
+/* Wall-time limit of every bounded device wait of kernels launched with ctx (mbarrier waits on
+ * asynchronous copies and tensor-core commits): `microseconds`, or 0 for the default of 2 s. A wait
+ * that runs out records MT_ERR_TIMEOUT for mt_ctx_check and ends its kernel early (its outputs are
+ * then incomplete). Synchronous; applies to kernels launched after it returns. No counterpart in the
+ * reference, whose command-buffer errors surface at StepRecorder.finish (Engine.swift:70-85). */
+mt_status mt_ctx_set_wait_limit(mt_ctx* ctx, unsigned int microseconds);
+/* Failure-detection check: enqueues a one-thread kernel whose bounded wait nothing completes (a
+ * shared-memory barrier that no one arrives on, no copy in flight). It gives up after the wait limit
+ * and records a timeout, so the next mt_ctx_check returns MT_ERR_TIMEOUT and clears it; the context
+ * then works as before. No counterpart in the reference. */
+mt_status mt_ctx_wait_probe(mt_ctx* ctx, void* stream);
 /* Tensor-core GEMM tiling for plans made on ctx from now on: -1 automatic (default), 0 single-CTA
  * tiles of 128 weight rows, 1 CTA pairs (clusters of two SMs sharing 256-weight-row tiles through
  * tcgen05 cta_group::2). Results agree to rounding; the choice only changes speed. No counterpart
@@ -210,10 +221,16 @@ mt_status mt_linear_split(mt_ctx* ctx, void* stream, const mt_bf16* x_hi, const 
  * (larger calls return MT_ERR_CAPACITY). The first call on a device looks up the array's device
  * address with that device current; make that first call before any stream capture. Every call on
  * a device uses the same array, so calls that can overlap on the GPU (streams not ordered with each
- * other) race and corrupt each other's results: order them. Errors are reported by the status only
- * (there is no context for a message). Has no counterpart in the reference. */
+ * other) race and corrupt each other's results: order them. Argument and launch errors are reported
+ * by the returned status only (there is no context for a message); a bounded device wait that gives
+ * up while the call runs on the GPU is recorded in a status word of the library's own on that device
+ * and reported by mt_linear_static_status. Has no counterpart in the reference. */
 mt_status mt_linear_static(void* stream, const float* x, int ldx, int m, const mt_bf16* w, const mt_bf16* w2,
                            const mt_bf16* bias, int n, int k, float* y, int ldy, uint32_t flags);
+/* Synchronises `stream`, then reads and clears the device-side status of mt_linear_static on the
+ * current device: MT_ERR_TIMEOUT if one of its kernels gave up a bounded wait since the last query
+ * (that call's y is incomplete), MT_OK otherwise, MT_ERR_CUDA on a CUDA error. Allocates nothing. */
+mt_status mt_linear_static_status(void* stream);
 
 /* y = x * rsqrt(mean(x^2) + eps) * w per row. Replaces Encoder.rmsnorm (Kernels.swift:163-171),
  * kernel rmsnorm (Shaders.swift:418-441). width % 4 == 0. */
@@ -245,6 +262,21 @@ mt_status mt_attention(mt_ctx* ctx, void* stream, const float* q, int ldq, int m
 mt_status mt_rope_attention(mt_ctx* ctx, void* stream, const float* qkv, int ldq, int m, int hq, int hkv, int pos0,
                             int window, float* k_cache, float* v_cache, int capacity, const float* inv_freq,
                             float* out, int ldo, int chunk_keys);
+
+/* One decode pass of a Qwen stack (QwenForward.dispatches, Qwen.swift:72-97) for `requests`
+ * independent sequences of `rows` new rows each (rows <= 4, requests * rows <= 8): the reference's LLM
+ * decode token (one row, Engine.swift:381-385) and VAE frame decode (four rows, VAEDecoder.swift:86-107).
+ * x [requests * rows, hidden] fp32: the new rows' residual stream (the input embeddings), updated in
+ * place to the stream after the last layer; z [requests * rows, hidden]: the final norm of every row
+ * (normRows = rows). Request r's cache starts at kv + r * kv_stride floats, laid out
+ * [layers][K|V][kv_heads][capacity][64] fp32 (KVCache, Qwen.swift:7-26), slot = position % capacity;
+ * positions (device int32 [requests]) = tokens already cached per request; the new rows take
+ * positions[r] .. positions[r] + rows - 1 and are appended. With w->cfg.window == 0 the caller keeps
+ * positions[r] + rows <= capacity; with a window the cache may be a ring (window + rows - 1 <= capacity).
+ * Replaces the decode use of QwenForward.dispatches; scratch comes from the context (the first call
+ * with a given shape and rope theta sets it up synchronously, so make it before any stream capture). */
+mt_status mt_qwen_decode(mt_ctx* ctx, void* stream, const mt_qwen_weights* w, int requests, int rows, float* x,
+                         float* kv, long long kv_stride, int capacity, const int32_t* positions, float* z);
 
 /* Full attention over `batch` sequences of `seq` <= 8 rows with interleaved RoPE (pairs 2l, 2l+1,
  * angle = row * inv_freq[l]). qkv rows are [q | k | v] of heads*64 each, row stride ld.

@@ -116,14 +116,18 @@ PROTOTYPES = {
     "mt_ctx_check": (c_int, [_P, _P]),
     "mt_linear_route": (c_int, [c_int, c_int, c_int]),
     "mt_ctx_set_gemm_pairs": (c_int, [_P, c_int]),
+    "mt_ctx_set_wait_limit": (c_int, [_P, c_uint32]),
+    "mt_ctx_wait_probe": (c_int, [_P, _P]),
     "mt_linear": (c_int, [_P, _P, _P, c_int, c_int, _P, _P, _P, c_int, c_int, _P, c_int, c_uint32]),
     "mt_linear_split": (c_int, [_P, _P, _P, _P, c_int, c_int, _P, _P, _P, c_int, c_int, _P, c_int, _P, _P, c_int,
                                 c_uint32]),
     "mt_linear_static": (c_int, [_P, _P, c_int, c_int, _P, _P, _P, c_int, c_int, _P, c_int, c_uint32]),
+    "mt_linear_static_status": (c_int, [_P]),
     "mt_rmsnorm": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P, _P, c_int, c_float]),
     "mt_rope_attention": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, c_int, _P, _P, c_int,
                                   c_int]),
     "mt_copy": (c_int, [_P, _P, _P, c_int, _P]),
+    "mt_qwen_decode": (c_int, [_P, _P, _P, c_int, c_int, _P, _P, ctypes.c_longlong, c_int, _P, _P]),
     "mt_rope_cache": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, _P, c_int, _P]),
     "mt_attention": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, c_int, _P, c_int]),
     "mt_dit_attention": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, c_int]),
@@ -252,6 +256,15 @@ class Context:
         conv = [ptr(a) if (hasattr(a, "data_ptr") or hasattr(a, "ctypes")) else a for a in args]
         st = fn(self._ctx, stream if stream is not None else current_stream(), *conv)
         self._check(st, "mt_" + name)
+
+    def set_wait_limit(self, microseconds: int):
+        """Wall-time limit of the kernels' bounded waits (0 = the default 2 s)."""
+        self._check(lib().mt_ctx_set_wait_limit(self._ctx, microseconds), "mt_ctx_set_wait_limit")
+
+    def wait_probe(self, stream=None):
+        """Enqueues a kernel whose bounded wait runs out; the next check() raises MT_ERR_TIMEOUT."""
+        self._check(lib().mt_ctx_wait_probe(self._ctx, stream if stream is not None else current_stream()),
+                    "mt_ctx_wait_probe")
 
     def set_gemm_pairs(self, mode: int):
         """Tensor-core GEMM tiling for later plans: -1 automatic, 0 single-CTA tiles, 1 CTA pairs."""

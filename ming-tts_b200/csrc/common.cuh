@@ -4,7 +4,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <string>
+#include <utility>
 
 #include "../../include/mingcuda.h"
 
@@ -15,10 +17,12 @@
 struct mt_ctx {
     int device = 0;
     int sm_count = 0;
-    unsigned int* d_status = nullptr;  // [0] = error code, [1] = site id, [2] = detail
+    unsigned int* d_status = nullptr;  // [0] = error code, [1] = site id, [2] = detail, [3] = wait limit (us)
     void* scratch = nullptr;           // grows on demand, see mt_scratch()
     size_t scratch_bytes = 0;
     int gemm_pairs = -1;               // tensor-core GEMM CTA pairs: -1 automatic, 0 never, 1 where valid
+    float* rope = nullptr;             // [32] NeoX rotation frequencies for rope_theta (mt_qwen_decode)
+    float rope_theta = 0.f;
     std::string err;
 };
 
@@ -37,7 +41,29 @@ mt_status check_launch(mt_ctx* ctx, const char* what);
 // Returns a device buffer of at least `bytes` owned by ctx. Grows (synchronising `stream` first)
 // when too small.
 mt_status scratch(mt_ctx* ctx, cudaStream_t stream, size_t bytes, void** out);
+// Device table of the 32 NeoX inverse frequencies theta^(-2i/64) (Qwen.swift:60), computed on the
+// host in fp32 as the reference does and kept by the context; uploads synchronously when theta
+// changes (so the first call with a theta must not be inside a stream capture).
+mt_status rope_table(mt_ctx* ctx, float theta, const float** out);
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Runs a set-up step once per CUDA device, on the first call with that device current. Function
+// attributes such as the dynamic shared-memory opt-in belong to the function in one device's
+// context, so a process that drives several GPUs needs them set on each; several host threads
+// may reach the first call at once.
+constexpr int kMaxDevices = 64;
+struct PerDeviceOnce {
+    std::once_flag flags[kMaxDevices];
+    template <typename F>
+    void operator()(F&& f) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+            f();
+            return;
+        }
+        std::call_once(flags[dev], std::forward<F>(f));
+    }
+};
 
 }  // namespace mt
 
@@ -193,15 +219,22 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
-constexpr uint64_t MBAR_WAIT_NS = 2000000000ull;  // 2 s per wait
+constexpr uint64_t MBAR_WAIT_NS = 2000000000ull;  // 2 s per wait unless the status word sets a limit
 
-// Bounded wait on the phase with the given parity: gives up after MBAR_WAIT_NS of wall time
+// Wall-time limit of one bounded wait: word 3 of the status word holds it in microseconds
+// (mt_ctx_set_wait_limit); 0 or no status word means MBAR_WAIT_NS.
+__device__ __forceinline__ uint64_t wait_limit_ns(const unsigned int* status) {
+    const unsigned int us = status ? *reinterpret_cast<const volatile unsigned int*>(status + 3) : 0u;
+    return us ? (uint64_t)us * 1000ull : MBAR_WAIT_NS;
+}
+
+// Bounded wait on the phase with the given parity: gives up after the wait limit of wall time
 // (checked every 256 polls) or as soon as another thread of the CTA has raised *abort; a wait that
 // times out records the site in the status word, raises *abort and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status, unsigned site,
                                           volatile int* abort) {
     const uint32_t addr = smem_u32(bar);
-    uint64_t t0 = 0;
+    uint64_t t0 = 0, limit = 0;
     for (uint32_t i = 0;; i++) {
         uint32_t ok;
         asm volatile(
@@ -215,8 +248,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
         if ((i & 255u) == 255u) {
             if (*abort) return false;
             const uint64_t now = global_ns();
-            if (t0 == 0) t0 = now;
-            else if (now - t0 > MBAR_WAIT_NS) break;
+            if (t0 == 0) {
+                t0 = now;
+                limit = wait_limit_ns(status);
+            } else if (now - t0 > limit) {
+                break;
+            }
         }
     }
     report_status(status, mt::DEV_TIMEOUT, site, blockIdx.x);

@@ -44,6 +44,39 @@ mt_status scratch(mt_ctx* ctx, cudaStream_t stream, size_t bytes, void** out) {
     return MT_OK;
 }
 
+// A bounded wait that nothing completes: one thread initialises a shared-memory barrier expecting
+// one arrival, never arrives on it and waits for its first phase. The wait gives up after the
+// context's wait limit and records DEV_TIMEOUT at site 90 in the status word; no asynchronous copy
+// is in flight, so the kernel simply returns and the context stays usable.
+__global__ void wait_probe_kernel(unsigned int* status) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    pdl_wait();
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        mbar_init(&bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_wait(&bar, 0, status, 90, &abort_flag);
+    }
+}
+
+mt_status rope_table(mt_ctx* ctx, float theta, const float** out) {
+    if (!ctx->rope) {
+        cudaError_t e = cudaMalloc(&ctx->rope, 32 * sizeof(float));
+        if (e != cudaSuccess) return fail(ctx, MT_ERR_NOMEM, "rope table: %s", cudaGetErrorString(e));
+        ctx->rope_theta = 0.f;
+    }
+    if (ctx->rope_theta != theta) {
+        float inv[32];
+        for (int i = 0; i < 32; i++) inv[i] = 1.0f / powf(theta, (float)(2 * i) / 64.0f);
+        cudaError_t e = cudaMemcpy(ctx->rope, inv, sizeof(inv), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "rope table upload: %s", cudaGetErrorString(e));
+        ctx->rope_theta = theta;
+    }
+    *out = ctx->rope;
+    return MT_OK;
+}
+
 }  // namespace mt
 
 extern "C" {
@@ -76,6 +109,7 @@ void mt_ctx_destroy(mt_ctx* ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->rope) cudaFree(ctx->rope);
     if (ctx->d_status) cudaFree(ctx->d_status);
     delete ctx;
 }
@@ -92,12 +126,26 @@ mt_status mt_ctx_check(mt_ctx* ctx, void* stream) {
     e = cudaMemcpy(st, ctx->d_status, sizeof(st), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return mt::fail(ctx, MT_ERR_CUDA, "status read: %s", cudaGetErrorString(e));
     if (st[0] != mt::DEV_OK) {
-        cudaMemset(ctx->d_status, 0, sizeof(st));
+        cudaMemset(ctx->d_status, 0, 3 * sizeof(unsigned int));  // word 3 (the wait limit) stays
         if (st[0] == mt::DEV_TIMEOUT)
             return mt::fail(ctx, MT_ERR_TIMEOUT, "device wait gave up (site %u, detail %u)", st[1], st[2]);
         return mt::fail(ctx, MT_ERR_ARG, "device check failed (code %u, site %u, detail %u)", st[0], st[1], st[2]);
     }
     return MT_OK;
+}
+
+mt_status mt_ctx_set_wait_limit(mt_ctx* ctx, unsigned int microseconds) {
+    if (!ctx) return MT_ERR_ARG;
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e == cudaSuccess) e = cudaMemcpy(ctx->d_status + 3, &microseconds, sizeof(unsigned int), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return mt::fail(ctx, MT_ERR_CUDA, "mt_ctx_set_wait_limit: %s", cudaGetErrorString(e));
+    return MT_OK;
+}
+
+mt_status mt_ctx_wait_probe(mt_ctx* ctx, void* stream) {
+    if (!ctx) return MT_ERR_ARG;
+    launch_k(mt::wait_probe_kernel, 1, 32, 0, mt::as_stream(stream), ctx->d_status);
+    return mt::check_launch(ctx, "mt_ctx_wait_probe");
 }
 
 mt_status mt_write_wav_f32(const char* path, const float* samples, long long count, int sample_rate) {

@@ -1,0 +1,110 @@
+// decode.cu -- mt_qwen_decode: one decode pass of a Qwen stack for a few rows (<= 8 in all).
+//
+// Reference: QwenForward.dispatches (Sources/MingTTS/Engine/Qwen.swift:72-97) as the LLM decode
+// token runs it (one row, Engine.swift:381-385) and as the VAE decoder runs its four frame rows
+// (VAEDecoder.swift:86-107), over caller-owned fp32 KV caches in the reference's layout
+// (Qwen.swift:7-26). Per layer: RMSNorm -> q/k/v GEMV (+bias) -> RoPE + KV append + attention ->
+// o GEMV (+=) -> RMSNorm -> gate/up GEMV (SiLU gate) -> down GEMV (+=); then the final norm of every
+// row.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mt {
+
+namespace {
+
+constexpr int kDecodeMaxRows = 8;  // rows of all requests together: the CUDA-core GEMV route
+
+// Scratch of one call, carved from the context's scratch area (fp32): normed rows, q/k/v rows,
+// attention rows and the gated MLP rows.
+struct DecodeScratch {
+    float *normed, *qkv, *attn, *mlp;
+};
+
+size_t decode_scratch_floats(const mt_qwen_config& c, int M) {
+    const size_t qkvw = (size_t)(c.heads + 2 * c.kv_heads) * 64;
+    auto up = [](size_t n) { return (n + 63) & ~size_t(63); };  // 256-byte aligned pieces
+    return up((size_t)M * c.hidden) + up((size_t)M * qkvw) + up((size_t)M * c.heads * 64) + up((size_t)M * c.intermediate);
+}
+
+DecodeScratch carve(float* base, const mt_qwen_config& c, int M) {
+    const size_t qkvw = (size_t)(c.heads + 2 * c.kv_heads) * 64;
+    auto up = [](size_t n) { return (n + 63) & ~size_t(63); };
+    DecodeScratch s;
+    s.normed = base;
+    s.qkv = s.normed + up((size_t)M * c.hidden);
+    s.attn = s.qkv + up((size_t)M * qkvw);
+    s.mlp = s.attn + up((size_t)M * c.heads * 64);
+    return s;
+}
+
+void gemv(const float* x, int ldx, int m, const uint16_t* w, const uint16_t* w2, const uint16_t* bias, int n, int k,
+          float* y, int ldy, uint32_t flags, cudaStream_t s) {
+    LinearArgs a{};
+    a.x = x; a.ldx = ldx; a.m = m; a.n = n; a.k = k; a.w = w; a.w2 = w2; a.bias = bias;
+    a.y = y; a.ldy = ldy; a.flags = flags; a.split_k = 1;
+    launch_gemv(a, s);
+}
+
+void norm(const float* x, int ld, int rows, int width, const uint16_t* g, float eps, float* y, cudaStream_t s) {
+    RmsArgs a{};
+    a.x = x; a.ldx = ld; a.rows = rows; a.width = width; a.w = g; a.eps = eps; a.y = y; a.ldy = ld;
+    launch_rmsnorm(a, s);
+}
+
+}  // namespace
+
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" mt_status mt_qwen_decode(mt_ctx* ctx, void* stream, const mt_qwen_weights* w, int requests, int rows,
+                                    float* x, float* kv, long long kv_stride, int capacity, const int32_t* positions,
+                                    float* z) {
+    MT_REQUIRE(ctx, ctx && w && x && kv && positions && z && w->layers && w->final_norm, MT_ERR_ARG,
+               "mt_qwen_decode: null argument");
+    const mt_qwen_config& c = w->cfg;
+    const int M = requests * rows;
+    MT_REQUIRE(ctx, requests >= 1 && rows >= 1 && M <= kDecodeMaxRows && attention_decode_supported(rows, c.heads, c.kv_heads),
+               MT_ERR_SHAPE, "mt_qwen_decode: %d requests x %d rows (rows <= %d, at most %d rows in all; heads %d/%d)",
+               requests, rows, ATTN_DECODE_MAX_ROWS, kDecodeMaxRows, c.heads, c.kv_heads);
+    MT_REQUIRE(ctx, c.layers >= 1 && c.hidden % 8 == 0 && c.intermediate % 8 == 0 && c.heads * 64 % 8 == 0 && c.window >= 0,
+               MT_ERR_SHAPE, "mt_qwen_decode: hidden %d intermediate %d", c.hidden, c.intermediate);
+    const long long cache_floats = (long long)c.layers * 2 * c.kv_heads * capacity * 64;
+    MT_REQUIRE(ctx, capacity > 0 && kv_stride >= cache_floats && kv_stride % 4 == 0 &&
+                        (c.window == 0 || c.window + rows - 1 <= capacity),
+               MT_ERR_CAPACITY, "mt_qwen_decode: capacity %d, request stride %lld floats (needs %lld), window %d",
+               capacity, kv_stride, cache_floats, c.window);
+    MT_REQUIRE(ctx, ((uintptr_t)x & 15u) == 0 && ((uintptr_t)kv & 15u) == 0 && ((uintptr_t)z & 15u) == 0, MT_ERR_ARG,
+               "mt_qwen_decode: x, kv and z need 16-byte alignment");
+    cudaStream_t s = as_stream(stream);
+    const float* inv_freq = nullptr;
+    mt_status st = rope_table(ctx, c.rope_theta, &inv_freq);
+    if (st != MT_OK) return st;
+    void* buf = nullptr;
+    st = mt::scratch(ctx, s, decode_scratch_floats(c, M) * sizeof(float), &buf);
+    if (st != MT_OK) return st;
+    DecodeScratch sc = carve(static_cast<float*>(buf), c, M);
+
+    const int H = c.hidden, qkvw = (c.heads + 2 * c.kv_heads) * 64, A = c.heads * 64;
+    const size_t tensor = (size_t)c.kv_heads * capacity * 64;
+    for (int l = 0; l < c.layers; l++) {
+        const mt_qwen_layer& L = w->layers[l];
+        float* kc = kv + (size_t)(2 * l) * tensor;
+        norm(x, H, M, H, L.norm1, c.eps, sc.normed, s);
+        gemv(sc.normed, H, M, L.qkv_w, nullptr, L.qkv_b, qkvw, H, sc.qkv, qkvw, MT_LINEAR_BIAS, s);
+        AttnDecodeArgs da{};
+        da.qkv = sc.qkv; da.ldq = qkvw; da.requests = requests; da.rows_per_req = rows; da.hq = c.heads;
+        da.hkv = c.kv_heads; da.pos0 = 0; da.pos_dev = positions; da.window = c.window; da.kc = kc; da.vc = kc + tensor;
+        da.req_stride = kv_stride; da.cap = capacity; da.inv_freq = inv_freq; da.out = sc.attn; da.ldo = A;
+        da.max_keys = c.window > 0 ? c.window : capacity; da.status = ctx->d_status;
+        launch_attention_decode(da, s);
+        gemv(sc.attn, A, M, L.o_w, nullptr, nullptr, H, A, x, H, MT_LINEAR_ACCUM, s);
+        norm(x, H, M, H, L.norm2, c.eps, sc.normed, s);
+        gemv(sc.normed, H, M, L.gate_w, L.up_w, nullptr, c.intermediate, H, sc.mlp, c.intermediate, MT_LINEAR_SILU_GATE,
+             s);
+        gemv(sc.mlp, c.intermediate, M, L.down_w, nullptr, nullptr, H, c.intermediate, x, H, MT_LINEAR_ACCUM, s);
+    }
+    norm(x, H, M, H, w->final_norm, c.eps, z, s);
+    return check_launch(ctx, "mt_qwen_decode");
+}

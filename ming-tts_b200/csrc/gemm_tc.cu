@@ -826,22 +826,24 @@ static GemmKernel gemm_kernel_for(bool gated, int kind, int ka) {
     return ka == 2 ? gemm_kernel_ka<2>(gated, kind) : gemm_kernel_ka<1>(gated, kind);
 }
 
-// Shared-memory opt-in for every instantiation (once per process; plans exist per device but the
-// attribute is per function).
+// Shared-memory opt-in for every instantiation, once per device (the attribute belongs to the
+// function in the current device's context).
 static void set_gemm_attributes() {
-    static bool done = false;
-    if (done) return;
-    const int kinds[] = {EPI_GENERIC, EPI_F32, EPI_F32_ACCUM, EPI_SPLIT, EPI_SPLIT_GELU, EPI_SPLIT_GATE,
-                         EPI_F32_SILU, EPI_RED};
-    for (int kd : kinds) {
-        for (int ka = 1; ka <= TC_KA_MAX; ka++) {
-            cudaFuncSetAttribute(gemm_kernel_for(false, kd, ka), cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
-            cudaFuncSetAttribute(gemm_kernel_for(true, kd, ka), cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+    static PerDeviceOnce once;
+    once([] {
+        const int kinds[] = {EPI_GENERIC, EPI_F32, EPI_F32_ACCUM, EPI_SPLIT, EPI_SPLIT_GELU, EPI_SPLIT_GATE,
+                             EPI_F32_SILU, EPI_RED};
+        for (int kd : kinds) {
+            for (int ka = 1; ka <= TC_KA_MAX; ka++) {
+                cudaFuncSetAttribute(gemm_kernel_for(false, kd, ka), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     201 * 1024);
+                cudaFuncSetAttribute(gemm_kernel_for(true, kd, ka), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     201 * 1024);
+            }
         }
-    }
-    cudaFuncSetAttribute(gemm_tc_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
-    cudaFuncSetAttribute(gemm_tc_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
-    done = true;
+        cudaFuncSetAttribute(gemm_tc_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+        cudaFuncSetAttribute(gemm_tc_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 201 * 1024);
+    });
 }
 
 mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
@@ -931,9 +933,9 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     return MT_OK;
 }
 
-// Plan for callers without a context (mt_linear_static): no split-K, no status word, no error
-// strings; returns MT_ERR_CUDA only if a tensor map cannot be encoded. Inputs are validated by
-// the caller.
+// Plan for callers without a context (mt_linear_static): no split-K, no error strings; returns
+// MT_ERR_CUDA only if a tensor map cannot be encoded. Inputs are validated by the caller, which
+// also sets e.status (the plan leaves it null: a wait that gives up then records nothing).
 mt_status make_gemm_plan_bare(int sm_count, const LinearArgs& a, GemmPlan* plan) {
     const bool gated = (a.flags & MT_LINEAR_SILU_GATE) != 0;
     TcEpi& e = plan->e;

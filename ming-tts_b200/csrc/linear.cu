@@ -35,7 +35,7 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[MR], float (&acc2)[MR], 
 }
 
 template <int MR, int G, bool GATED>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(LinearArgs a) {
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(LinearArgs a) {
     constexpr int C = GEMV_THREADS / G;  // columns per block
     constexpr int U = G >= 128 ? 8 : 4;  // chunks per thread loaded ahead of the dependency wait
     __shared__ float red[GATED ? 2 : 1][GEMV_THREADS / 32][MR];
@@ -141,11 +141,11 @@ static void launch_gemv_g(const LinearArgs& a, int G, cudaStream_t s) {
     const int C = GEMV_THREADS / G;
     dim3 grid((a.n + C - 1) / C, (a.m + MR - 1) / MR);
     switch (G) {
-        case 8: launch_k(gemv_kernel<MR, 8, GATED>, grid, GEMV_THREADS, 0, s, a); break;
-        case 16: launch_k(gemv_kernel<MR, 16, GATED>, grid, GEMV_THREADS, 0, s, a); break;
-        case 32: launch_k(gemv_kernel<MR, 32, GATED>, grid, GEMV_THREADS, 0, s, a); break;
-        case 64: launch_k(gemv_kernel<MR, 64, GATED>, grid, GEMV_THREADS, 0, s, a); break;
-        default: launch_k(gemv_kernel<MR, 128, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        case 8: launch_k(gemv_stream_kernel<MR, 8, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        case 16: launch_k(gemv_stream_kernel<MR, 16, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        case 32: launch_k(gemv_stream_kernel<MR, 32, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        case 64: launch_k(gemv_stream_kernel<MR, 64, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        default: launch_k(gemv_stream_kernel<MR, 128, GATED>, grid, GEMV_THREADS, 0, s, a); break;
     }
 }
 

@@ -20,30 +20,37 @@ namespace {
 // part of it has to start at zero: every call writes the m * k entries of both planes it then reads.
 constexpr size_t kStaticMaxActivations = size_t(1) << 20;
 static __device__ __align__(256) uint16_t g_static_scratch[2 * kStaticMaxActivations];
+// Status word of these calls on this GPU, laid out as a context's ([0] code, [1] site, [2] detail,
+// [3] wait limit, 0 = the default): a bounded wait of the GEMM that gives up records itself here.
+static __device__ __align__(16) unsigned int g_static_status[4];
 
-constexpr int kMaxDevices = 64;
-std::atomic<uint16_t*> g_scratch[kMaxDevices];
-std::atomic<int> g_sm_count[kMaxDevices];
+std::atomic<uint16_t*> g_scratch[mt::kMaxDevices];
+std::atomic<unsigned int*> g_status[mt::kMaxDevices];
+std::atomic<int> g_sm_count[mt::kMaxDevices];
 std::mutex g_setup;
 
-// The array's name is only a host-side stand-in in host code; the device address comes from
+// The arrays' names are only host-side stand-ins in host code; their device addresses come from
 // cudaGetSymbolAddress, resolved once per device with that device current.
-mt_status device_scratch(int dev, uint16_t** out, int* sms) {
+mt_status device_scratch(int dev, uint16_t** out, unsigned int** status, int* sms) {
     uint16_t* p = g_scratch[dev].load(std::memory_order_acquire);
     if (!p) {
         std::lock_guard<std::mutex> lock(g_setup);
         p = g_scratch[dev].load(std::memory_order_relaxed);
         if (!p) {
             void* addr = nullptr;
+            void* st = nullptr;
             if (cudaGetSymbolAddress(&addr, g_static_scratch) != cudaSuccess || !addr) return MT_ERR_CUDA;
+            if (cudaGetSymbolAddress(&st, g_static_status) != cudaSuccess || !st) return MT_ERR_CUDA;
             int count = 0;
             if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return MT_ERR_CUDA;
             g_sm_count[dev].store(count, std::memory_order_relaxed);
+            g_status[dev].store(static_cast<unsigned int*>(st), std::memory_order_relaxed);
             p = static_cast<uint16_t*>(addr);
             g_scratch[dev].store(p, std::memory_order_release);
         }
     }
     *out = p;
+    *status = g_status[dev].load(std::memory_order_relaxed);
     *sms = g_sm_count[dev].load(std::memory_order_relaxed);
     return MT_OK;
 }
@@ -68,8 +75,9 @@ extern "C" mt_status mt_linear_static(void* stream, const float* x, int ldx, int
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MT_ERR_CUDA;
     uint16_t* scratch = nullptr;
+    unsigned int* status = nullptr;
     int sms = 0;
-    mt_status st = device_scratch(dev, &scratch, &sms);
+    mt_status st = device_scratch(dev, &scratch, &status, &sms);
     if (st != MT_OK) return st;
     cudaStream_t s = as_stream(stream);
     // The planes are rewritten in full for the m x k activations of this call before the GEMM
@@ -83,6 +91,22 @@ extern "C" mt_status mt_linear_static(void* stream, const float* x, int ldx, int
     GemmPlan plan;
     st = make_gemm_plan_bare(sms, a, &plan);
     if (st != MT_OK) return st;
+    plan.e.status = status;
     run_gemm_plan(plan, s);
-    return cudaGetLastError() == cudaSuccess ? MT_OK : MT_ERR_CUDA;
+    // Peek, not get: the launches are checked without clearing an error that belongs to the caller.
+    return cudaPeekAtLastError() == cudaSuccess ? MT_OK : MT_ERR_CUDA;
+}
+
+extern "C" mt_status mt_linear_static_status(void* stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MT_ERR_CUDA;
+    if (cudaStreamSynchronize(as_stream(stream)) != cudaSuccess) return MT_ERR_CUDA;
+    // Before the first mt_linear_static on this device nothing can have been recorded.
+    if (!g_scratch[dev].load(std::memory_order_acquire)) return MT_OK;
+    unsigned int word[3] = {0, 0, 0};
+    if (cudaMemcpyFromSymbol(word, g_static_status, sizeof(word)) != cudaSuccess) return MT_ERR_CUDA;
+    if (word[0] == DEV_OK) return MT_OK;
+    const unsigned int zero[3] = {0, 0, 0};
+    if (cudaMemcpyToSymbol(g_static_status, zero, sizeof(zero)) != cudaSuccess) return MT_ERR_CUDA;
+    return word[0] == DEV_TIMEOUT ? MT_ERR_TIMEOUT : MT_ERR_ARG;
 }

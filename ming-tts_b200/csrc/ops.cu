@@ -263,11 +263,8 @@ size_t attention_smem(int G, int max_keys) {
 void launch_attention(const AttnArgs& a, cudaStream_t s) {
     const int G = a.hq / a.hkv;
     const size_t smem = attention_smem(G, a.max_keys);
-    static bool configured = false;  // set once, before any graph capture (the first call is eager)
-    if (!configured) {
-        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        configured = true;
-    }
+    static PerDeviceOnce once;  // per device, on the first (eager) call, before any graph capture
+    once([] { cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); });
     launch_k(attention_kernel, dim3(a.rows, a.hkv), ATT_THREADS, smem, s, a);
 }
 
@@ -567,11 +564,8 @@ void launch_attention_decode(const AttnDecodeArgs& a, cudaStream_t s) {
     if (a.chunk_keys > 0 && a.chunk_keys < SC) SC = (a.chunk_keys + 15) & ~15;
     if (SC < 8 * G) SC = 8 * G;  // the final reduction reuses the K/V area: 16 x G x 256 bytes
     while (SC > 16 && ad_dyn_bytes(SC, a.rows_per_req, nrg) > kBudget) SC -= 16;
-    static bool configured = false;  // set once, before any graph capture (the first call is eager)
-    if (!configured) {
-        cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBudget);
-        configured = true;
-    }
+    static PerDeviceOnce once;  // per device, on the first (eager) call, before any graph capture
+    once([] { cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBudget); });
     launch_k(attention_decode_kernel, dim3(a.requests, a.hkv), AD_THREADS, ad_dyn_bytes(SC, a.rows_per_req, nrg), s, a, SC);
 }
 

@@ -49,6 +49,8 @@ PROTOTYPES = {
     "or_sinusoid": (None, [c_float, _P]),
     "or_generate": (c_int, [_P, _P, POINTER(GenerateIO)]),
     "or_llm_decode": (c_int, [_P, _P, c_int, c_int, _P, c_int, _P]),
+    "or_flow_patch": (c_int, [_P, _P, _P, _P, _P, c_float, _P]),
+    "or_vae_decode_clip": (ctypes.c_long, [_P, _P, _P, c_int, _P, ctypes.c_long]),
     "or_vae_encode": (c_int, [_P, _P, _P, ctypes.c_long, _P, _P]),
     "or_aggregate_latents": (c_int, [_P, _P, _P, c_int, _P]),
 }

@@ -311,6 +311,72 @@ int or_llm_decode(const mt_qwen_weights* w, float* cache, int cap, int length, c
     return 0;
 }
 
+/* One flow-matching patch (the "flow" stage of MingEngine.encodeStep, Engine.swift:387-403): c_emb of
+ * the LLM output z, then flow_steps Euler steps of the CFG DiT from noise with the given history;
+ * the latent goes to y_out [latent]. */
+int or_flow_patch(const mt_model_config* cfg, const mt_model_weights* w, const float* z, const float* history,
+                  const float* noise, float cfg_scale, float* y_out) {
+    const int L = cfg->latent_dim, Df = cfg->flow.hidden, FS = cfg->flow_steps;
+    float* ts = ALLOC(FS + 1);
+    or_flow_timesteps(FS, ts);
+    float* sinus = ALLOC((size_t)FS * cfg->time_dim);
+    for (int k = 0; k < FS; k++) or_sinusoid(ts[k], sinus + (size_t)k * cfg->time_dim);
+    float* tmid = ALLOC((size_t)FS * Df);
+    float* temb = ALLOC((size_t)FS * Df);
+    or_linear(sinus, cfg->time_dim, FS, w->flow_t1_w, NULL, w->flow_t1_b, Df, cfg->time_dim, tmid, Df,
+              MT_LINEAR_BIAS | MT_LINEAR_SILU);
+    or_linear(tmid, Df, FS, w->flow_t2_w, NULL, w->flow_t2_b, Df, Df, temb, Df, MT_LINEAR_BIAS);
+    float* cemb = ALLOC(Df);
+    float* ditX = ALLOC(6 * Df);
+    float* ditOut = ALLOC(6 * L);
+    float* vel = ALLOC(2 * L);
+    dit_state flow;
+    dit_init(&flow, &w->flow, 6);
+    or_linear(z, cfg->llm.hidden, 1, w->flow_c_w, NULL, w->flow_c_b, Df, cfg->llm.hidden, cemb, Df, MT_LINEAR_BIAS);
+    memcpy(y_out, noise, sizeof(float) * L);
+    for (int k = 0; k < FS; k++) {
+        or_flow_assemble(y_out, history, cemb, w->flow_c_b, temb + (size_t)k * Df, w->flow_x_w, w->flow_x_b, Df, L, ditX);
+        dit_forward(&flow, ditX, 2, 3, 6, ditOut);
+        or_flow_euler(y_out, ditOut, L, 2, 5, L, cfg_scale, ts[k + 1] - ts[k], vel);
+    }
+    dit_free(&flow);
+    free(ts); free(sinus); free(tmid); free(temb); free(cemb); free(ditX); free(ditOut); free(vel);
+    return 0;
+}
+
+/* The streaming VAE decoder over `count` latents [count, latent] (VAEDecoder.swift:64-107): fc1 of
+ * every latent, then each latent's frames decoded and emitted as the generation loop and its flush
+ * do (latent d once latent d + 1 exists, the last one without a look-ahead). pcm receives up to
+ * pcm_cap samples; returns the sample count. */
+long or_vae_decode_clip(const mt_model_config* cfg, const mt_model_weights* w, const float* latents, int count,
+                        float* pcm, long pcm_cap) {
+    const int Hv = cfg->vae.hidden;
+    vae_state vae;
+    memset(&vae, 0, sizeof(vae));
+    vae.cfg = cfg;
+    vae.w = w;
+    qwen_init(&vae.stack, &w->vae, 4 * (count + 1) + 8, 4);
+    vae.h = ALLOC(3 * Hv);
+    vae.frames = ALLOC(4 * Hv);
+    vae.hidden = ALLOC(4 * Hv);
+    vae.spec = ALLOC(4 * (cfg->nfft + 2));
+    vae.ring = ALLOC(8 * cfg->nfft);
+    vae.pcm = ALLOC(4 * cfg->hop + (cfg->nfft - cfg->hop) / 2);
+    long total = 0;
+    for (int n = 0; n <= count; n++) {
+        if (n < count) vae_fc1(&vae, latents + (size_t)n * cfg->latent_dim);
+        while (vae.decoded + 1 < vae.latents || (n == count && vae.decoded < vae.latents)) {
+            const int d = vae.decoded;
+            const int c = vae_decode(&vae, d, d + 1 < vae.latents, NULL);
+            if (pcm && total + c <= pcm_cap) memcpy(pcm + total, vae.pcm, sizeof(float) * c);
+            total += c;
+        }
+    }
+    qwen_free(&vae.stack);
+    free(vae.h); free(vae.frames); free(vae.hidden); free(vae.spec); free(vae.ring); free(vae.pcm);
+    return total;
+}
+
 /* bf16Rounded (VAEEncoder.swift:110-114). */
 static float bf16_rounded(float x) {
     uint32_t u;

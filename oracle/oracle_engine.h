@@ -42,6 +42,12 @@ typedef struct {
 int or_generate(const mt_model_config* cfg, const mt_model_weights* w, or_generate_io* io);
 int or_llm_decode(const mt_qwen_weights* w, float* cache, int cap, int length, const float* x_in, int rows,
                   float* z_out);
+/* The flow stage of one step (Engine.swift:387-403): 10 CFG Euler steps from noise -> y_out [latent]. */
+int or_flow_patch(const mt_model_config* cfg, const mt_model_weights* w, const float* z, const float* history,
+                  const float* noise, float cfg_scale, float* y_out);
+/* VAEDecoder.swift:64-107 over count latents, flush included; returns the samples emitted. */
+long or_vae_decode_clip(const mt_model_config* cfg, const mt_model_weights* w, const float* latents, int count,
+                        float* pcm, long pcm_cap);
 /* VAEEncoder.encode (VAEEncoder.swift:56-107): count samples (a multiple of frame * patch) ->
  * mean/std [count / (frame * patch), latent]. Returns 0, or -1 on a bad count. */
 int or_vae_encode(const mt_model_config* cfg, const mt_encoder_weights* w, const float* samples, long count,

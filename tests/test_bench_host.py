@@ -28,7 +28,7 @@ def _run_bench(args, env_extra=None, timeout=600):
 def test_reference_arm_line():
     """`--impl reference` times the CPU oracle of the full model and prints one JSON line with the
     arm's keys; its value, cpu_baseline and e2e agree, with no host-device bytes."""
-    r = _run_bench(["--impl", "reference", "--steps", "1", "--warmup", "3"])
+    r = _run_bench(["--impl", "reference", "--steps", "1", "--warmup", "3", "--prompt", "8"])
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1
@@ -40,6 +40,20 @@ def test_reference_arm_line():
     assert cb["value"] == e2e["value"] == d["value"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     assert d["config"]["workload"]
+
+
+def test_reference_arm_loads_only_the_oracle():
+    """The reference arm times the oracle without the product library: after a run, the process has
+    mapped liboracle.so and not libmingcuda.so, and has not imported the product package."""
+    code = ("import sys, json; sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '3', "
+            "'--prompt', '4']; sys.path.insert(0, '.'); import bench; bench.main(); "
+            "maps = open('/proc/self/maps').read(); "
+            "print(json.dumps({'oracle': 'liboracle.so' in maps, 'product': 'libmingcuda' in maps, "
+            "'package': 'mingtts_b200' in sys.modules}))")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    assert d == {"oracle": True, "product": False, "package": False}
 
 
 def test_reference_arm_other_ranks_exit_quietly():

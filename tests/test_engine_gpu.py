@@ -87,7 +87,9 @@ def engine_generate(mt, eng, cfg, embeds=None, ids=None, noise=None, steps=1, cf
 
 
 def compare(mt, oracle, ctx, cfg, R, T, steps, seed, use_graphs=True, use_ids=False, lat_rel=1e-3, groups=0,
-            with_history=False):
+            with_history=False, check=None):
+    """Runs R requests through the engine and checks requests `check` (default: all) against the
+    oracle's one-request loop."""
     model = mt.Model(ctx, cfg, seed=seed)
     host = model.arena_to_host()
     tensors = model.tensors()
@@ -108,7 +110,7 @@ def compare(mt, oracle, ctx, cfg, R, T, steps, seed, use_graphs=True, use_ids=Fa
     eng = mt.Engine(ctx, model, R, T, steps, use_graphs=use_graphs, groups=groups)
     got = engine_generate(mt, eng, cfg, embeds=None if use_ids else embeds, ids=ids, noise=noise, steps=steps,
                           initial_history=hist)
-    for r in range(R):
+    for r in (range(R) if check is None else check):
         want = oracle_generate(oracle, cfg, w_host, np.ascontiguousarray(embeds[r]), np.ascontiguousarray(noise[r]), steps,
                                initial_history=None if hist is None else np.ascontiguousarray(hist[r]))
         tag = f"R{R} request {r}"
@@ -290,3 +292,28 @@ def test_full_model_batched_parity(ctx, mt, oracle):
 def test_full_model_two_groups_parity(ctx, mt, oracle):
     # Two request groups of 10 (LLM 10 rows, flow 60, aggregator 20 each) on concurrent streams.
     compare(mt, oracle, ctx, mt.default_config(), R=20, T=4, steps=3, seed=8, use_ids=True, groups=2)
+
+
+def test_serving_config_parity(ctx, mt, oracle):
+    """The benchmarked configuration (64 requests, 128-token prompts) for 40 steps: LLM 64-row tiles,
+    flow 384-row plans with split-K, aggregator 128 rows, VAE 256-row plans, an 8192-row prefill,
+    and the VAE ring of 128 positions wrapping after latent 32. Three requests spread over the
+    tiles are checked against the oracle."""
+    compare(mt, oracle, ctx, mt.default_config(), R=64, T=128, steps=40, seed=11, use_ids=True, check=[0, 33, 63])
+
+
+@pytest.mark.parametrize("R", [2, 9])
+def test_long_cache_parity(ctx, mt, oracle, R):
+    """Positions 424..447 of the 512-entry cache: the decode attention stages more keys than its
+    shared memory holds (chunks of 416 keys) and merges them with the online softmax, inside the
+    engine; R = 2 runs the LLM rows on the CUDA-core GEMV, R = 9 on the tensor cores."""
+    compare(mt, oracle, ctx, mt.default_config(), R=R, T=424, steps=24, seed=12, use_ids=True, check=[0, R - 1])
+
+
+def test_alternate_dit_dims_parity(ctx, mt, oracle):
+    """BASELINE config 3's DiT dimensions (hidden 512, 8 heads, 6 blocks, MLP 2048) in the reference's
+    block structure (DiT.swift:35-52) for the flow head; the kernels are shape-generic."""
+    cfg = mt.default_config()
+    cfg.flow.hidden, cfg.flow.heads, cfg.flow.depth, cfg.flow.ff = 512, 8, 6, 2048
+    compare(mt, oracle, ctx, cfg, R=12, T=4, steps=3, seed=14, use_ids=True, check=[0, 5, 11])
+    compare(mt, oracle, ctx, cfg, R=1, T=4, steps=3, seed=15, use_ids=True)

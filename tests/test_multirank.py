@@ -32,8 +32,10 @@ def _worker(rank, world, port, out):
         t = bench.dist_max(float(rank + 1) * 0.5, world, device="cpu")
         bench.barrier(world, device="cpu")
         first, count = bench.rank_requests(rank, 3)
-        ids, noise = bench.request_inputs(mt, cfg, count, 4, 2, first)
-        out[rank] = (t, first, ids, noise)
+        ids, noise = bench.request_inputs(bench.product_noise(mt), cfg.vocab, cfg.latent_dim, count, 4, 2, first)
+        # config 5's strong-scaling partition: 64 requests in all, 32 per rank
+        strong_first, strong_count = bench.rank_requests(rank, 64 // world)
+        out[rank] = (t, first, ids, noise, strong_first, strong_count)
     finally:
         dist.destroy_process_group()
 
@@ -54,11 +56,13 @@ def test_two_gloo_ranks():
     for r in range(world):
         assert out[r][0] == pytest.approx(1.0)  # max over ranks of 0.5 and 1.0
     assert out[0][1] == 0 and out[1][1] == 3
+    assert [(out[r][4], out[r][5]) for r in range(world)] == [(0, 32), (32, 32)]
     assert not np.array_equal(out[0][2], out[1][2])
     assert not np.array_equal(out[0][3], out[1][3])
     # Reproducible: rank 1's inputs are the global requests 3..5 drawn in one process.
     bench = _load_bench()
     mt = bench.load_package()
-    ids, noise = bench.request_inputs(mt, mt.small_config(), 6, 4, 2, 0)
+    cfg = mt.small_config()
+    ids, noise = bench.request_inputs(bench.product_noise(mt), cfg.vocab, cfg.latent_dim, 6, 4, 2, 0)
     np.testing.assert_array_equal(out[1][2], ids[3:])
     np.testing.assert_array_equal(out[1][3], noise[3:])

@@ -111,3 +111,30 @@ def test_oracle_initial_history(mt, oracle):
     np.testing.assert_array_equal(zeros["latents"], plain["latents"])
     np.testing.assert_array_equal(zeros["pcm"], plain["pcm"])
     assert np.abs(voice["latents"][0] - plain["latents"][0]).max() > 1e-3
+
+
+def test_oracle_stage_helpers_match_generation(mt, oracle):
+    """or_flow_patch and or_vae_decode_clip (the CPU legs of BASELINE configs 3 and 4) reproduce the
+    generation loop's own stages: step 0's latent from z with a zero history, and the whole waveform
+    from the loop's latents."""
+    cfg = mt.small_config()
+    arena, tensors = host_arena(mt, oracle, cfg, seed=5)
+    w, keep = mt.weights_struct(cfg, arena.ctypes.data, tensors)
+    steps, T, L = 5, 4, cfg.latent_dim
+    rs = np.random.default_rng(1)
+    embeds = (0.5 * rs.standard_normal((T, cfg.llm.hidden))).astype(np.float32)
+    noise = oracle.gaussian_noise(steps * L, 8).reshape(steps, L)
+    g = oracle_generate(oracle, cfg, w, embeds, noise, steps)
+    y = np.zeros(L, np.float32)
+    z0 = np.ascontiguousarray(g["z"][0])
+    hist = np.zeros(L, np.float32)
+    n0 = np.ascontiguousarray(noise[0])
+    assert oracle.lib().or_flow_patch(ctypes.addressof(cfg), ctypes.addressof(w), z0.ctypes.data, hist.ctypes.data,
+                                      n0.ctypes.data, 2.0, y.ctypes.data) == 0
+    np.testing.assert_array_equal(y, g["latents"][0])
+    lat = np.ascontiguousarray(g["latents"])
+    pcm = np.zeros(4 * cfg.hop * (steps + 1), np.float32)
+    n = oracle.lib().or_vae_decode_clip(ctypes.addressof(cfg), ctypes.addressof(w), lat.ctypes.data, steps,
+                                        pcm.ctypes.data, pcm.size)
+    assert n == g["pcm"].size
+    np.testing.assert_array_equal(pcm[:n], g["pcm"])
