@@ -174,6 +174,13 @@ mt_status mt_ctx_set_wait_limit(mt_ctx* ctx, unsigned int microseconds);
  * and records a timeout, so the next mt_ctx_check returns MT_ERR_TIMEOUT and clears it; the context
  * then works as before. No counterpart in the reference. */
 mt_status mt_ctx_wait_probe(mt_ctx* ctx, void* stream);
+/* Small-batch stacks (at most 8 activation rows: mt_qwen_decode, and the engine's decode passes
+ * at few requests made on ctx from now on): 1 runs every layer of a pass in one launch of
+ * the persistent stack kernel where the shapes fit it, 0 (default) launches one kernel per operation
+ * as the reference dispatches them, 2 requires the persistent kernel (mt_qwen_decode then returns
+ * MT_ERR_SHAPE for a pass it cannot take). Results agree to rounding; the choice only changes
+ * speed. No counterpart in the reference. */
+mt_status mt_ctx_set_persistent(mt_ctx* ctx, int mode);
 /* Tensor-core GEMM tiling for plans made on ctx from now on: -1 automatic (default), 0 single-CTA
  * tiles of 128 weight rows, 1 CTA pairs (clusters of two SMs sharing 256-weight-row tiles through
  * tcgen05 cta_group::2). Results agree to rounding; the choice only changes speed. No counterpart

@@ -117,6 +117,7 @@ PROTOTYPES = {
     "mt_linear_route": (c_int, [c_int, c_int, c_int]),
     "mt_ctx_set_gemm_pairs": (c_int, [_P, c_int]),
     "mt_ctx_set_wait_limit": (c_int, [_P, c_uint32]),
+    "mt_ctx_set_persistent": (c_int, [_P, c_int]),
     "mt_ctx_wait_probe": (c_int, [_P, _P]),
     "mt_linear": (c_int, [_P, _P, _P, c_int, c_int, _P, _P, _P, c_int, c_int, _P, c_int, c_uint32]),
     "mt_linear_split": (c_int, [_P, _P, _P, _P, c_int, c_int, _P, _P, _P, c_int, c_int, _P, c_int, _P, _P, c_int,
@@ -256,6 +257,11 @@ class Context:
         conv = [ptr(a) if (hasattr(a, "data_ptr") or hasattr(a, "ctypes")) else a for a in args]
         st = fn(self._ctx, stream if stream is not None else current_stream(), *conv)
         self._check(st, "mt_" + name)
+
+    def set_persistent(self, mode: int):
+        """Small-batch stacks: 1 the persistent stack kernel where it fits, 0 one launch per op (default),
+        2 the persistent kernel required."""
+        self._check(lib().mt_ctx_set_persistent(self._ctx, mode), "mt_ctx_set_persistent")
 
     def set_wait_limit(self, microseconds: int):
         """Wall-time limit of the kernels' bounded waits (0 = the default 2 s)."""

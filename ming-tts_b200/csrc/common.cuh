@@ -21,6 +21,7 @@ struct mt_ctx {
     void* scratch = nullptr;           // grows on demand, see mt_scratch()
     size_t scratch_bytes = 0;
     int gemm_pairs = -1;               // tensor-core GEMM CTA pairs: -1 automatic, 0 never, 1 where valid
+    int persistent = 0;                // small-batch stacks: 1 the persistent stack kernel where it fits, 0 never
     float* rope = nullptr;             // [32] NeoX rotation frequencies for rope_theta (mt_qwen_decode)
     float rope_theta = 0.f;
     std::string err;

@@ -142,6 +142,12 @@ mt_status mt_ctx_set_wait_limit(mt_ctx* ctx, unsigned int microseconds) {
     return MT_OK;
 }
 
+mt_status mt_ctx_set_persistent(mt_ctx* ctx, int mode) {
+    if (!ctx || mode < 0 || mode > 2) return MT_ERR_ARG;
+    ctx->persistent = mode;
+    return MT_OK;
+}
+
 mt_status mt_ctx_wait_probe(mt_ctx* ctx, void* stream) {
     if (!ctx) return MT_ERR_ARG;
     launch_k(mt::wait_probe_kernel, 1, 32, 0, mt::as_stream(stream), ctx->d_status);

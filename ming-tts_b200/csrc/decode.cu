@@ -5,7 +5,8 @@
 // (VAEDecoder.swift:86-107), over caller-owned fp32 KV caches in the reference's layout
 // (Qwen.swift:7-26). Per layer: RMSNorm -> q/k/v GEMV (+bias) -> RoPE + KV append + attention ->
 // o GEMV (+=) -> RMSNorm -> gate/up GEMV (SiLU gate) -> down GEMV (+=); then the final norm of every
-// row.
+// row. Passes that fit run as one launch of the persistent stack kernel (stack.cu); the others as
+// one launch per kernel above.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -18,13 +19,45 @@ constexpr int kDecodeMaxRows = 8;  // rows of all requests together: the CUDA-co
 // Scratch of one call, carved from the context's scratch area (fp32): normed rows, q/k/v rows,
 // attention rows and the gated MLP rows.
 struct DecodeScratch {
-    float *normed, *qkv, *attn, *mlp;
+    float *normed, *qkv, *attn, *mlp, *sync, *part;
 };
 
-size_t decode_scratch_floats(const mt_qwen_config& c, int M) {
+// Sync words and attention partials of the persistent stack kernel (at most 32 layers).
+constexpr size_t kSyncWords = STACK_MAX_LAYERS * 5 + 2 + (size_t)STACK_MAX_LAYERS * STACK_MAX_UNITS;
+
+size_t decode_scratch_floats(const mt_qwen_config& c, int M, int ctas) {
     const size_t qkvw = (size_t)(c.heads + 2 * c.kv_heads) * 64;
     auto up = [](size_t n) { return (n + 63) & ~size_t(63); };  // 256-byte aligned pieces
-    return up((size_t)M * c.hidden) + up((size_t)M * qkvw) + up((size_t)M * c.heads * 64) + up((size_t)M * c.intermediate);
+    return up((size_t)M * c.hidden) + up((size_t)M * qkvw) + up((size_t)M * c.heads * 64) + up((size_t)M * c.intermediate) +
+           up(kSyncWords) + up(stack_part_floats(ctas));
+}
+
+bool aligned(const void* p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0; }
+
+// The persistent stack kernel's view of the call, or false when it does not apply (shape limits,
+// unaligned weights, or the context's choice).
+bool stack_params(mt_ctx* ctx, const mt_qwen_weights* w, int requests, int rows, float* x, float* kv, long long kv_stride,
+                  int capacity, const int32_t* positions, float* z, const float* inv_freq, const DecodeScratch& sc,
+                  StackParams* out) {
+    const mt_qwen_config& c = w->cfg;
+    if (ctx->persistent == 0 || c.layers > STACK_MAX_LAYERS) return false;
+    StackParams& p = *out;
+    p = StackParams{};
+    p.kind = STACK_QWEN; p.layers = c.layers; p.M = requests * rows; p.seq_rows = rows; p.seqs = requests;
+    p.hidden = c.hidden; p.heads = c.heads; p.kv_heads = c.kv_heads; p.inter = c.intermediate; p.eps = c.eps;
+    p.window = c.window; p.cap = capacity; p.kv_stride = kv_stride; p.pos = positions; p.kv = kv; p.inv_freq = inv_freq;
+    p.x = x; p.qkv = sc.qkv; p.attn = sc.attn; p.mlp = sc.mlp; p.z = z; p.final_norm = w->final_norm;
+    p.sync = reinterpret_cast<unsigned int*>(sc.sync); p.attn_part = sc.part; p.status = ctx->d_status;
+    if (!aligned(w->final_norm, 8)) return false;
+    for (int l = 0; l < c.layers; l++) {
+        const mt_qwen_layer& L = w->layers[l];
+        const uint16_t* ptrs[8] = {L.norm1, L.qkv_w, L.qkv_b, L.o_w, L.norm2, L.gate_w, L.up_w, L.down_w};
+        for (int i = 0; i < 8; i++) p.L[l].p[i] = ptrs[i];
+        if (!aligned(L.norm1, 8) || !aligned(L.norm2, 8) || !aligned(L.qkv_w, 16) || !aligned(L.o_w, 16) ||
+            !aligned(L.gate_w, 16) || !aligned(L.up_w, 16) || !aligned(L.down_w, 16))
+            return false;
+    }
+    return stack_supported(p, ctx->sm_count);
 }
 
 DecodeScratch carve(float* base, const mt_qwen_config& c, int M) {
@@ -35,6 +68,8 @@ DecodeScratch carve(float* base, const mt_qwen_config& c, int M) {
     s.qkv = s.normed + up((size_t)M * c.hidden);
     s.attn = s.qkv + up((size_t)M * qkvw);
     s.mlp = s.attn + up((size_t)M * c.heads * 64);
+    s.sync = s.mlp + up((size_t)M * c.intermediate);
+    s.part = s.sync + up(kSyncWords);
     return s;
 }
 
@@ -82,9 +117,18 @@ extern "C" mt_status mt_qwen_decode(mt_ctx* ctx, void* stream, const mt_qwen_wei
     mt_status st = rope_table(ctx, c.rope_theta, &inv_freq);
     if (st != MT_OK) return st;
     void* buf = nullptr;
-    st = mt::scratch(ctx, s, decode_scratch_floats(c, M) * sizeof(float), &buf);
+    st = mt::scratch(ctx, s, decode_scratch_floats(c, M, ctx->sm_count) * sizeof(float), &buf);
     if (st != MT_OK) return st;
     DecodeScratch sc = carve(static_cast<float*>(buf), c, M);
+    StackParams sp;
+    if (stack_params(ctx, w, requests, rows, x, kv, kv_stride, capacity, positions, z, inv_freq, sc, &sp)) {
+        launch_stack(sp, ctx->sm_count, s);
+        return check_launch(ctx, "mt_qwen_decode (persistent)");
+    }
+    MT_REQUIRE(ctx, ctx->persistent != 2, MT_ERR_SHAPE,
+               "mt_qwen_decode: the persistent stack kernel cannot run this pass (%d requests x %d rows, window %d, "
+               "capacity %d; %s %s)", requests, rows, c.window, capacity,
+               stack_resident_blocks() < 1 ? "it does not fit one block per SM:" : "shapes", stack_resident_why());
 
     const int H = c.hidden, qkvw = (c.heads + 2 * c.kv_heads) * 64, A = c.heads * 64;
     const size_t tensor = (size_t)c.kv_heads * capacity * 64;

@@ -78,6 +78,11 @@ struct Group {
     std::vector<QwenLayerPlans> llm_dec;
     std::vector<DitBlockPlans> flow_blocks, agg_blocks;
     Lin cond, agg_final, stop_lin;
+    // Few rows: the LLM token, flow DiT pass and aggregator as persistent stack launches.
+    bool llm_ps = false, flow_ps = false, agg_ps = false;
+    StackParams llm_sp{}, flow_sp{}, agg_sp{};
+    unsigned int* sync = nullptr;  // sync words of this group's stack launches (its stream runs them in turn)
+    float* part = nullptr;         // their attention partials
 };
 
 }  // namespace mt
@@ -125,9 +130,13 @@ struct mt_engine {
     bool begun = false, prefilled = false;
 
     // Plans for the current (R, T).
-    int plan_R = -1, plan_T = -1;
+    int plan_R = -1, plan_T = -1, plan_persistent = -1;
     std::vector<QwenLayerPlans> llm_pre, vae_layers;
     Lin vae_head;
+    bool vae_ps = false;        // VAE decode stack as one persistent launch (4R <= 8 rows)
+    StackParams vae_sp{};
+    unsigned int* vae_sync = nullptr;
+    float* vae_part = nullptr;
     Group groups[kMaxGroups];
     int G = 1;  // groups of the current generation
 
@@ -288,6 +297,51 @@ mt_status plan_dit(mt_engine* e, std::vector<DitBlockPlans>& plans, const mt_dit
     return MT_OK;
 }
 
+// >= stack_sync_words of any pass: phase counters, abort flag and per-unit attention counters
+constexpr int kStackSyncWords = STACK_MAX_LAYERS * 5 + 2 + STACK_MAX_LAYERS * STACK_MAX_UNITS;
+
+// A Qwen pass over `rows` rows (rows_per_req per request, positions pos_dev) as one persistent stack
+// launch; false where the context disables it or the shapes do not fit (then one launch per op).
+bool qwen_stack(mt_engine* e, const mt_qwen_weights& W, const QwenBufs& b, int rows, int rows_per_req,
+                const int* pos_dev, float* z, unsigned int* sync, float* part, StackParams* out) {
+    const mt_qwen_config& c = W.cfg;
+    if (e->ctx->persistent == 0 || rows > kGemvMax || c.layers > STACK_MAX_LAYERS) return false;
+    StackParams& p = *out;
+    p = StackParams{};
+    p.kind = STACK_QWEN; p.layers = c.layers; p.M = rows; p.seq_rows = rows_per_req; p.seqs = rows / rows_per_req;
+    p.hidden = c.hidden; p.heads = c.heads; p.kv_heads = c.kv_heads; p.inter = c.intermediate; p.eps = c.eps;
+    p.window = c.window; p.cap = b.cap; p.kv_stride = (long long)c.layers * 2 * c.kv_heads * b.cap * 64;
+    p.pos = pos_dev; p.kv = b.kv; p.inv_freq = b.inv_freq;
+    p.x = b.x; p.qkv = b.qkv; p.attn = b.attn.f; p.mlp = b.mlp.f; p.z = z; p.final_norm = W.final_norm;
+    p.sync = sync; p.attn_part = part; p.status = e->ctx->d_status;
+    for (int l = 0; l < c.layers; l++) {
+        const mt_qwen_layer& L = W.layers[l];
+        const mt_bf16* ptrs[8] = {L.norm1, L.qkv_w, L.qkv_b, L.o_w, L.norm2, L.gate_w, L.up_w, L.down_w};
+        for (int i = 0; i < 8; i++) p.L[l].p[i] = ptrs[i];
+    }
+    return stack_supported(p, e->ctx->sm_count);
+}
+
+// The blocks of a DiT pass over `batch` sequences of `seq` rows as one persistent stack launch.
+bool dit_stack(mt_engine* e, const mt_dit_weights& W, const DitBufs& b, int batch, int seq, unsigned int* sync,
+               StackParams* out) {
+    const mt_dit_config& c = W.cfg;
+    if (e->ctx->persistent == 0 || batch * seq > kGemvMax || c.depth > STACK_MAX_LAYERS) return false;
+    StackParams& p = *out;
+    p = StackParams{};
+    p.kind = STACK_DIT; p.layers = c.depth; p.M = batch * seq; p.seq_rows = seq; p.seqs = batch;
+    p.hidden = c.hidden; p.heads = c.heads; p.kv_heads = c.heads; p.inter = c.ff; p.eps = c.eps;
+    p.inv_freq = W.inv_freq;
+    p.x = b.x; p.qkv = b.qkv; p.attn = b.attn.f; p.mlp = b.ff.f;
+    p.sync = sync; p.status = e->ctx->d_status;
+    for (int i = 0; i < c.depth; i++) {
+        const mt_dit_block& B = W.blocks[i];
+        const mt_bf16* ptrs[10] = {B.norm1, B.qkv_w, B.qkv_b, B.out_w, B.out_b, B.norm2, B.ff1_w, B.ff1_b, B.ff2_w, B.ff2_b};
+        for (int k = 0; k < 10; k++) p.L[i].p[k] = ptrs[k];
+    }
+    return stack_supported(p, e->ctx->sm_count);
+}
+
 Act act_rows(const Act& a, size_t row) {
     Act v = a;
     const size_t off = row * (size_t)a.ld;
@@ -361,11 +415,17 @@ mt_status plan_group(mt_engine* e, Group& g, int r0, int Rg) {
     TRY(plan_dit(e, g.agg_blocks, e->w.agg, g.agg, 2 * Rg, nullptr, 0));
     TRY(make_lin(e, &g.agg_final, g.agg_norm, Rg, e->w.agg.final_w, nullptr, e->w.agg.final_b, c.agg.out_dim,
                  c.agg.hidden, g.llm.x, H, nullptr, 0));
+    // Stack launches take every SM: only where one chain runs at a time (a single request group).
+    const bool solo = group_count(e, e->R) == 1;
+    g.llm_ps = solo && qwen_stack(e, e->w.llm, g.llm, Rg, 1, g.llm_pos, g.z.f, g.sync, g.part, &g.llm_sp);
+    g.flow_ps = solo && dit_stack(e, e->w.flow, g.flow, 2 * Rg, 3, g.sync, &g.flow_sp);
+    g.agg_ps = solo && dit_stack(e, e->w.agg, g.agg, Rg, 2, g.sync, &g.agg_sp);
     return MT_OK;
 }
 
 mt_status build_plans(mt_engine* e) {
-    if (e->plan_R == e->R && e->plan_T == e->T) return MT_OK;
+    if (e->plan_R == e->R && e->plan_T == e->T && e->plan_persistent == e->ctx->persistent) return MT_OK;
+    e->plan_persistent = e->ctx->persistent;
     const int R = e->R, T = e->T;
     const mt_model_config& c = e->cfg;
     TRY(plan_qwen(e, e->llm_pre, e->w.llm, e->llm, R * T, e->ws_a, e->ws_a_floats));
@@ -378,6 +438,8 @@ mt_status build_plans(mt_engine* e) {
     TRY(plan_qwen(e, e->vae_layers, e->w.vae, e->vae, 4 * R, e->ws_b, e->ws_b_floats));
     TRY(make_lin(e, &e->vae_head, e->vae_hidden, 4 * R, e->w.vae_head_w, nullptr, e->w.vae_head_b, c.nfft + 2,
                  c.vae.hidden, e->spec, c.nfft + 2, nullptr, 0));
+    e->vae_ps = e->G == 1 && qwen_stack(e, e->w.vae, e->vae, 4 * R, 4, e->state_dev + st_vae_pos(R), e->vae_hidden.f,
+                                        e->vae_sync, e->vae_part, &e->vae_sp);
     e->plan_R = R;
     e->plan_T = T;
     return MT_OK;
@@ -507,6 +569,11 @@ mt_status precompute_temb(mt_engine* e) {
 
 void llm_token(mt_engine* e, Group& g, cudaStream_t s) {
     const mt_qwen_config& c = e->cfg.llm;
+    if (g.llm_ps) {  // every layer and the final norm in one launch
+        launch_stack(g.llm_sp, e->ctx->sm_count, s);
+        g_kernels++;
+        return;
+    }
     qwen_forward(e, e->w.llm, g.llm, g.llm_dec, g.R, 1, 0, g.llm_pos, g.llm.cap, s);
     norm(g.llm.x, c.hidden, g.R, c.hidden, e->w.llm.final_norm, c.eps, g.z, g.R, true, s);
 }
@@ -521,7 +588,12 @@ void flow_stage(mt_engine* e, Group& g, cudaStream_t s) {
         launch_flow_assemble_batched(g.y, g.hist, g.cemb, e->w.flow_c_b, e->temb + (size_t)k * Df, e->w.flow_x_w,
                                      e->w.flow_x_b, Df, L, g.flow.x, R, s);
         g_kernels++;
-        dit_blocks(e, e->w.flow, g.flow, g.flow_blocks, 2 * R, 3, s);
+        if (g.flow_ps) {
+            launch_stack(g.flow_sp, e->ctx->sm_count, s);
+            g_kernels++;
+        } else {
+            dit_blocks(e, e->w.flow, g.flow, g.flow_blocks, 2 * R, 3, s);
+        }
         FlowFinalArgs fa{};
         fa.X = g.flow.x; fa.hidden = Df; fa.norm_w = e->w.flow.final_norm; fa.eps = c.flow.eps;
         fa.final_w = e->w.flow.final_w; fa.final_b = e->w.flow.final_b; fa.latent = L; fa.y = g.y;
@@ -538,7 +610,12 @@ void agg_stage(mt_engine* e, Group& g, cudaStream_t s) {
     const int R = g.R, L = c.latent_dim;
     const int Da = c.agg.hidden;
     launch_agg_assemble(g.y, e->w.agg_cls, e->w.agg_x_w, e->w.agg_x_b, Da, L, g.agg.x, R, s); g_kernels++;
-    dit_blocks(e, e->w.agg, g.agg, g.agg_blocks, R, 2, s);
+    if (g.agg_ps) {
+        launch_stack(g.agg_sp, e->ctx->sm_count, s);
+        g_kernels++;
+    } else {
+        dit_blocks(e, e->w.agg, g.agg, g.agg_blocks, R, 2, s);
+    }
     norm(g.agg.x, 2 * Da, R, Da, e->w.agg.final_norm, c.agg.eps, g.agg_norm, R, false, s);
     run(g.agg_final, s);
 }
@@ -555,8 +632,13 @@ void vae_decode(mt_engine* e, cudaStream_t s) {
     const int R = e->R, Hv = c.vae.hidden;
     launch_vae_upsample(e->vae_h, Hv, e->state_dev, e->vae.x, R, s); g_kernels++;
     const int max_keys = c.vae.window > 0 ? c.vae.window : e->vae.cap;
-    qwen_forward(e, e->w.vae, e->vae, e->vae_layers, 4 * R, 4, 0, e->state_dev + st_vae_pos(R), max_keys, s);
-    norm(e->vae.x, Hv, 4 * R, Hv, e->w.vae.final_norm, c.vae.eps, e->vae_hidden, 4 * R, true, s);
+    if (e->vae_ps) {  // every layer and the final norm in one launch
+        launch_stack(e->vae_sp, e->ctx->sm_count, s);
+        g_kernels++;
+    } else {
+        qwen_forward(e, e->w.vae, e->vae, e->vae_layers, 4 * R, 4, 0, e->state_dev + st_vae_pos(R), max_keys, s);
+        norm(e->vae.x, Hv, 4 * R, Hv, e->w.vae.final_norm, c.vae.eps, e->vae_hidden, 4 * R, true, s);
+    }
     run(e->vae_head, s);
     IstftArgs ia{};
     ia.spec = e->spec; ia.ld_spec = c.nfft + 2; ia.count = 4 * R; ia.nfft = c.nfft; ia.window = e->w.vae_window;
@@ -602,8 +684,19 @@ void upload_state(mt_engine* e, cudaStream_t s) {
 void enqueue_step(mt_engine* e, cudaStream_t s, bool with_llm, bool with_decode, bool timed) {
     cudaEvent_t* ev = e->stage_ev;
     if (timed) cudaEventRecord(ev[0], s);
+    // A VAE decode that runs as a persistent stack launch takes every SM for its duration, as the
+    // LLM token's does: it runs on the step stream before the groups instead of concurrently.
+    const bool serial_decode = with_decode && e->vae_ps;
+    if (serial_decode) {
+        if (timed) cudaEventRecord(ev[4], s);
+        vae_decode(e, s);
+        if (timed) {
+            cudaEventRecord(ev[5], s);
+            cudaEventRecord(ev[0], s);
+        }
+    }
     cudaEventRecord(e->ev_fork, s);
-    if (with_decode) {
+    if (with_decode && !serial_decode) {
         cudaStreamWaitEvent(e->sb, e->ev_fork, 0);
         if (timed) cudaEventRecord(ev[4], e->sb);
         vae_decode(e, e->sb);
@@ -624,7 +717,7 @@ void enqueue_step(mt_engine* e, cudaStream_t s, bool with_llm, bool with_decode,
         if (i > 0) cudaEventRecord(g.done, gs);
     }
     for (int i = 1; i < e->G; i++) cudaStreamWaitEvent(s, e->groups[i].done, 0);
-    if (with_decode) cudaStreamWaitEvent(s, e->ev_join, 0);
+    if (with_decode && !serial_decode) cudaStreamWaitEvent(s, e->ev_join, 0);
 }
 
 }  // namespace
@@ -687,6 +780,12 @@ mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_o
     ETRY(dalloc(e, &e->ws_a, e->ws_a_floats));
     ETRY(dalloc(e, &e->ws_b, e->ws_b_floats));
     ETRY(dalloc(e, &e->ids_stage, (size_t)R * T));
+    ETRY(dalloc(e, &e->vae_sync, kStackSyncWords));
+    ETRY(dalloc(e, &e->vae_part, stack_part_floats(ctx->sm_count)));
+    for (int i = 0; i < kMaxGroups; i++) {
+        ETRY(dalloc(e, &e->groups[i].sync, kStackSyncWords));
+        ETRY(dalloc(e, &e->groups[i].part, stack_part_floats(ctx->sm_count)));
+    }
     if (cudaMallocHost(&e->state_slots[0], st_size(R) * sizeof(int)) != cudaSuccess ||
         cudaMallocHost(&e->state_slots[1], st_size(R) * sizeof(int)) != cudaSuccess ||
         cudaMallocHost(&e->ring_host, (size_t)kPcmRing * R * e->max_chunk * sizeof(float)) != cudaSuccess ||
@@ -771,7 +870,7 @@ mt_status mt_engine_begin(mt_engine* e, void* stream, int requests, int prompt_r
     e->n = 0;
     e->latents_fed = e->decoded = e->emitted = 0;
     e->prefilled = false;
-    if (e->plan_R != requests) {
+    if (e->plan_R != requests || e->plan_persistent != ctx->persistent) {
         for (int i = 0; i < 2; i++) {
             if (e->graph_exec[i]) cudaGraphExecDestroy(e->graph_exec[i]);
             if (e->graph[i]) cudaGraphDestroy(e->graph[i]);

@@ -153,4 +153,38 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan);
 mt_status make_gemm_plan_bare(int sm_count, const LinearArgs& a, GemmPlan* plan);
 void run_gemm_plan(const GemmPlan& p, cudaStream_t s);
 
+// Persistent small-batch stack (stack.cu): every layer of a Qwen decode pass, or every block of a
+// DiT pass, in one cooperative launch over at most 8 activation rows.
+constexpr int STACK_MAX_LAYERS = 32;
+constexpr int STACK_MAX_UNITS = 64;  // attention units (sequence, kv head) of a Qwen pass, at most
+enum : int { STACK_QWEN = 0, STACK_DIT = 1 };
+struct StackLayer { const uint16_t* p[10]; };  // Qwen: norm1 qkv_w qkv_b o_w norm2 gate_w up_w down_w;
+                                                // DiT: norm1 qkv_w qkv_b out_w out_b norm2 ff1_w ff1_b ff2_w ff2_b
+struct StackParams {
+    int kind, layers;
+    int M, seq_rows, seqs;           // M = seqs * seq_rows rows; Qwen: rows per request; DiT: sequence length
+    int hidden, heads, kv_heads, inter;
+    float eps;
+    int window, cap;                 // Qwen KV cache: window (0 = causal), capacity (slot = position % cap)
+    long long kv_stride;             // floats between requests' caches ([layers][K|V][kv][cap][64] each)
+    const int* pos;                  // device [seqs]: cached positions per request (Qwen)
+    float* kv;
+    const float* inv_freq;           // [32]: NeoX frequencies (Qwen) or the DiT's rotary inv_freq
+    float* x;                        // residual rows [M, hidden], updated in place
+    float *qkv, *attn, *mlp;         // scratch rows
+    float* z;                        // Qwen: final norm of every row [M, hidden] (NULL: none)
+    const uint16_t* final_norm;
+    unsigned int* sync;              // stack_sync_words() words, zeroed by launch_stack
+    float* attn_part;                // Qwen: stack_part_floats() floats of attention partials
+    unsigned int* status;            // context status word (bounded waits)
+    StackLayer L[STACK_MAX_LAYERS];
+};
+bool stack_supported(const StackParams& p, int ctas);
+int stack_resident_blocks();  // blocks of the stack kernel one SM of the current device holds (>= 1 to launch)
+const char* stack_resident_why();  // what kept it below one block, when it is
+int stack_phases(const StackParams& p);
+int stack_sync_words(const StackParams& p);  // phase counters, abort flag, per-unit attention counters
+size_t stack_part_floats(int ctas);
+void launch_stack(const StackParams& p, int ctas, cudaStream_t s);
+
 }  // namespace mt

@@ -3,8 +3,9 @@
 Qwen2-0.5B dimensions with random-init weights (seed 1), the KV cache of every layer pre-filled to
 256 (and 500) of 512 positions with bf16-representable N(0,1) values, one new row per sequence:
 M = 1 (the reference's decode, Engine.swift:381-385) and M = 2 (the config's CFG pair as two
-sequences with their own caches). Two steps in a row, so the second attends to the row the first
-appended. The oracle restates QwenForward.dispatches (Qwen.swift:72-97) with fp64 dot products.
+sequences with their own caches), and 8 sequences (the most the small-batch path takes). Two steps
+in a row, so the second attends to the row the first appended. Each case runs on both paths of
+mt_qwen_decode: the persistent stack kernel (one launch per pass) and one launch per operation. The oracle restates QwenForward.dispatches (Qwen.swift:72-97) with fp64 dot products.
 Bar: residual stream and final-norm rows within 1e-3 relative (max |err| / max |ref|), appended
 cache rows within 1e-4.
 """
@@ -39,8 +40,17 @@ def prefilled_cache(oracle, cfg, cap, length, seed):
     return cache
 
 
-@pytest.mark.parametrize("requests,length", [(1, 256), (2, 256), (1, 500), (2, 500)])
-def test_llm_decode_step_matches_oracle(ctx, mt, oracle, llm, requests, length):
+@pytest.fixture(params=[2, 0], ids=["persistent", "per-op"])
+def path(request, ctx):
+    """Both implementations of mt_qwen_decode: the persistent stack kernel (required: an error if it
+    cannot run) and one launch per op."""
+    ctx.set_persistent(request.param)
+    yield request.param
+    ctx.set_persistent(0)
+
+
+@pytest.mark.parametrize("requests,length", [(1, 256), (2, 256), (1, 500), (2, 500), (8, 300)])
+def test_llm_decode_step_matches_oracle(ctx, mt, oracle, llm, path, requests, length):
     import torch
     cfg, model, w_dev, w_host, _ = llm
     c, H, cap = cfg.llm, cfg.llm.hidden, cfg.llm_capacity
@@ -87,3 +97,36 @@ def test_decode_rejects_bad_shapes(ctx, mt, llm):
     with pytest.raises(mt.MingError) as e:  # request stride smaller than one cache
         ctx.call("qwen_decode", ctypes.byref(w_dev.llm), 1, 1, x, kv, 8, 512, pos, x)
     assert e.value.status == mt.MT_ERR_CAPACITY
+
+
+def test_vae_style_decode_matches_oracle(ctx, mt, oracle, path):
+    """Four rows per sequence over a 65-key window in a 128-slot ring (the VAE decoder's shape,
+    VAEDecoder.swift:86-107), reduced dimensions, two sequences, positions past the ring's wrap."""
+    import torch
+    cfg = mt.small_config()
+    model = mt.Model(ctx, cfg, seed=4, with_embeddings=False)
+    host = model.arena_to_host()
+    w_host, keep = mt.weights_struct(cfg, host.ctypes.data, model.tensors())
+    w_dev = ctypes.cast(mt.lib().mt_model_get_weights(model.handle), ctypes.POINTER(mt.ModelWeights)).contents
+    c, H, cap, S, R = cfg.vae, cfg.vae.hidden, 128, 4, 2
+    rs = np.random.default_rng(4)
+    # the oracle keeps every position; the device cache is a ring of `cap` slots
+    full = [np.zeros((c.layers, 2, c.kv_heads, 512, 64), np.float32) for _ in range(R)]
+    ring = torch.zeros(R * c.layers * 2 * c.kv_heads * cap * 64, device="cuda")
+    stride = c.layers * 2 * c.kv_heads * cap * 64
+    pos = torch.zeros(R, dtype=torch.int32, device="cuda")
+    for step in range(40):  # 160 positions: the ring wraps after 128
+        x0 = (0.5 * rs.standard_normal((R * S, H))).astype(np.float32)
+        x = torch.from_numpy(x0.copy()).cuda()
+        z = torch.zeros(R * S, H, device="cuda")
+        ctx.call("qwen_decode", ctypes.byref(w_dev.vae), R, S, x, ring, stride, cap, pos, z)
+        ctx.check()
+        got = z.cpu().numpy()
+        for r in range(R):
+            zr = np.zeros((S, H), np.float32)
+            xr = np.ascontiguousarray(x0[r * S:(r + 1) * S])
+            assert oracle.lib().or_llm_decode(ctypes.addressof(w_host.vae), full[r].ctypes.data, 512, 4 * step,
+                                              xr.ctypes.data, S, zr.ctypes.data) == 0
+            assert rel_err(got[r * S:(r + 1) * S], zr) < 1e-3, f"step {step} sequence {r}"
+        pos += S
+    model.close()

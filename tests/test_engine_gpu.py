@@ -53,9 +53,10 @@ def engine_generate(mt, eng, cfg, embeds=None, ids=None, noise=None, steps=1, cf
               token_ids=dev(ids) if ids is not None else None, noise=dev(noise),
               initial_history=dev(initial_history) if initial_history is not None else None, steps=steps, cfg=cfg_scale)
     eng.prefill()
-    res = dict(stop=[], z=[], agg=[], pcm=[[] for _ in range(R)], chunks=[], vae_hidden=[])
+    res = dict(stop=[], z=[], agg=[], pcm=[[] for _ in range(R)], chunks=[], vae_hidden=[], kernels=0)
     for n in range(steps):
         count = eng.step()
+        res["kernels"] = max(res["kernels"], mt.lib().mt_engine_step_kernels(eng.handle))
         torch.cuda.synchronize()
         res["stop"].append(eng.read(mt.BUF_STOP_LOGITS, R))
         res["z"].append(eng.read(mt.BUF_Z, R))
@@ -317,3 +318,32 @@ def test_alternate_dit_dims_parity(ctx, mt, oracle):
     cfg.flow.hidden, cfg.flow.heads, cfg.flow.depth, cfg.flow.ff = 512, 8, 6, 2048
     compare(mt, oracle, ctx, cfg, R=12, T=4, steps=3, seed=14, use_ids=True, check=[0, 5, 11])
     compare(mt, oracle, ctx, cfg, R=1, T=4, steps=3, seed=15, use_ids=True)
+
+
+@pytest.mark.parametrize("R", [1, 2, 4])
+def test_persistent_stacks_match_per_op(ctx, mt, oracle, R):
+    """With few requests the engine runs the LLM token (R <= 8 rows), the VAE decode (4R <= 8),
+    the flow DiT pass (6R <= 8) and the aggregator (2R <= 8) as persistent stack launches; the
+    per-op path (one launch per kernel) gives the same generation, and both match the oracle."""
+    cfg = mt.small_config()
+    ctx.set_persistent(0)
+    off = compare(mt, oracle, ctx, cfg, R=R, T=5, steps=6, seed=30 + R)
+    try:
+        ctx.set_persistent(1)
+        on = compare(mt, oracle, ctx, cfg, R=R, T=5, steps=6, seed=30 + R)
+    finally:
+        ctx.set_persistent(0)
+    assert on["kernels"] < off["kernels"]  # some stacks ran as single launches
+    assert rel_err(on["latents"], off["latents"]) < 1e-5
+    for a, b in zip(on["pcm"], off["pcm"]):
+        assert cosine(a, b) > 0.999999
+
+
+def test_single_request_full_model_parity(ctx, mt, oracle):
+    """One request at the reference dimensions (the reference's own use): every stack of the step
+    runs as a persistent launch (LLM 1 row, flow 6 rows, aggregator 2 rows, VAE 4 rows)."""
+    try:
+        ctx.set_persistent(1)
+        compare(mt, oracle, ctx, mt.default_config(), R=1, T=12, steps=5, seed=16, use_ids=True)
+    finally:
+        ctx.set_persistent(0)
