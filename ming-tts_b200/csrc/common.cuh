@@ -22,6 +22,8 @@ struct mt_ctx {
     size_t scratch_bytes = 0;
     int gemm_pairs = -1;               // tensor-core GEMM CTA pairs: -1 automatic, 0 never, 1 where valid
     int persistent = 0;                // small-batch stacks: 1 the persistent stack kernel where it fits, 0 never
+    void* stack_area = nullptr;        // mt_qwen_decode's persistent-stack area (zeroed at allocation)
+    size_t stack_area_bytes = 0;
     float* rope = nullptr;             // [32] NeoX rotation frequencies for rope_theta (mt_qwen_decode)
     float rope_theta = 0.f;
     std::string err;

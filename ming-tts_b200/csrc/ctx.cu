@@ -109,6 +109,7 @@ void mt_ctx_destroy(mt_ctx* ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->stack_area) cudaFree(ctx->stack_area);
     if (ctx->rope) cudaFree(ctx->rope);
     if (ctx->d_status) cudaFree(ctx->d_status);
     delete ctx;

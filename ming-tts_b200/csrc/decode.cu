@@ -19,26 +19,21 @@ constexpr int kDecodeMaxRows = 8;  // rows of all requests together: the CUDA-co
 // Scratch of one call, carved from the context's scratch area (fp32): normed rows, q/k/v rows,
 // attention rows and the gated MLP rows.
 struct DecodeScratch {
-    float *normed, *qkv, *attn, *mlp, *sync, *part;
+    float *normed, *qkv, *attn, *mlp;
 };
 
-// Sync words and attention partials of the persistent stack kernel (at most 32 layers).
-constexpr size_t kSyncWords = STACK_MAX_LAYERS * 5 + 2 + (size_t)STACK_MAX_LAYERS * STACK_MAX_UNITS;
-
-size_t decode_scratch_floats(const mt_qwen_config& c, int M, int ctas) {
+size_t decode_scratch_floats(const mt_qwen_config& c, int M) {
     const size_t qkvw = (size_t)(c.heads + 2 * c.kv_heads) * 64;
     auto up = [](size_t n) { return (n + 63) & ~size_t(63); };  // 256-byte aligned pieces
-    return up((size_t)M * c.hidden) + up((size_t)M * qkvw) + up((size_t)M * c.heads * 64) + up((size_t)M * c.intermediate) +
-           up(kSyncWords) + up(stack_part_floats(ctas));
+    return up((size_t)M * c.hidden) + up((size_t)M * qkvw) + up((size_t)M * c.heads * 64) + up((size_t)M * c.intermediate);
 }
 
 bool aligned(const void* p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0; }
 
-// The persistent stack kernel's view of the call, or false when it does not apply (shape limits,
-// unaligned weights, or the context's choice).
+// The persistent stack kernel's view of the call (without its area), or false when it does not
+// apply (shape limits, unaligned weights, or the context's choice).
 bool stack_params(mt_ctx* ctx, const mt_qwen_weights* w, int requests, int rows, float* x, float* kv, long long kv_stride,
-                  int capacity, const int32_t* positions, float* z, const float* inv_freq, const DecodeScratch& sc,
-                  StackParams* out) {
+                  int capacity, const int32_t* positions, float* z, const float* inv_freq, StackParams* out) {
     const mt_qwen_config& c = w->cfg;
     if (ctx->persistent == 0 || c.layers > STACK_MAX_LAYERS) return false;
     StackParams& p = *out;
@@ -46,8 +41,7 @@ bool stack_params(mt_ctx* ctx, const mt_qwen_weights* w, int requests, int rows,
     p.kind = STACK_QWEN; p.layers = c.layers; p.M = requests * rows; p.seq_rows = rows; p.seqs = requests;
     p.hidden = c.hidden; p.heads = c.heads; p.kv_heads = c.kv_heads; p.inter = c.intermediate; p.eps = c.eps;
     p.window = c.window; p.cap = capacity; p.kv_stride = kv_stride; p.pos = positions; p.kv = kv; p.inv_freq = inv_freq;
-    p.x = x; p.qkv = sc.qkv; p.attn = sc.attn; p.mlp = sc.mlp; p.z = z; p.final_norm = w->final_norm;
-    p.sync = reinterpret_cast<unsigned int*>(sc.sync); p.attn_part = sc.part; p.status = ctx->d_status;
+    p.x = x; p.z = z; p.final_norm = w->final_norm; p.status = ctx->d_status;
     if (!aligned(w->final_norm, 8)) return false;
     for (int l = 0; l < c.layers; l++) {
         const mt_qwen_layer& L = w->layers[l];
@@ -60,6 +54,26 @@ bool stack_params(mt_ctx* ctx, const mt_qwen_weights* w, int requests, int rows,
     return stack_supported(p, ctx->sm_count);
 }
 
+// The context's stack area, grown (after the device drains: earlier launches may still use it)
+// to at least `bytes`; a new area starts zeroed.
+mt_status ctx_stack_area(mt_ctx* ctx, size_t bytes, void** out) {
+    if (bytes > ctx->stack_area_bytes) {
+        if (ctx->stack_area) {
+            const cudaError_t e = cudaDeviceSynchronize();
+            if (e != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "stack area grow sync: %s", cudaGetErrorString(e));
+            cudaFree(ctx->stack_area);
+            ctx->stack_area = nullptr;
+            ctx->stack_area_bytes = 0;
+        }
+        const size_t want = bytes < ((size_t)1 << 20) ? ((size_t)1 << 20) : bytes;
+        const mt_status st = stack_area_alloc(want, &ctx->stack_area);
+        if (st != MT_OK) return fail(ctx, st, "persistent-stack area of %zu bytes", want);
+        ctx->stack_area_bytes = want;
+    }
+    *out = ctx->stack_area;
+    return MT_OK;
+}
+
 DecodeScratch carve(float* base, const mt_qwen_config& c, int M) {
     const size_t qkvw = (size_t)(c.heads + 2 * c.kv_heads) * 64;
     auto up = [](size_t n) { return (n + 63) & ~size_t(63); };
@@ -68,8 +82,6 @@ DecodeScratch carve(float* base, const mt_qwen_config& c, int M) {
     s.qkv = s.normed + up((size_t)M * c.hidden);
     s.attn = s.qkv + up((size_t)M * qkvw);
     s.mlp = s.attn + up((size_t)M * c.heads * 64);
-    s.sync = s.mlp + up((size_t)M * c.intermediate);
-    s.part = s.sync + up(kSyncWords);
     return s;
 }
 
@@ -116,12 +128,12 @@ extern "C" mt_status mt_qwen_decode(mt_ctx* ctx, void* stream, const mt_qwen_wei
     const float* inv_freq = nullptr;
     mt_status st = rope_table(ctx, c.rope_theta, &inv_freq);
     if (st != MT_OK) return st;
-    void* buf = nullptr;
-    st = mt::scratch(ctx, s, decode_scratch_floats(c, M, ctx->sm_count) * sizeof(float), &buf);
-    if (st != MT_OK) return st;
-    DecodeScratch sc = carve(static_cast<float*>(buf), c, M);
     StackParams sp;
-    if (stack_params(ctx, w, requests, rows, x, kv, kv_stride, capacity, positions, z, inv_freq, sc, &sp)) {
+    if (stack_params(ctx, w, requests, rows, x, kv, kv_stride, capacity, positions, z, inv_freq, &sp)) {
+        void* area = nullptr;
+        st = ctx_stack_area(ctx, stack_area_bytes(sp), &area);
+        if (st != MT_OK) return st;
+        stack_bind(sp, area);
         launch_stack(sp, ctx->sm_count, s);
         return check_launch(ctx, "mt_qwen_decode (persistent)");
     }
@@ -129,6 +141,10 @@ extern "C" mt_status mt_qwen_decode(mt_ctx* ctx, void* stream, const mt_qwen_wei
                "mt_qwen_decode: the persistent stack kernel cannot run this pass (%d requests x %d rows, window %d, "
                "capacity %d; %s %s)", requests, rows, c.window, capacity,
                stack_resident_blocks() < 1 ? "it does not fit one block per SM:" : "shapes", stack_resident_why());
+    void* buf = nullptr;
+    st = mt::scratch(ctx, s, decode_scratch_floats(c, M) * sizeof(float), &buf);
+    if (st != MT_OK) return st;
+    DecodeScratch sc = carve(static_cast<float*>(buf), c, M);
 
     const int H = c.hidden, qkvw = (c.heads + 2 * c.kv_heads) * 64, A = c.heads * 64;
     const size_t tensor = (size_t)c.kv_heads * capacity * 64;

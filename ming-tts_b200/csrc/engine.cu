@@ -81,8 +81,7 @@ struct Group {
     // Few rows: the LLM token, flow DiT pass and aggregator as persistent stack launches.
     bool llm_ps = false, flow_ps = false, agg_ps = false;
     StackParams llm_sp{}, flow_sp{}, agg_sp{};
-    unsigned int* sync = nullptr;  // sync words of this group's stack launches (its stream runs them in turn)
-    float* part = nullptr;         // their attention partials
+    void* stack_area = nullptr;  // area of this group's stack launches (its stream runs them in turn)
 };
 
 }  // namespace mt
@@ -135,8 +134,7 @@ struct mt_engine {
     Lin vae_head;
     bool vae_ps = false;        // VAE decode stack as one persistent launch (4R <= 8 rows)
     StackParams vae_sp{};
-    unsigned int* vae_sync = nullptr;
-    float* vae_part = nullptr;
+    void* vae_area = nullptr;   // area of the VAE decode's stack launches
     Group groups[kMaxGroups];
     int G = 1;  // groups of the current generation
 
@@ -297,13 +295,10 @@ mt_status plan_dit(mt_engine* e, std::vector<DitBlockPlans>& plans, const mt_dit
     return MT_OK;
 }
 
-// >= stack_sync_words of any pass: phase counters, abort flag and per-unit attention counters
-constexpr int kStackSyncWords = STACK_MAX_LAYERS * 5 + 2 + STACK_MAX_LAYERS * STACK_MAX_UNITS;
-
 // A Qwen pass over `rows` rows (rows_per_req per request, positions pos_dev) as one persistent stack
 // launch; false where the context disables it or the shapes do not fit (then one launch per op).
 bool qwen_stack(mt_engine* e, const mt_qwen_weights& W, const QwenBufs& b, int rows, int rows_per_req,
-                const int* pos_dev, float* z, unsigned int* sync, float* part, StackParams* out) {
+                const int* pos_dev, float* z, void* area, StackParams* out) {
     const mt_qwen_config& c = W.cfg;
     if (e->ctx->persistent == 0 || rows > kGemvMax || c.layers > STACK_MAX_LAYERS) return false;
     StackParams& p = *out;
@@ -312,19 +307,18 @@ bool qwen_stack(mt_engine* e, const mt_qwen_weights& W, const QwenBufs& b, int r
     p.hidden = c.hidden; p.heads = c.heads; p.kv_heads = c.kv_heads; p.inter = c.intermediate; p.eps = c.eps;
     p.window = c.window; p.cap = b.cap; p.kv_stride = (long long)c.layers * 2 * c.kv_heads * b.cap * 64;
     p.pos = pos_dev; p.kv = b.kv; p.inv_freq = b.inv_freq;
-    p.x = b.x; p.qkv = b.qkv; p.attn = b.attn.f; p.mlp = b.mlp.f; p.z = z; p.final_norm = W.final_norm;
-    p.sync = sync; p.attn_part = part; p.status = e->ctx->d_status;
+    p.x = b.x; p.z = z; p.final_norm = W.final_norm; p.status = e->ctx->d_status;
     for (int l = 0; l < c.layers; l++) {
         const mt_qwen_layer& L = W.layers[l];
         const mt_bf16* ptrs[8] = {L.norm1, L.qkv_w, L.qkv_b, L.o_w, L.norm2, L.gate_w, L.up_w, L.down_w};
         for (int i = 0; i < 8; i++) p.L[l].p[i] = ptrs[i];
     }
+    stack_bind(p, area);
     return stack_supported(p, e->ctx->sm_count);
 }
 
 // The blocks of a DiT pass over `batch` sequences of `seq` rows as one persistent stack launch.
-bool dit_stack(mt_engine* e, const mt_dit_weights& W, const DitBufs& b, int batch, int seq, unsigned int* sync,
-               StackParams* out) {
+bool dit_stack(mt_engine* e, const mt_dit_weights& W, const DitBufs& b, int batch, int seq, void* area, StackParams* out) {
     const mt_dit_config& c = W.cfg;
     if (e->ctx->persistent == 0 || batch * seq > kGemvMax || c.depth > STACK_MAX_LAYERS) return false;
     StackParams& p = *out;
@@ -332,14 +326,30 @@ bool dit_stack(mt_engine* e, const mt_dit_weights& W, const DitBufs& b, int batc
     p.kind = STACK_DIT; p.layers = c.depth; p.M = batch * seq; p.seq_rows = seq; p.seqs = batch;
     p.hidden = c.hidden; p.heads = c.heads; p.kv_heads = c.heads; p.inter = c.ff; p.eps = c.eps;
     p.inv_freq = W.inv_freq;
-    p.x = b.x; p.qkv = b.qkv; p.attn = b.attn.f; p.mlp = b.ff.f;
-    p.sync = sync; p.status = e->ctx->d_status;
+    p.x = b.x; p.status = e->ctx->d_status;
     for (int i = 0; i < c.depth; i++) {
         const mt_dit_block& B = W.blocks[i];
         const mt_bf16* ptrs[10] = {B.norm1, B.qkv_w, B.qkv_b, B.out_w, B.out_b, B.norm2, B.ff1_w, B.ff1_b, B.ff2_w, B.ff2_b};
         for (int k = 0; k < 10; k++) p.L[i].p[k] = ptrs[k];
     }
+    stack_bind(p, area);
     return stack_supported(p, e->ctx->sm_count);
+}
+
+// Stack-area bytes of the largest pass (8 rows) of each kind: a Qwen stack with rows_per_req rows
+// per request over a cap-position cache, or a DiT stack.
+size_t qwen_area_bound(const mt_qwen_config& c, int rows_per_req, int cap) {
+    StackParams p{};
+    p.kind = STACK_QWEN; p.M = 8; p.seq_rows = rows_per_req; p.seqs = 8 / rows_per_req;
+    p.hidden = c.hidden; p.heads = c.heads; p.kv_heads = c.kv_heads; p.inter = c.intermediate;
+    p.window = c.window; p.cap = cap;
+    return stack_area_bytes(p);
+}
+size_t dit_area_bound(const mt_dit_config& c) {
+    StackParams p{};
+    p.kind = STACK_DIT; p.M = 8; p.seq_rows = 1; p.seqs = 8;
+    p.hidden = c.hidden; p.heads = c.heads; p.kv_heads = c.heads; p.inter = c.ff;
+    return stack_area_bytes(p);
 }
 
 Act act_rows(const Act& a, size_t row) {
@@ -417,9 +427,9 @@ mt_status plan_group(mt_engine* e, Group& g, int r0, int Rg) {
                  c.agg.hidden, g.llm.x, H, nullptr, 0));
     // Stack launches take every SM: only where one chain runs at a time (a single request group).
     const bool solo = group_count(e, e->R) == 1;
-    g.llm_ps = solo && qwen_stack(e, e->w.llm, g.llm, Rg, 1, g.llm_pos, g.z.f, g.sync, g.part, &g.llm_sp);
-    g.flow_ps = solo && dit_stack(e, e->w.flow, g.flow, 2 * Rg, 3, g.sync, &g.flow_sp);
-    g.agg_ps = solo && dit_stack(e, e->w.agg, g.agg, Rg, 2, g.sync, &g.agg_sp);
+    g.llm_ps = solo && qwen_stack(e, e->w.llm, g.llm, Rg, 1, g.llm_pos, g.z.f, g.stack_area, &g.llm_sp);
+    g.flow_ps = solo && dit_stack(e, e->w.flow, g.flow, 2 * Rg, 3, g.stack_area, &g.flow_sp);
+    g.agg_ps = solo && dit_stack(e, e->w.agg, g.agg, Rg, 2, g.stack_area, &g.agg_sp);
     return MT_OK;
 }
 
@@ -439,7 +449,7 @@ mt_status build_plans(mt_engine* e) {
     TRY(make_lin(e, &e->vae_head, e->vae_hidden, 4 * R, e->w.vae_head_w, nullptr, e->w.vae_head_b, c.nfft + 2,
                  c.vae.hidden, e->spec, c.nfft + 2, nullptr, 0));
     e->vae_ps = e->G == 1 && qwen_stack(e, e->w.vae, e->vae, 4 * R, 4, e->state_dev + st_vae_pos(R), e->vae_hidden.f,
-                                        e->vae_sync, e->vae_part, &e->vae_sp);
+                                        e->vae_area, &e->vae_sp);
     e->plan_R = R;
     e->plan_T = T;
     return MT_OK;
@@ -780,11 +790,17 @@ mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_o
     ETRY(dalloc(e, &e->ws_a, e->ws_a_floats));
     ETRY(dalloc(e, &e->ws_b, e->ws_b_floats));
     ETRY(dalloc(e, &e->ids_stage, (size_t)R * T));
-    ETRY(dalloc(e, &e->vae_sync, kStackSyncWords));
-    ETRY(dalloc(e, &e->vae_part, stack_part_floats(ctx->sm_count)));
-    for (int i = 0; i < kMaxGroups; i++) {
-        ETRY(dalloc(e, &e->groups[i].sync, kStackSyncWords));
-        ETRY(dalloc(e, &e->groups[i].part, stack_part_floats(ctx->sm_count)));
+    {
+        // Persistent-stack areas (zeroed here, once): one per request group, one for the VAE decode.
+        const size_t group_area = std::max(qwen_area_bound(c.llm, 1, c.llm_capacity),
+                                           std::max(dit_area_bound(c.flow), dit_area_bound(c.agg)));
+        uint8_t* a = nullptr;
+        ETRY(dalloc(e, &a, qwen_area_bound(c.vae, 4, ring)));
+        e->vae_area = a;
+        for (int i = 0; i < kMaxGroups; i++) {
+            ETRY(dalloc(e, &a, group_area));
+            e->groups[i].stack_area = a;
+        }
     }
     if (cudaMallocHost(&e->state_slots[0], st_size(R) * sizeof(int)) != cudaSuccess ||
         cudaMallocHost(&e->state_slots[1], st_size(R) * sizeof(int)) != cudaSuccess ||

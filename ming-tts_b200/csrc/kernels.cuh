@@ -156,7 +156,6 @@ void run_gemm_plan(const GemmPlan& p, cudaStream_t s);
 // Persistent small-batch stack (stack.cu): every layer of a Qwen decode pass, or every block of a
 // DiT pass, in one cooperative launch over at most 8 activation rows.
 constexpr int STACK_MAX_LAYERS = 32;
-constexpr int STACK_MAX_UNITS = 64;  // attention units (sequence, kv head) of a Qwen pass, at most
 enum : int { STACK_QWEN = 0, STACK_DIT = 1 };
 struct StackLayer { const uint16_t* p[10]; };  // Qwen: norm1 qkv_w qkv_b o_w norm2 gate_w up_w down_w;
                                                 // DiT: norm1 qkv_w qkv_b out_w out_b norm2 ff1_w ff1_b ff2_w ff2_b
@@ -170,12 +169,13 @@ struct StackParams {
     const int* pos;                  // device [seqs]: cached positions per request (Qwen)
     float* kv;
     const float* inv_freq;           // [32]: NeoX frequencies (Qwen) or the DiT's rotary inv_freq
-    float* x;                        // residual rows [M, hidden], updated in place
-    float *qkv, *attn, *mlp;         // scratch rows
+    float* x;                        // residual rows [M, hidden]: read at the start, written at the end
     float* z;                        // Qwen: final norm of every row [M, hidden] (NULL: none)
     const uint16_t* final_norm;
-    unsigned int* sync;              // stack_sync_words() words, zeroed by launch_stack
-    float* attn_part;                // Qwen: stack_part_floats() floats of attention partials
+    // Stack area (stack_bind): sync words and the mailbox rows that carry activations between CTAs.
+    unsigned int* sync;
+    unsigned long long *mb_x, *mb_qkv, *mb_att, *mb_mlp;
+    int chunks;                      // Qwen: attention chunks per unit, at most
     unsigned int* status;            // context status word (bounded waits)
     StackLayer L[STACK_MAX_LAYERS];
 };
@@ -183,8 +183,12 @@ bool stack_supported(const StackParams& p, int ctas);
 int stack_resident_blocks();  // blocks of the stack kernel one SM of the current device holds (>= 1 to launch)
 const char* stack_resident_why();  // what kept it below one block, when it is
 int stack_phases(const StackParams& p);
-int stack_sync_words(const StackParams& p);  // phase counters, abort flag, per-unit attention counters
-size_t stack_part_floats(int ctas);
+// Bytes of the stack area a pass needs (shape fields set). An area belongs to one launch sequence:
+// it is zeroed once (stack_area_alloc) and every launch that uses it runs after the previous one on
+// the GPU; passes of different shapes may share it.
+size_t stack_area_bytes(const StackParams& p);
+void stack_bind(StackParams& p, void* area);
+mt_status stack_area_alloc(size_t bytes, void** out);
 void launch_stack(const StackParams& p, int ctas, cudaStream_t s);
 
 }  // namespace mt
