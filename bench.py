@@ -46,6 +46,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 AUDIO_PER_STEP = 0.08  # 3528 samples at 44.1 kHz (Text/MingRequest.swift:104)
 RUN_STEPS = 256        # config 5: prefill then 256 autoregressive steps
+SAMPLE_RATE = 44100
 METRIC = "audio-sec/sec of the Ming-3.0-tts-0.5B step loop (config 5 serving, per-GPU replicas)"
 # DRAM bytes (read + write) of one launch of the roofline GEMM at the flow ff1 shape, from an ncu
 # capture of that kernel (dram__bytes_read.sum + dram__bytes_write.sum); reported, not measured here.
@@ -324,6 +325,45 @@ def time_decode(mt, ctx, model, cfg, requests, length=256, iters=20, rounds=3):
     return best
 
 
+def convdec_flops(cfg, frames):
+    """Algorithmic FLOPs of one conv-decoder call: 2 per multiply-add of every convolution (a
+    transposed convolution of kernel 2 s: 2 input frames x C_in per output value)."""
+    C, S, K = list(cfg.channels), list(cfg.strides), cfg.kernel
+    f = 2 * frames * C[0] * cfg.latent_dim * K
+    t = frames
+    for i in range(4):
+        f += 2 * t * S[i] * C[i + 1] * 2 * C[i]
+        t *= S[i]
+        f += 2 * 2 * t * C[i + 1] * C[i + 1] * K
+    return f + 2 * t * C[4] * K
+
+
+def time_convdec(mt, ctx, frames=216, iters=10, rounds=3):
+    """Config 4: one mt_convdec_decode of `frames` latent frames (10 s of audio at 216), inputs
+    resident, CUDA events on the launching stream, best of `rounds` means over `iters` calls."""
+    import torch
+    cfg = mt.default_convdec_config()
+    dec = mt.ConvDecoder(ctx, mt.convdec_random_weights(cfg, 4), cfg, max_frames=frames)
+    lat = torch.randn(frames, cfg.latent_dim, device="cuda")
+    pcm = dec.decode(lat)
+    for _ in range(3):
+        dec.decode(lat, pcm)
+    best = None
+    for _ in range(rounds):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            dec.decode(lat, pcm)
+        e.record()
+        e.synchronize()
+        t = s.elapsed_time(e) * 1e-3 / iters
+        best = t if best is None else min(best, t)
+    ctx.check()
+    samples = dec.samples(frames)
+    dec.close()
+    return best, samples, convdec_flops(cfg, frames)
+
+
 # ------------------------------------------------------------------------------------------------
 # Serving measurements
 # ------------------------------------------------------------------------------------------------
@@ -513,6 +553,17 @@ def cpu_configs(oracle, hm):
     t4 = (time.perf_counter() - t0) * 125 / sample
     out["config4"] = {"ms_per_10s_clip": round(t4 * 1e3, 1), "audio_s_per_s": round(10.0 / t4, 3),
                       "sample": f"{sample} latents decoded (flush included), scaled to 125"}
+    # Config 4 as BASELINE describes it: the 1-D convolutional decoder, fp64 host restatement;
+    # 4 latent frames timed and scaled to 216 (10 s).
+    from oracle import convdec as cdo
+    ccfg = cdo.default_config()
+    cw = cdo.random_weights(ccfg, 4)
+    lat = oracle.gaussian_noise(4 * ccfg.latent_dim, 4).reshape(4, ccfg.latent_dim)
+    t0 = time.perf_counter()
+    cdo.decode(ccfg, cw, lat)
+    tc = (time.perf_counter() - t0) * 216 / 4
+    out["config4_conv"] = {"ms_per_10s_clip": round(tc * 1e3, 1), "audio_s_per_s": round(216 * 2048 / 44100 / tc, 3),
+                           "sample": "4 latent frames through the fp64 numpy restatement, scaled to 216"}
     return out
 
 
@@ -619,6 +670,8 @@ def main():
                     help="N,K[,M]: time the CUDA-core GEMV over a >= 1 GiB weight pool alone and exit (for focused profiling)")
     ap.add_argument("--decode", type=int, default=0,
                     help="M: time the config-2 decode step at M sequences alone and exit (for focused profiling)")
+    ap.add_argument("--convdec", type=int, default=0,
+                    help="frames: time the config-4 convolutional decoder alone and exit (for focused profiling)")
     ap.add_argument("--profile", action="store_true",
                     help="prefill, warm-up and timed steps only (for a profiler's launch list); prints ms/step")
     args = ap.parse_args()
@@ -644,6 +697,12 @@ def main():
         nbytes = n * k * 2 + m * k * 4 + m * n * 4
         print(json.dumps({"gemv": [m, n, k], "us": round(t * 1e6, 3), "gbs": round(nbytes / t / 1e9, 1),
                           "pool_copies": copies}), flush=True)
+        return
+    if args.convdec:
+        t, samples, fl = time_convdec(mt, ctx, args.convdec)
+        print(json.dumps({"convdec": args.convdec, "ms": round(t * 1e3, 4), "samples": samples,
+                          "audio_s_per_s": round(samples / SAMPLE_RATE / t, 1),
+                          "tflops": round(fl / t / 1e12, 1)}), flush=True)
         return
     cfg = mt.default_config()
     model = mt.Model(ctx, cfg, seed=1, with_embeddings=True)
@@ -736,6 +795,15 @@ def main():
                                "gbs": round(nb / t_d / 1e9, 1), "frac": round(nb / t_d / 1e9 / hbm_peak, 4)}
         decode["shape"] = "config 2: 24-layer LLM decode + stop head, KV cache 256 of 512 positions, M sequences"
         decode["peak_gbs"] = hbm_peak
+        t_cd, cd_samples, cd_flops = time_convdec(mt, ctx, 216)
+        t_cd = dist_max(t_cd, world)
+        convdec = {"frames": 216, "samples": cd_samples, "ms": round(t_cd * 1e3, 4),
+                   "audio_s_per_s": round(cd_samples / SAMPLE_RATE / t_cd, 1),
+                   "tflops": round(cd_flops / t_cd / 1e12, 1), "gflop": round(cd_flops / 1e9, 2),
+                   "frac": round(cd_flops / t_cd / 1e12 / bf16_peak, 4), "peak_tflops": bf16_peak,
+                   "note": "config 4: conv_in + 4 x (transposed conv + 2-conv residual block) + conv/tanh head, "
+                           "implicit GEMMs on tcgen05 (bf16 hi+lo: 0.5 of peak is the cap); this library's own "
+                           "decoder definition, not the reference's (parity unpinned)"}
         extra = {
             "ttfa_ms": {"p50": round(ttfa[0] * 1e3, 2), "calls": ttfa[1], "requests_per_call": R,
                         "includes": "ids+noise H2D, prefill of all requests, steps 0-2, first PCM chunk D2H "
@@ -746,6 +814,7 @@ def main():
                      "pool": f"{copies} distinct weight copies (>= 1 GiB), graph replay",
                      "peak_gbs": hbm_peak, "peak_kind": peak_kind},
             "decode": decode,
+            "config4_conv": convdec,
             "single_request": single,
             "stages_ms": {"llm": stage_ms[0], "flow": stage_ms[1], "agg": stage_ms[2], "vae_concurrent": stage_ms[3],
                           "note": "one eager step, events per stage; the VAE decode runs on a second stream"},

@@ -281,7 +281,10 @@ mt_status mt_rope_attention(mt_ctx* ctx, void* stream, const float* qkv, int ldq
  * positions[r] .. positions[r] + rows - 1 and are appended. With w->cfg.window == 0 the caller keeps
  * positions[r] + rows <= capacity; with a window the cache may be a ring (window + rows - 1 <= capacity).
  * Replaces the decode use of QwenForward.dispatches; scratch comes from the context (the first call
- * with a given shape and rope theta sets it up synchronously, so make it before any stream capture). */
+ * with a given shape and rope theta sets it up synchronously, so make it before any stream capture).
+ * On the persistent path (mt_ctx_set_persistent) the context also keeps a zeroed stack area, grown
+ * (after a device synchronisation) when a larger pass needs it; persistent calls on one context must
+ * not overlap on the GPU (each takes every SM). */
 mt_status mt_qwen_decode(mt_ctx* ctx, void* stream, const mt_qwen_weights* w, int requests, int rows, float* x,
                          float* kv, long long kv_stride, int capacity, const int32_t* positions, float* z);
 
@@ -532,6 +535,53 @@ void mt_gaussian_noise_host(float* out, size_t count, uint64_t seed);
 void mt_randn_bf16_host(mt_bf16* out, size_t count, uint64_t seed, float std);
 mt_status mt_randn_bf16(mt_ctx* ctx, void* stream, mt_bf16* out, size_t count, uint64_t seed,
                         float std);
+
+/* ---------------------------------------------------------------------------------------------
+ * 1-D convolutional waveform decoder (latents -> 44.1 kHz mono)
+ *
+ * No counterpart in the reference: its VAE decoder is the windowed Qwen stack + ISTFT above
+ * (VAEDecoder.swift:1-108). This is the convolution stack that BASELINE config 4 describes,
+ * defined here (parity is against this library's own fp64 host restatement, not the reference):
+ *   x   = conv_in(latents)                                  kernel k, latent_dim -> C0
+ *   for stage i = 0..3 (stride s_i, C_i -> C_{i+1}):
+ *     u = conv_transpose(silu(x))                           kernel 2 s_i, stride s_i, padding s_i / 2
+ *     x = u + conv_b(silu(conv_a(silu(u))))                 kernels k, C_{i+1} -> C_{i+1}
+ *   pcm = tanh(conv_out(silu(x)))                           kernel k, C_4 -> 1
+ * Convolutions pad (k - 1) / 2 zeros at both ends (lengths are kept); every layer has a bias.
+ * Layouts follow PyTorch: Conv1d weight [out][in][k], ConvTranspose1d weight [in][out][2 s].
+ * Each convolution runs as an implicit GEMM on the tcgen05 tensor cores (time rows x output
+ * channels, K = taps x input channels), the transposed ones as one polyphase GEMM each.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct mt_convdec_config {
+    int latent_dim;   /* 64 (a multiple of 64) */
+    int channels[5];  /* C0..C4: 512, 256, 128, 64, 64 (multiples of 64) */
+    int strides[4];   /* 8, 8, 4, 8 (even) */
+    int kernel;       /* 7 (odd, <= 7) */
+} mt_convdec_config;
+
+/* Device bf16 weights in PyTorch layouts (see above). */
+typedef struct mt_convdec_weights {
+    const mt_bf16 *in_w, *in_b;          /* [C0][latent_dim][k], [C0] */
+    const mt_bf16 *up_w[4], *up_b[4];    /* [C_i][C_{i+1}][2 s_i], [C_{i+1}] */
+    const mt_bf16 *a_w[4], *a_b[4];      /* [C_{i+1}][C_{i+1}][k], [C_{i+1}] */
+    const mt_bf16 *b_w[4], *b_b[4];      /* [C_{i+1}][C_{i+1}][k], [C_{i+1}] */
+    const mt_bf16 *out_w, *out_b;        /* [1][C4][k], [1] */
+} mt_convdec_weights;
+
+typedef struct mt_convdec mt_convdec;
+
+/* Samples out of `frames` latent frames: frames x s_0 x s_1 x s_2 x s_3. */
+long long mt_convdec_samples(const mt_convdec_config* cfg, int frames);
+/* Repacks the weights into GEMM layouts (the caller's buffers may be freed afterwards) and
+ * allocates the activation buffers for up to max_frames frames (zero halo rows included).
+ * Synchronous. */
+mt_status mt_convdec_create(mt_ctx* ctx, const mt_convdec_config* cfg, const mt_convdec_weights* w, int max_frames,
+                            mt_convdec** out);
+/* latents: device fp32 [frames][latent_dim]; pcm: device fp32 [mt_convdec_samples(frames)].
+ * Enqueued on `stream`; tensor maps are encoded on the host when `frames` differs from the
+ * previous call. */
+mt_status mt_convdec_decode(mt_convdec* dec, void* stream, const float* latents, int frames, float* pcm);
+void mt_convdec_destroy(mt_convdec* dec);
 
 #ifdef __cplusplus
 }

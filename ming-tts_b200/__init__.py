@@ -99,6 +99,16 @@ class EngineOptions(ctypes.Structure):
                 ("use_graphs", c_int), ("groups", c_int)]
 
 
+class ConvDecConfig(ctypes.Structure):
+    _fields_ = [("latent_dim", c_int), ("channels", c_int * 5), ("strides", c_int * 4), ("kernel", c_int)]
+
+
+class ConvDecWeights(ctypes.Structure):
+    _fields_ = [("in_w", c_void_p), ("in_b", c_void_p), ("up_w", c_void_p * 4), ("up_b", c_void_p * 4),
+                ("a_w", c_void_p * 4), ("a_b", c_void_p * 4), ("b_w", c_void_p * 4), ("b_b", c_void_p * 4),
+                ("out_w", c_void_p), ("out_b", c_void_p)]
+
+
 MT_DTYPE_BF16, MT_DTYPE_F32 = 0, 1
 BUF_Z, BUF_STOP_LOGITS, BUF_LATENTS, BUF_AGG_OUT, BUF_VELOCITY0, BUF_VAE_HIDDEN, BUF_PCM = range(7)
 
@@ -181,6 +191,10 @@ PROTOTYPES = {
     "mt_gaussian_noise_host": (None, [_P, c_size_t, c_uint64]),
     "mt_randn_bf16_host": (None, [_P, c_size_t, c_uint64, c_float]),
     "mt_randn_bf16": (c_int, [_P, _P, _P, c_size_t, c_uint64, c_float]),
+    "mt_convdec_samples": (ctypes.c_longlong, [POINTER(ConvDecConfig), c_int]),
+    "mt_convdec_create": (c_int, [_P, POINTER(ConvDecConfig), POINTER(ConvDecWeights), c_int, POINTER(c_void_p)]),
+    "mt_convdec_decode": (c_int, [_P, _P, _P, c_int, _P]),
+    "mt_convdec_destroy": (None, [_P]),
 }
 
 _lib = None
@@ -558,6 +572,92 @@ class Encoder:
         if self._e:
             lib().mt_encoder_destroy(self._e)
             self._e = c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------------------------------------
+# 1-D convolutional waveform decoder (mt_convdec_*)
+# ------------------------------------------------------------------------------------------------
+def default_convdec_config() -> ConvDecConfig:
+    """The decoder of BASELINE config 4: 64 latent channels, 512 -> 256 -> 128 -> 64 -> 64 channels,
+    upsampling strides 8, 8, 4, 8 (2048 samples per latent frame), kernel 7."""
+    c = ConvDecConfig()
+    c.latent_dim = 64
+    c.channels[:] = [512, 256, 128, 64, 64]
+    c.strides[:] = [8, 8, 4, 8]
+    c.kernel = 7
+    return c
+
+
+def convdec_shapes(cfg: ConvDecConfig):
+    """(name, PyTorch-layout shape, fan_in) of every decoder tensor, in a fixed order."""
+    C, S, K, L = list(cfg.channels), list(cfg.strides), cfg.kernel, cfg.latent_dim
+    out = [("in_w", (C[0], L, K), L * K), ("in_b", (C[0],), 0)]
+    for i in range(4):
+        out += [(f"up_w{i}", (C[i], C[i + 1], 2 * S[i]), 2 * C[i]), (f"up_b{i}", (C[i + 1],), 0),
+                (f"a_w{i}", (C[i + 1], C[i + 1], K), C[i + 1] * K), (f"a_b{i}", (C[i + 1],), 0),
+                (f"b_w{i}", (C[i + 1], C[i + 1], K), C[i + 1] * K), (f"b_b{i}", (C[i + 1],), 0)]
+    out += [("out_w", (1, C[4], K), C[4] * K), ("out_b", (1,), 0)]
+    return out
+
+
+def convdec_random_weights(cfg: ConvDecConfig, seed: int = 4):
+    """Seeded random-init weights as bf16 bits (uint16) in PyTorch layouts: N(0, 1 / fan_in) for
+    convolution weights (activations keep unit scale through the stack), N(0, 0.02^2) for biases;
+    tensor i draws from the SplitMix stream seeded seed * 1000 + i."""
+    import numpy as np
+    out = {}
+    for i, (name, shape, fan_in) in enumerate(convdec_shapes(cfg)):
+        n = int(np.prod(shape))
+        bits = np.zeros(n, np.uint16)
+        std = (1.0 / fan_in) ** 0.5 if fan_in else 0.02
+        lib().mt_randn_bf16_host(bits.ctypes.data, n, seed * 1000 + i, std)
+        out[name] = bits.reshape(shape)
+    return out
+
+
+class ConvDecoder:
+    """mt_convdec: latents [frames, latent_dim] -> PCM [frames * prod(strides)] on the tensor cores."""
+
+    def __init__(self, ctx: Context, weights: dict, cfg: ConvDecConfig | None = None, max_frames: int = 216):
+        import torch
+        self.ctx = ctx
+        self.cfg = cfg if cfg is not None else default_convdec_config()
+        self.max_frames = max_frames
+        dev = {k: torch.from_numpy(v.astype("uint16").view("int16").copy()).cuda() for k, v in weights.items()}
+        w = ConvDecWeights()
+        w.in_w, w.in_b, w.out_w, w.out_b = (dev[k].data_ptr() for k in ("in_w", "in_b", "out_w", "out_b"))
+        for i in range(4):
+            w.up_w[i], w.up_b[i] = dev[f"up_w{i}"].data_ptr(), dev[f"up_b{i}"].data_ptr()
+            w.a_w[i], w.a_b[i] = dev[f"a_w{i}"].data_ptr(), dev[f"a_b{i}"].data_ptr()
+            w.b_w[i], w.b_b[i] = dev[f"b_w{i}"].data_ptr(), dev[f"b_b{i}"].data_ptr()
+        self._d = c_void_p()
+        ctx._check(lib().mt_convdec_create(ctx.handle, ctypes.byref(self.cfg), ctypes.byref(w), max_frames,
+                                           ctypes.byref(self._d)), "mt_convdec_create")
+        del dev  # the decoder holds its own repacked copies
+
+    def samples(self, frames: int) -> int:
+        return int(lib().mt_convdec_samples(ctypes.byref(self.cfg), frames))
+
+    def decode(self, latents, pcm=None, stream=None):
+        """latents: CUDA fp32 tensor [frames, latent_dim]; returns (or fills) the CUDA fp32 PCM tensor."""
+        import torch
+        frames = latents.shape[0]
+        if pcm is None:
+            pcm = torch.empty(self.samples(frames), device=latents.device, dtype=torch.float32)
+        self.ctx._check(lib().mt_convdec_decode(self._d, stream if stream is not None else current_stream(),
+                                                latents.data_ptr(), frames, pcm.data_ptr()), "mt_convdec_decode")
+        return pcm
+
+    def close(self):
+        if self._d:
+            lib().mt_convdec_destroy(self._d)
+            self._d = c_void_p()
 
     def __del__(self):
         try:

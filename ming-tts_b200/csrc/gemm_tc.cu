@@ -192,7 +192,7 @@ __device__ __forceinline__ void epilogue_tile(const TcEpi& e, const TileCoord& t
 #pragma unroll
             for (int j = 0; j < 16; j++) {
                 uint16_t h, l;
-                split_bf16(val[j], h, l);
+                split_bf16(e.split_silu ? silu(val[j]) : val[j], h, l);
                 if (j < valid) {
                     hp[(size_t)j * e.ld_ysplit] = h;
                     lp[(size_t)j * e.ld_ysplit] = l;
@@ -408,12 +408,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                     for (int a = 0; a < na; a++) {
                         uint8_t* xs = st + a * atom_bytes + w_bytes * (GATED ? 2 : 1);
-                        const int kc = (kb + a) * TC_BK;
+                        int kc = (kb + a) * TC_BK, row = tc.m0;
+                        if (e.conv_cin) {  // convolution: a K atom lies inside one tap (conv_cin % 64 == 0)
+                            const int tap = kc / e.conv_cin;
+                            kc -= tap * e.conv_cin;
+                            row += tap + e.conv_row0;
+                        }
                         if (e.x_planes) {  // both planes, one copy (their order is free: the epilogue sums them)
-                            tma_load_3d(xs, &tm_xhi, &full_bar[s], kc, tc.m0, 0);
+                            tma_load_3d(xs, &tm_xhi, &full_bar[s], kc, row, 0);
                         } else {
-                            tma_load_2d(xs, &tm_xhi, &full_bar[s], kc, tc.m0);
-                            tma_load_2d(xs + x_bytes, &tm_xlo, &full_bar[s], kc, tc.m0);
+                            tma_load_2d(xs, &tm_xhi, &full_bar[s], kc, row);
+                            tma_load_2d(xs + x_bytes, &tm_xlo, &full_bar[s], kc, row);
                         }
                     }
                 }
@@ -790,7 +795,7 @@ static int epi_kind(const TcEpi& e, bool gated) {
     const bool accum = (e.flags & MT_LINEAR_ACCUM) != 0;
     const bool f32 = e.y != nullptr, split = e.y_hi != nullptr;
     if (e.mode == 1) return EPI_RED;  // split-K of a linear epilogue into fp32 y
-    if (e.mode != 0) return EPI_GENERIC;
+    if (e.mode != 0 || e.split_silu) return EPI_GENERIC;
     if (gated) return (!act && !accum && split && !f32) ? EPI_SPLIT_GATE : EPI_GENERIC;
     if (f32 && !split) {
         if (!act) return accum ? EPI_F32_ACCUM : EPI_F32;
@@ -849,7 +854,7 @@ static void set_gemm_attributes() {
 mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     const bool gated = (a.flags & MT_LINEAR_SILU_GATE) != 0;
     MT_REQUIRE(ctx, a.m > 0 && a.n > 0 && a.k > 0, MT_ERR_SHAPE, "gemm_tc: empty shape m %d n %d k %d", a.m, a.n, a.k);
-    MT_REQUIRE(ctx, a.k % 8 == 0 && a.ld_split % 8 == 0 && a.ld_split >= a.k, MT_ERR_SHAPE,
+    MT_REQUIRE(ctx, a.k % 8 == 0 && a.ld_split % 8 == 0 && (a.ld_split >= a.k || a.conv_cin > 0), MT_ERR_SHAPE,
                "gemm_tc: k %d ld %d need multiples of 8", a.k, a.ld_split);
     MT_REQUIRE(ctx, ((uintptr_t)a.w & 15u) == 0 && ((uintptr_t)a.x_hi & 15u) == 0 && ((uintptr_t)a.x_lo & 15u) == 0 &&
                         (!gated || ((uintptr_t)a.w2 & 15u) == 0),
@@ -857,14 +862,22 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     MT_REQUIRE(ctx, a.y || a.y_hi, MT_ERR_ARG, "gemm_tc: no output");
     MT_REQUIRE(ctx, !(a.flags & MT_LINEAR_BIAS) || a.bias, MT_ERR_ARG, "gemm_tc: BIAS needs bias");
     MT_REQUIRE(ctx, !(a.flags & MT_LINEAR_ACCUM) || a.y, MT_ERR_ARG, "gemm_tc: ACCUM needs fp32 y");
+    const bool conv = a.conv_cin > 0;
+    MT_REQUIRE(ctx, !conv || (a.conv_cin % TC_BK == 0 && a.k % a.conv_cin == 0 && a.conv_row0 >= 0 && a.x_rows > 0 &&
+                              a.ld_split >= a.conv_cin && !gated),
+               MT_ERR_SHAPE, "gemm_tc: convolution channels %d (multiple of 64 dividing k %d), row offset %d, rows %d",
+               a.conv_cin, a.k, a.conv_row0, a.x_rows);
     TcEpi& e = plan->e;
     e = TcEpi{};
     e.m = a.m; e.n = a.n; e.k = a.k;
+    e.conv_cin = conv ? a.conv_cin : 0;
+    e.conv_row0 = conv ? a.conv_row0 : 0;
+    e.split_silu = a.split_silu ? 1 : 0;
     const bool linear = !(a.flags & (MT_LINEAR_GELU | MT_LINEAR_SILU | MT_LINEAR_SILU_GATE)) && a.y && !a.y_hi;
     // Split-K by default only where partial sums can be reduced into y without zeroing it first
     // (ACCUM: y holds the residual). Tile rows measured on the engine's shapes: narrow tiles for few
     // rows (more CTAs), 128 rows once M is large (fewer weight re-reads through L2).
-    const bool splittable = linear && (a.flags & MT_LINEAR_ACCUM);
+    const bool splittable = linear && (a.flags & MT_LINEAR_ACCUM) && !conv && !a.split_silu;
     const int kb_total = (a.k + TC_BK - 1) / TC_BK;
     const int sms = ctx->sm_count > 0 ? ctx->sm_count : 148;
     const int n_tiles128 = (a.n + TC_BM - 1) / TC_BM;
@@ -882,7 +895,7 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     MT_REQUIRE(ctx, e.bn % 16 == 0 && e.bn <= (gated ? 64 : 128), MT_ERR_SHAPE, "gemm_tc: tile rows %d (16..%d)", e.bn,
                gated ? 64 : 128);
     // CTA pairs (256 weight rows per tile, one activation plane per CTA): on request only for now.
-    const bool pair = ctx->gemm_pairs == 1;
+    const bool pair = ctx->gemm_pairs == 1 && !conv;
     const int tile_rows = pair ? 2 * TC_BM : TC_BM;
     const int tiles_n = (a.n + tile_rows - 1) / tile_rows;
     const int slots = pair ? sms / 2 : sms;  // concurrent work units
@@ -920,9 +933,10 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
 
     bool ok = make_map(&plan->tw, a.w, a.n, a.k, a.k, TC_BM);
     ok = ok && make_map(&plan->tw2, gated ? a.w2 : a.w, a.n, a.k, a.k, TC_BM);
-    ok = ok && make_map(&plan->tl, a.x_lo, a.m, a.k, a.ld_split, e.bn);
-    e.x_planes = !pair && make_planes_map(&plan->th, a.x_hi, a.x_lo, a.m, a.k, a.ld_split, e.bn) ? 1 : 0;
-    if (!e.x_planes) ok = ok && make_map(&plan->th, a.x_hi, a.m, a.k, a.ld_split, e.bn);
+    const int x_rows = conv ? a.x_rows : a.m, x_cols = conv ? a.conv_cin : a.k;
+    ok = ok && make_map(&plan->tl, a.x_lo, x_rows, x_cols, a.ld_split, e.bn);
+    e.x_planes = !pair && make_planes_map(&plan->th, a.x_hi, a.x_lo, x_rows, x_cols, a.ld_split, e.bn) ? 1 : 0;
+    if (!e.x_planes) ok = ok && make_map(&plan->th, a.x_hi, x_rows, x_cols, a.ld_split, e.bn);
     MT_REQUIRE(ctx, ok, MT_ERR_CUDA, "gemm_tc: cuTensorMapEncodeTiled failed (m %d n %d k %d)", a.m, a.n, a.k);
     plan->gated = gated;
     plan->pair = pair;

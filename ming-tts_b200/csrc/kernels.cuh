@@ -103,6 +103,11 @@ struct LinearArgs {
     int bn_override;                           // tensor-core route: activation rows per tile (0 = auto)
     float* ws;                                 // tensor-core route: fp32 [m, 2n] workspace for split-K
                                                //   with a nonlinear epilogue (optional)
+    // Tensor-core route, implicit-GEMM convolution over time-major rows (0 = a plain GEMM): K is
+    // taps x conv_cin; K column tap * conv_cin + c of activation row m reads plane row
+    // m + tap + conv_row0, column c (rows outside [0, x_rows) read zeros).
+    int conv_cin, conv_row0, x_rows;
+    int split_silu;                            // tensor-core route: the hi/lo output planes hold silu(y)
 };
 void launch_gemv(const LinearArgs& a, cudaStream_t s);
 mt_status launch_gemm_tc(mt_ctx* ctx, const LinearArgs& a, cudaStream_t s);
@@ -136,6 +141,8 @@ struct TcEpi {
     int kind;          // EPI_* epilogue specialisation chosen by the planner (EPI_GENERIC: runtime flags)
     int x_planes;      // 1: the x_hi map is 3-D and one copy loads both activation planes of a stage
     int ka;            // K atoms (64-wide K blocks) per pipeline stage, 1 or 2
+    int conv_cin, conv_row0;  // implicit-GEMM convolution (LinearArgs): 0 = plain GEMM
+    int split_silu;    // the hi/lo planes take silu of the output value
     float* ws; int ldws;
     unsigned int* status;
 };
