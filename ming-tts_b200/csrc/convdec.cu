@@ -28,19 +28,29 @@ namespace mt {
 
 namespace {
 
-constexpr int kHalo = 3;  // zero rows before and after every activation buffer (taps of a 7-wide kernel)
+constexpr int kHalo = 4;  // zero rows before and after every activation buffer (>= the 3 of a 7-wide
+                          // kernel, and a multiple of the frame groups below)
 
-// Conv1d weight [co][ci][k] -> GEMM rows [co][k * ci_n + ci].
-__global__ void repack_conv_kernel(const uint16_t* __restrict__ w, int co_n, int ci_n, int k_n,
+// Conv1d weight [co][ci][k] -> GEMM rows for G output frames per row: row g * co_n + co, column
+// w * ci_n + ci over a window of G + k_n - 1 input frames, = weight[co][ci][w - g] (0 outside the
+// kernel). G = 1 is the plain [co][k * ci_n + ci] layout.
+__global__ void repack_conv_kernel(const uint16_t* __restrict__ w, int co_n, int ci_n, int k_n, int G,
                                    uint16_t* __restrict__ out) {
-    const long long total = (long long)co_n * ci_n * k_n;
+    const int win = G + k_n - 1;
+    const long long total = (long long)G * co_n * win * ci_n;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-        const int co = (int)(i / ((long long)ci_n * k_n));
-        const int rem = (int)(i - (long long)co * ci_n * k_n);
-        const int k = rem / ci_n, ci = rem - k * ci_n;
-        out[i] = w[((size_t)co * ci_n + ci) * k_n + k];
+        const int row = (int)(i / ((long long)win * ci_n));
+        const int col = (int)(i - (long long)row * win * ci_n);
+        const int g = row / co_n, co = row - g * co_n;
+        const int wi = col / ci_n, ci = col - wi * ci_n;
+        const int k = wi - g;
+        out[i] = (k >= 0 && k < k_n) ? w[((size_t)co * ci_n + ci) * k_n + k] : (uint16_t)0;
     }
 }
+
+// Output frames per GEMM row for a residual-block convolution of C channels: enough to fill the
+// MMA's 128 weight rows when C is narrower.
+int conv_group(int C) { return (C < 128 && 128 % C == 0 && kHalo % (128 / C) == 0) ? 128 / C : 1; }
 
 // ConvTranspose1d weight [ci][co][2 s] (stride s, padding s / 2) -> polyphase GEMM rows
 // [r * co_n + co][tap * ci_n + ci], tap 0/1/2 = input frame j - 1 / j / j + 1 of output sample
@@ -64,41 +74,59 @@ __global__ void repack_upconv_kernel(const uint16_t* __restrict__ w, const uint1
     }
 }
 
-// pcm[t] = tanh(b + sum_k sum_c w[c][k] silu(x[t + k - (K - 1) / 2][c])) over channels-last fp32 x
-// (rows outside [0, frames) read as zero, the convolution's padding; silu(0) = 0). A block stages
-// its rows (+ the kernel's reach) once, applying silu, then one thread per sample.
+// pcm[t] = tanh(b + sum_k d_k[t + k - (K - 1) / 2]) with d_k[r] = sum_c w[c][k] silu(x[r][c]) over
+// channels-last fp32 x (rows outside [0, frames) read as zero, the convolution's padding; silu(0) =
+// 0). A block stages silu of its rows (its samples plus the kernel's reach) with coalesced loads
+// into a padded tile, gives each row one thread that forms all K tap sums, then one thread per
+// sample adds K of them.
 constexpr int kOutTile = 256;
+constexpr int kOutMaxK = 7;
 __global__ void __launch_bounds__(256) conv_out_tanh_kernel(const float* __restrict__ x_pad, int frames, int C, int K,
                                                             const uint16_t* __restrict__ w, const uint16_t* __restrict__ b,
                                                             float* __restrict__ pcm) {
     extern __shared__ float sm[];
-    float* xs = sm;                                   // [(kOutTile + K - 1)][C + 1]
-    float* ws = sm + (size_t)(kOutTile + K - 1) * (C + 1);  // [K][C]
+    const int rows = kOutTile + K - 1, ldx = C + 1;
+    float* ws = sm;                               // [C][K]
+    float* d = ws + (size_t)C * K;                // [rows][kOutMaxK]
+    float* xs = d + (size_t)rows * kOutMaxK;      // [rows][C + 1]
     pdl_wait();
     const int t0 = blockIdx.x * kOutTile, half = (K - 1) / 2;
-    const int rows = kOutTile + K - 1;
-    for (int i = threadIdx.x; i < K * C; i += blockDim.x) {
-        const int k = i / C, c = i - k * C;
-        ws[i] = bf16f(w[(size_t)c * K + k]);
+    for (int i = threadIdx.x; i < K * C; i += blockDim.x) ws[i] = bf16f(w[i]);  // [1][C][K] as [c][k]
+    const int per = C / 4;
+    for (int i = threadIdx.x; i < rows * per; i += blockDim.x) {
+        const int rr = i / per, c4 = i - rr * per;
+        const int t = t0 + rr - half;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t >= 0 && t < frames) v = __ldg(reinterpret_cast<const float4*>(x_pad + (size_t)(t + kHalo) * C) + c4);
+        float* xr = xs + (size_t)rr * ldx + 4 * c4;
+        xr[0] = silu(v.x);
+        xr[1] = silu(v.y);
+        xr[2] = silu(v.z);
+        xr[3] = silu(v.w);
     }
-    for (int i = threadIdx.x; i < rows * C; i += blockDim.x) {
-        const int rr = i / C, c = i - rr * C;
-        const int t = t0 + rr - half;  // time index of the staged row
-        float v = 0.f;
-        if (t >= 0 && t < frames) v = x_pad[(size_t)(t + kHalo) * C + c];
-        xs[(size_t)rr * (C + 1) + c] = silu(v);
+    __syncthreads();
+    for (int rr = threadIdx.x; rr < rows; rr += blockDim.x) {
+        float acc[kOutMaxK];
+#pragma unroll
+        for (int k = 0; k < kOutMaxK; k++) acc[k] = 0.f;
+        const float* xr = xs + (size_t)rr * ldx;
+        for (int c = 0; c < C; c++) {
+            const float v = xr[c];
+            const float* wr = ws + (size_t)c * K;
+#pragma unroll
+            for (int k = 0; k < kOutMaxK; k++)
+                if (k < K) acc[k] = fmaf(wr[k], v, acc[k]);
+        }
+#pragma unroll
+        for (int k = 0; k < kOutMaxK; k++) d[(size_t)rr * kOutMaxK + k] = acc[k];
     }
     __syncthreads();
     pdl_launch();
     const int t = t0 + threadIdx.x;
     if (t >= frames) return;
-    float acc = bf16f(b[0]);
-    for (int k = 0; k < K; k++) {
-        const float* xr = xs + (size_t)(threadIdx.x + k) * (C + 1);
-        const float* wr = ws + (size_t)k * C;
-        for (int c = 0; c < C; c++) acc = fmaf(wr[c], xr[c], acc);
-    }
-    pcm[t] = tanhf(acc);
+    float out = bf16f(b[0]);
+    for (int k = 0; k < K; k++) out += d[(size_t)(threadIdx.x + k) * kOutMaxK + k];
+    pcm[t] = tanhf(out);
 }
 
 }  // namespace
@@ -124,6 +152,7 @@ struct mt_convdec {
     // GEMM-layout weights
     uint16_t *in_w = nullptr, *in_b = nullptr;
     uint16_t *up_w[4] = {}, *up_b[4] = {}, *a_w[4] = {}, *a_b[4] = {}, *b_w[4] = {}, *b_b[4] = {};
+    int group[4] = {1, 1, 1, 1};  // output frames per GEMM row of stage i's residual-block convolutions
     uint16_t *out_w = nullptr, *out_b = nullptr;
     uint16_t *lat_hi = nullptr, *lat_lo = nullptr;  // latent planes [max_frames + 2 halo][latent_dim]
     ConvLevel lv[5];
@@ -162,7 +191,7 @@ bool config_ok(const mt_convdec_config& c) {
         if (c.channels[i] <= 0 || c.channels[i] % 64) return false;
     for (int i = 0; i < 4; i++)
         if (c.strides[i] < 2 || c.strides[i] > 32 || c.strides[i] % 2) return false;
-    return c.kernel >= 1 && c.kernel % 2 == 1 && (c.kernel - 1) / 2 <= kHalo;
+    return c.kernel >= 1 && c.kernel % 2 == 1 && c.kernel <= kOutMaxK && (c.kernel - 1) / 2 <= kHalo;
 }
 
 long long level_frames(const mt_convdec_config& c, int frames, int level) {
@@ -171,26 +200,28 @@ long long level_frames(const mt_convdec_config& c, int frames, int level) {
     return t;
 }
 
-void repack_conv(const uint16_t* w, int co, int ci, int k, uint16_t* out) {
-    const long long total = (long long)co * ci * k;
+void repack_conv(const uint16_t* w, int co, int ci, int k, int G, uint16_t* out) {
+    const long long total = (long long)G * co * (G + k - 1) * ci;
     const int blocks = (int)std::min<long long>((total + 255) / 256, 148 * 16);
-    repack_conv_kernel<<<blocks, 256>>>(w, co, ci, k, out);
+    repack_conv_kernel<<<blocks, 256>>>(w, co, ci, k, G, out);
 }
 
 // One implicit-GEMM convolution: `taps` frames of x (planes of C_in channels, rows = H + frames)
-// centred on each output row, into n output channels.
+// centred on each output frame, into n output channels; G output frames per GEMM row (the planes
+// viewed as rows of G frames: frames and kHalo are multiples of G).
 LinearArgs conv_args(const uint16_t* x_hi, const uint16_t* x_lo, int c_in, int taps, int frames, int n,
-                     const uint16_t* w, const uint16_t* bias) {
+                     const uint16_t* w, const uint16_t* bias, int G = 1) {
     LinearArgs a{};
     a.x_hi = x_hi;
     a.x_lo = x_lo;
-    a.ld_split = c_in;
+    a.ld_split = G * c_in;
     a.conv_cin = c_in;
     a.conv_row0 = kHalo - (taps - 1) / 2;
-    a.x_rows = kHalo + frames;
-    a.m = frames;
-    a.n = n;
-    a.k = taps * c_in;
+    a.conv_group = G;
+    a.x_rows = (kHalo + frames) / G;
+    a.m = frames / G;
+    a.n = G * n;
+    a.k = (G + taps - 1) * c_in;
     a.w = w;
     a.bias = bias;
     a.flags = MT_LINEAR_BIAS;
@@ -225,19 +256,21 @@ mt_status build_plans(mt_convdec* d, int frames) {
         u.y_lo = dst.lo + (size_t)H * co;
         u.ld_ysplit = s * co;
         CD_TRY(make_gemm_plan(d->ctx, u, &d->up_plan[i]));
-        // residual block: h = conv_a(silu(u)) (its planes hold silu(h)), u += conv_b(silu(h))
-        LinearArgs a = conv_args(dst.hi, dst.lo, co, K, t_out, co, d->a_w[i], d->a_b[i]);
+        // residual block: h = conv_a(silu(u)) (its planes hold silu(h)), u += conv_b(silu(h)); G
+        // frames per GEMM row
+        const int G = d->group[i];
+        LinearArgs a = conv_args(dst.hi, dst.lo, co, K, t_out, co, d->a_w[i], d->a_b[i], G);
         a.y_hi = dst.h_hi + (size_t)H * co;
         a.y_lo = dst.h_lo + (size_t)H * co;
-        a.ld_ysplit = co;
+        a.ld_ysplit = G * co;
         CD_TRY(make_gemm_plan(d->ctx, a, &d->a_plan[i]));
-        LinearArgs b = conv_args(dst.h_hi, dst.h_lo, co, K, t_out, co, d->b_w[i], d->b_b[i]);
+        LinearArgs b = conv_args(dst.h_hi, dst.h_lo, co, K, t_out, co, d->b_w[i], d->b_b[i], G);
         b.flags |= MT_LINEAR_ACCUM;
         b.y = dst.f + (size_t)H * co;
-        b.ldy = co;
+        b.ldy = G * co;
         b.y_hi = dst.hi + (size_t)H * co;
         b.y_lo = dst.lo + (size_t)H * co;
-        b.ld_ysplit = co;
+        b.ld_ysplit = G * co;
         CD_TRY(make_gemm_plan(d->ctx, b, &d->b_plan[i]));
     }
     d->plan_frames = frames;
@@ -245,7 +278,8 @@ mt_status build_plans(mt_convdec* d, int frames) {
 }
 
 size_t out_smem(const mt_convdec_config& c) {
-    return ((size_t)(kOutTile + c.kernel - 1) * (c.channels[4] + 1) + (size_t)c.kernel * c.channels[4]) * sizeof(float);
+    const size_t rows = (size_t)kOutTile + c.kernel - 1;
+    return ((size_t)c.channels[4] * c.kernel + rows * kOutMaxK + rows * (c.channels[4] + 1)) * sizeof(float);
 }
 
 }  // namespace
@@ -261,7 +295,7 @@ extern "C" mt_status mt_convdec_create(mt_ctx* ctx, const mt_convdec_config* cfg
     *out = nullptr;
     MT_REQUIRE(ctx, config_ok(*cfg), MT_ERR_SHAPE,
                "mt_convdec_create: latent_dim and channels must be multiples of 64, strides even (2..32), kernel odd "
-               "(<= %d)", 2 * kHalo + 1);
+               "(<= %d)", kOutMaxK);
     MT_REQUIRE(ctx, max_frames >= 1 && level_frames(*cfg, max_frames, 4) + 2 * kHalo < (1LL << 31), MT_ERR_CAPACITY,
                "mt_convdec_create: max_frames %d", max_frames);
     bool have = w->in_w && w->in_b && w->out_w && w->out_b;
@@ -285,7 +319,7 @@ extern "C" mt_status mt_convdec_create(mt_ctx* ctx, const mt_convdec_config* cfg
     // weights in GEMM layouts
     CD_ETRY(cd_alloc(d, &d->in_w, (size_t)c.channels[0] * K * c.latent_dim));
     CD_ETRY(cd_alloc(d, &d->in_b, (size_t)c.channels[0]));
-    repack_conv(w->in_w, c.channels[0], c.latent_dim, K, d->in_w);
+    repack_conv(w->in_w, c.channels[0], c.latent_dim, K, 1, d->in_w);
     cudaMemcpy(d->in_b, w->in_b, sizeof(uint16_t) * c.channels[0], cudaMemcpyDefault);
     for (int i = 0; i < 4; i++) {
         const int ci = c.channels[i], co = c.channels[i + 1], s = c.strides[i];
@@ -295,14 +329,19 @@ extern "C" mt_status mt_convdec_create(mt_ctx* ctx, const mt_convdec_config* cfg
         repack_upconv_kernel<<<(int)std::min<long long>((total + 255) / 256, 148 * 16), 256>>>(w->up_w[i], w->up_b[i], ci,
                                                                                                co, s, d->up_w[i],
                                                                                                d->up_b[i]);
-        CD_ETRY(cd_alloc(d, &d->a_w[i], (size_t)co * K * co));
-        CD_ETRY(cd_alloc(d, &d->a_b[i], (size_t)co));
-        CD_ETRY(cd_alloc(d, &d->b_w[i], (size_t)co * K * co));
-        CD_ETRY(cd_alloc(d, &d->b_b[i], (size_t)co));
-        repack_conv(w->a_w[i], co, co, K, d->a_w[i]);
-        repack_conv(w->b_w[i], co, co, K, d->b_w[i]);
-        cudaMemcpy(d->a_b[i], w->a_b[i], sizeof(uint16_t) * co, cudaMemcpyDefault);
-        cudaMemcpy(d->b_b[i], w->b_b[i], sizeof(uint16_t) * co, cudaMemcpyDefault);
+        // frame groups where every call's row count at this level divides (a product of strides)
+        const int G = level_frames(c, 1, i + 1) % conv_group(co) == 0 ? conv_group(co) : 1;
+        d->group[i] = G;
+        CD_ETRY(cd_alloc(d, &d->a_w[i], (size_t)G * co * (G + K - 1) * co));
+        CD_ETRY(cd_alloc(d, &d->a_b[i], (size_t)G * co));
+        CD_ETRY(cd_alloc(d, &d->b_w[i], (size_t)G * co * (G + K - 1) * co));
+        CD_ETRY(cd_alloc(d, &d->b_b[i], (size_t)G * co));
+        repack_conv(w->a_w[i], co, co, K, G, d->a_w[i]);
+        repack_conv(w->b_w[i], co, co, K, G, d->b_w[i]);
+        for (int g = 0; g < G; g++) {  // the bias of output frame g of a row
+            cudaMemcpy(d->a_b[i] + (size_t)g * co, w->a_b[i], sizeof(uint16_t) * co, cudaMemcpyDefault);
+            cudaMemcpy(d->b_b[i] + (size_t)g * co, w->b_b[i], sizeof(uint16_t) * co, cudaMemcpyDefault);
+        }
     }
     CD_ETRY(cd_alloc(d, &d->out_w, (size_t)c.channels[4] * K));
     CD_ETRY(cd_alloc(d, &d->out_b, 1));

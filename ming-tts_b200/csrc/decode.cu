@@ -5,7 +5,7 @@
 // (VAEDecoder.swift:86-107), over caller-owned fp32 KV caches in the reference's layout
 // (Qwen.swift:7-26). Per layer: RMSNorm -> q/k/v GEMV (+bias) -> RoPE + KV append + attention ->
 // o GEMV (+=) -> RMSNorm -> gate/up GEMV (SiLU gate) -> down GEMV (+=); then the final norm of every
-// row. Passes that fit run as one launch of the persistent stack kernel (stack.cu); the others as
+// row. Each RMSNorm is folded into the GEMV that consumes it (up to 6 rows, gains 16-byte aligned). Passes that fit run as one launch of the persistent stack kernel (stack.cu); the others as
 // one launch per kernel above.
 #include "common.cuh"
 #include "kernels.cuh"
@@ -85,11 +85,13 @@ DecodeScratch carve(float* base, const mt_qwen_config& c, int M) {
     return s;
 }
 
+// One CUDA-core linear; with norm_w it reads RMSNorm(x) * norm_w (the norm folded in: no launch).
 void gemv(const float* x, int ldx, int m, const uint16_t* w, const uint16_t* w2, const uint16_t* bias, int n, int k,
-          float* y, int ldy, uint32_t flags, cudaStream_t s) {
+          float* y, int ldy, uint32_t flags, cudaStream_t s, const uint16_t* norm_w = nullptr, float eps = 0.f) {
     LinearArgs a{};
     a.x = x; a.ldx = ldx; a.m = m; a.n = n; a.k = k; a.w = w; a.w2 = w2; a.bias = bias;
     a.y = y; a.ldy = ldy; a.flags = flags; a.split_k = 1;
+    a.norm_w = norm_w; a.norm_eps = eps;
     launch_gemv(a, s);
 }
 
@@ -97,6 +99,19 @@ void norm(const float* x, int ld, int rows, int width, const uint16_t* g, float 
     RmsArgs a{};
     a.x = x; a.ldx = ld; a.rows = rows; a.width = width; a.w = g; a.eps = eps; a.y = y; a.ldy = ld;
     launch_rmsnorm(a, s);
+}
+
+// RMSNorm(x) * g, then the linear: folded into the GEMV for up to 6 rows when the gain is 16-byte
+// aligned (it loads as 16-byte vectors; with more rows the fold's per-chunk work makes the GEMV
+// compute-bound), else the norm's own launch into `normed` first.
+void norm_gemv(const float* x, int H, int m, const uint16_t* g, float eps, float* normed, const uint16_t* w,
+               const uint16_t* w2, const uint16_t* bias, int n, float* y, int ldy, uint32_t flags, cudaStream_t s) {
+    if (m <= 6 && ((uintptr_t)g & 15u) == 0) {
+        gemv(x, H, m, w, w2, bias, n, H, y, ldy, flags, s, g, eps);
+    } else {
+        norm(x, H, m, H, g, eps, normed, s);
+        gemv(normed, H, m, w, w2, bias, n, H, y, ldy, flags, s);
+    }
 }
 
 }  // namespace
@@ -151,8 +166,7 @@ extern "C" mt_status mt_qwen_decode(mt_ctx* ctx, void* stream, const mt_qwen_wei
     for (int l = 0; l < c.layers; l++) {
         const mt_qwen_layer& L = w->layers[l];
         float* kc = kv + (size_t)(2 * l) * tensor;
-        norm(x, H, M, H, L.norm1, c.eps, sc.normed, s);
-        gemv(sc.normed, H, M, L.qkv_w, nullptr, L.qkv_b, qkvw, H, sc.qkv, qkvw, MT_LINEAR_BIAS, s);
+        norm_gemv(x, H, M, L.norm1, c.eps, sc.normed, L.qkv_w, nullptr, L.qkv_b, qkvw, sc.qkv, qkvw, MT_LINEAR_BIAS, s);
         AttnDecodeArgs da{};
         da.qkv = sc.qkv; da.ldq = qkvw; da.requests = requests; da.rows_per_req = rows; da.hq = c.heads;
         da.hkv = c.kv_heads; da.pos0 = 0; da.pos_dev = positions; da.window = c.window; da.kc = kc; da.vc = kc + tensor;
@@ -160,9 +174,8 @@ extern "C" mt_status mt_qwen_decode(mt_ctx* ctx, void* stream, const mt_qwen_wei
         da.max_keys = c.window > 0 ? c.window : capacity; da.status = ctx->d_status;
         launch_attention_decode(da, s);
         gemv(sc.attn, A, M, L.o_w, nullptr, nullptr, H, A, x, H, MT_LINEAR_ACCUM, s);
-        norm(x, H, M, H, L.norm2, c.eps, sc.normed, s);
-        gemv(sc.normed, H, M, L.gate_w, L.up_w, nullptr, c.intermediate, H, sc.mlp, c.intermediate, MT_LINEAR_SILU_GATE,
-             s);
+        norm_gemv(x, H, M, L.norm2, c.eps, sc.normed, L.gate_w, L.up_w, nullptr, c.intermediate, sc.mlp, c.intermediate,
+                  MT_LINEAR_SILU_GATE, s);
         gemv(sc.mlp, c.intermediate, M, L.down_w, nullptr, nullptr, H, c.intermediate, x, H, MT_LINEAR_ACCUM, s);
     }
     norm(x, H, M, H, w->final_norm, c.eps, z, s);

@@ -259,6 +259,22 @@ void norm(const float* x, int ldx, int rows, int width, const mt_bf16* w, float 
     g_kernels++;
 }
 
+// Rows up to which a CUDA-core linear folds the RMSNorm before it: measured on the config-2 decode
+// step, one row gains 3%, eight rows lose 11% (the per-chunk gain and x^2 work makes the GEMV
+// compute-bound); the flow DiT's six rows gain 3%.
+constexpr int kFoldNormMax = 6;
+
+// A linear after an RMSNorm, on the CUDA-core route with few rows: it reads the residual rows and
+// folds the norm in (gain as x loads, 1/rms on the dot product), so the norm has no launch.
+bool folds_norm(int rows) { return rows <= kFoldNormMax; }
+void fold_norm(Lin* L, const float* x, int ld, const mt_bf16* g, float eps) {
+    if (L->tc || !folds_norm(L->g.m)) return;
+    L->g.x = x;
+    L->g.ldx = ld;
+    L->g.norm_w = g;
+    L->g.norm_eps = eps;
+}
+
 mt_status plan_qwen(mt_engine* e, std::vector<QwenLayerPlans>& plans, const mt_qwen_weights& W, QwenBufs& b, int rows,
                     float* ws, size_t ws_floats) {
     const mt_qwen_config& c = W.cfg;
@@ -273,6 +289,8 @@ mt_status plan_qwen(mt_engine* e, std::vector<QwenLayerPlans>& plans, const mt_q
                      &b.mlp, MT_LINEAR_SILU_GATE, ws, ws_floats));
         TRY(make_lin(e, &plans[l].down, b.mlp, rows, L.down_w, nullptr, nullptr, c.hidden, c.intermediate, b.x,
                      c.hidden, nullptr, MT_LINEAR_ACCUM));
+        fold_norm(&plans[l].qkv, b.x, c.hidden, L.norm1, c.eps);
+        fold_norm(&plans[l].gu, b.x, c.hidden, L.norm2, c.eps);
     }
     return MT_OK;
 }
@@ -291,6 +309,8 @@ mt_status plan_dit(mt_engine* e, std::vector<DitBlockPlans>& plans, const mt_dit
                      MT_LINEAR_GELU, ws, ws_floats));
         TRY(make_lin(e, &plans[i].ff2, b.ff, rows, B.ff2_w, nullptr, B.ff2_b, c.hidden, c.ff, b.x, c.hidden, nullptr,
                      MT_LINEAR_ACCUM));
+        fold_norm(&plans[i].qkv, b.x, c.hidden, B.norm1, c.eps);
+        fold_norm(&plans[i].ff1, b.x, c.hidden, B.norm2, c.eps);
     }
     return MT_OK;
 }
@@ -468,7 +488,7 @@ void qwen_forward(mt_engine* e, const mt_qwen_weights& W, QwenBufs& b, std::vect
         const mt_qwen_layer& L = W.layers[l];
         float* kc = b.kv + (size_t)(2 * l) * tensor;
         float* vc = kc + tensor;
-        norm(b.x, c.hidden, rows, c.hidden, L.norm1, c.eps, b.norm, rows, false, s);
+        if (!folds_norm(rows) || tc) norm(b.x, c.hidden, rows, c.hidden, L.norm1, c.eps, b.norm, rows, false, s);
         run(plans[l].qkv, s);
         if (attention_decode_supported(rows_per_req, c.heads, c.kv_heads)) {
             // Decode: every row of a request in one block, RoPE and the KV append fused in.
@@ -481,7 +501,7 @@ void qwen_forward(mt_engine* e, const mt_qwen_weights& W, QwenBufs& b, std::vect
             da.max_keys = max_keys; da.status = e->ctx->d_status;
             launch_attention_decode(da, s); g_kernels++;
             run(plans[l].o, s);
-            norm(b.x, c.hidden, rows, c.hidden, L.norm2, c.eps, b.norm, rows, false, s);
+            if (!folds_norm(rows) || tc) norm(b.x, c.hidden, rows, c.hidden, L.norm2, c.eps, b.norm, rows, false, s);
             run(plans[l].gu, s);
             run(plans[l].down, s);
             continue;
@@ -499,7 +519,7 @@ void qwen_forward(mt_engine* e, const mt_qwen_weights& W, QwenBufs& b, std::vect
         else { aa.out = b.attn.f; aa.ldo = b.attn.ld; }
         launch_attention(aa, s); g_kernels++;
         run(plans[l].o, s);
-        norm(b.x, c.hidden, rows, c.hidden, L.norm2, c.eps, b.norm, rows, false, s);
+        if (!folds_norm(rows) || tc) norm(b.x, c.hidden, rows, c.hidden, L.norm2, c.eps, b.norm, rows, false, s);
         run(plans[l].gu, s);
         run(plans[l].down, s);
     }
@@ -514,7 +534,7 @@ void dit_blocks(mt_engine* e, const mt_dit_weights& W, DitBufs& b, std::vector<D
     const bool tc = rows > kGemvMax;
     for (int i = 0; i < c.depth; i++) {
         const mt_dit_block& B = W.blocks[i];
-        norm(b.x, c.hidden, rows, c.hidden, B.norm1, c.eps, b.norm, rows, false, s);
+        if (!folds_norm(rows) || tc) norm(b.x, c.hidden, rows, c.hidden, B.norm1, c.eps, b.norm, rows, false, s);
         run(plans[i].qkv, s);
         DitAttnArgs da{};
         da.qkv = b.qkv; da.ld = 3 * c.hidden; da.batch = batch; da.seq = seq; da.heads = c.heads;
@@ -523,7 +543,7 @@ void dit_blocks(mt_engine* e, const mt_dit_weights& W, DitBufs& b, std::vector<D
         else { da.out = b.attn.f; da.ldo = b.attn.ld; }
         launch_dit_attention(da, s); g_kernels++;
         run(plans[i].out, s);
-        norm(b.x, c.hidden, rows, c.hidden, B.norm2, c.eps, b.norm, rows, false, s);
+        if (!folds_norm(rows) || tc) norm(b.x, c.hidden, rows, c.hidden, B.norm2, c.eps, b.norm, rows, false, s);
         run(plans[i].ff1, s);
         run(plans[i].ff2, s);
     }

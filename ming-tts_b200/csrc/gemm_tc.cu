@@ -236,7 +236,37 @@ __device__ __forceinline__ void epilogue_fast(const TcEpi& e, const TileCoord& t
             v[j] = t;
         }
         const bool full = valid == 16 && all_live;
-        if (KIND == EPI_F32 || KIND == EPI_F32_ACCUM || KIND == EPI_F32_SILU || KIND == EPI_RED) {
+        if (KIND == EPI_F32_SSILU || KIND == EPI_ACC_SSILU || KIND == EPI_SSILU) {
+            // fp32 stream (optionally accumulated) and the bf16 hi/lo planes of its silu
+            if (KIND != EPI_SSILU) {
+                float* __restrict__ yp = e.y + row0 * ldy + n;
+                if (KIND == EPI_ACC_SSILU) {
+                    float old[16];
+#pragma unroll
+                    for (int j = 0; j < 16; j++) old[j] = (full || (live_n && j < valid)) ? yp[j * ldy] : 0.f;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] += old[j];
+                }
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (full || (live_n && j < valid)) yp[j * ldy] = v[j];
+            }
+            uint16_t* __restrict__ hp = e.y_hi + row0 * lds + n;
+            uint16_t* __restrict__ lp = e.y_lo + row0 * lds + n;
+#pragma unroll
+            for (int j = 0; j < 16; j += 2) {
+                uint32_t h2, l2;
+                split_bf16x2(silu(v[j]), silu(v[j + 1]), h2, l2);
+                if (full || (live_n && j < valid)) {
+                    hp[j * lds] = (uint16_t)h2;
+                    lp[j * lds] = (uint16_t)l2;
+                }
+                if (full || (live_n && j + 1 < valid)) {
+                    hp[(j + 1) * lds] = (uint16_t)(h2 >> 16);
+                    lp[(j + 1) * lds] = (uint16_t)(l2 >> 16);
+                }
+            }
+        } else if (KIND == EPI_F32 || KIND == EPI_F32_ACCUM || KIND == EPI_F32_SILU || KIND == EPI_RED) {
             float* __restrict__ yp = e.y + row0 * ldy + n;
             if (full) {
                 if (KIND == EPI_F32_ACCUM) {
@@ -410,9 +440,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         uint8_t* xs = st + a * atom_bytes + w_bytes * (GATED ? 2 : 1);
                         int kc = (kb + a) * TC_BK, row = tc.m0;
                         if (e.conv_cin) {  // convolution: a K atom lies inside one tap (conv_cin % 64 == 0)
-                            const int tap = kc / e.conv_cin;
-                            kc -= tap * e.conv_cin;
-                            row += tap + e.conv_row0;
+                            const int tap = kc / e.conv_cin, q = tap + e.conv_row0;
+                            const int g = q / e.conv_group;
+                            kc += (q - g * e.conv_group - tap) * e.conv_cin;
+                            row += g;
                         }
                         if (e.x_planes) {  // both planes, one copy (their order is free: the epilogue sums them)
                             tma_load_3d(xs, &tm_xhi, &full_bar[s], kc, row, 0);
@@ -795,7 +826,12 @@ static int epi_kind(const TcEpi& e, bool gated) {
     const bool accum = (e.flags & MT_LINEAR_ACCUM) != 0;
     const bool f32 = e.y != nullptr, split = e.y_hi != nullptr;
     if (e.mode == 1) return EPI_RED;  // split-K of a linear epilogue into fp32 y
-    if (e.mode != 0 || e.split_silu) return EPI_GENERIC;
+    if (e.mode != 0) return EPI_GENERIC;
+    if (e.split_silu) {
+        if (gated || act || !split) return EPI_GENERIC;
+        if (!f32) return accum ? EPI_GENERIC : EPI_SSILU;
+        return accum ? EPI_ACC_SSILU : EPI_F32_SSILU;
+    }
     if (gated) return (!act && !accum && split && !f32) ? EPI_SPLIT_GATE : EPI_GENERIC;
     if (f32 && !split) {
         if (!act) return accum ? EPI_F32_ACCUM : EPI_F32;
@@ -822,6 +858,9 @@ static GemmKernel gemm_kernel_ka(bool gated, int kind) {
         case EPI_SPLIT_GELU: return gemm_tc_kernel<false, EPI_SPLIT_GELU, KA>;
         case EPI_F32_SILU: return gemm_tc_kernel<false, EPI_F32_SILU, KA>;
         case EPI_RED: return gemm_tc_kernel<false, EPI_RED, KA>;
+        case EPI_F32_SSILU: return gemm_tc_kernel<false, EPI_F32_SSILU, KA>;
+        case EPI_ACC_SSILU: return gemm_tc_kernel<false, EPI_ACC_SSILU, KA>;
+        case EPI_SSILU: return gemm_tc_kernel<false, EPI_SSILU, KA>;
         default: return gemm_tc_kernel<false, EPI_GENERIC, KA>;
     }
 }
@@ -836,8 +875,8 @@ static GemmKernel gemm_kernel_for(bool gated, int kind, int ka) {
 static void set_gemm_attributes() {
     static PerDeviceOnce once;
     once([] {
-        const int kinds[] = {EPI_GENERIC, EPI_F32, EPI_F32_ACCUM, EPI_SPLIT, EPI_SPLIT_GELU, EPI_SPLIT_GATE,
-                             EPI_F32_SILU, EPI_RED};
+        const int kinds[] = {EPI_GENERIC, EPI_F32,   EPI_F32_ACCUM, EPI_SPLIT,     EPI_SPLIT_GELU, EPI_SPLIT_GATE,
+                             EPI_F32_SILU, EPI_RED, EPI_F32_SSILU, EPI_ACC_SSILU, EPI_SSILU};
         for (int kd : kinds) {
             for (int ka = 1; ka <= TC_KA_MAX; ka++) {
                 cudaFuncSetAttribute(gemm_kernel_for(false, kd, ka), cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -872,6 +911,7 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
     e.m = a.m; e.n = a.n; e.k = a.k;
     e.conv_cin = conv ? a.conv_cin : 0;
     e.conv_row0 = conv ? a.conv_row0 : 0;
+    e.conv_group = conv && a.conv_group > 1 ? a.conv_group : 1;
     e.split_silu = a.split_silu ? 1 : 0;
     const bool linear = !(a.flags & (MT_LINEAR_GELU | MT_LINEAR_SILU | MT_LINEAR_SILU_GATE)) && a.y && !a.y_hi;
     // Split-K by default only where partial sums can be reduced into y without zeroing it first
@@ -933,7 +973,9 @@ mt_status make_gemm_plan(mt_ctx* ctx, const LinearArgs& a, GemmPlan* plan) {
 
     bool ok = make_map(&plan->tw, a.w, a.n, a.k, a.k, TC_BM);
     ok = ok && make_map(&plan->tw2, gated ? a.w2 : a.w, a.n, a.k, a.k, TC_BM);
-    const int x_rows = conv ? a.x_rows : a.m, x_cols = conv ? a.conv_cin : a.k;
+    const int x_rows = conv ? a.x_rows : a.m, x_cols = conv ? a.conv_cin * e.conv_group : a.k;
+    MT_REQUIRE(ctx, !conv || a.ld_split >= x_cols, MT_ERR_SHAPE, "gemm_tc: convolution row stride %d < %d",
+               a.ld_split, x_cols);
     ok = ok && make_map(&plan->tl, a.x_lo, x_rows, x_cols, a.ld_split, e.bn);
     e.x_planes = !pair && make_planes_map(&plan->th, a.x_hi, a.x_lo, x_rows, x_cols, a.ld_split, e.bn) ? 1 : 0;
     if (!e.x_planes) ok = ok && make_map(&plan->th, a.x_hi, x_rows, x_cols, a.ld_split, e.bn);

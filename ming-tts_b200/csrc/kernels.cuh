@@ -104,10 +104,16 @@ struct LinearArgs {
     float* ws;                                 // tensor-core route: fp32 [m, 2n] workspace for split-K
                                                //   with a nonlinear epilogue (optional)
     // Tensor-core route, implicit-GEMM convolution over time-major rows (0 = a plain GEMM): K is
-    // taps x conv_cin; K column tap * conv_cin + c of activation row m reads plane row
-    // m + tap + conv_row0, column c (rows outside [0, x_rows) read zeros).
-    int conv_cin, conv_row0, x_rows;
+    // taps x conv_cin; with q = tap + conv_row0, K column tap * conv_cin + c of GEMM row m reads plane
+    // row m + q / conv_group, column (q % conv_group) * conv_cin + c (rows outside [0, x_rows) read
+    // zeros). conv_group G > 1 views the activations as rows of G frames (ld_split >= G conv_cin).
+    int conv_cin, conv_row0, x_rows, conv_group;
     int split_silu;                            // tensor-core route: the hi/lo output planes hold silu(y)
+    // CUDA-core route: x is the raw residual stream and the linear reads RMSNorm(x) * norm_w
+    // (Shaders.swift:418-441) -- the gain scales x as it loads, the 1/rms of each row the dot
+    // product -- so no separate norm launch precedes it (NULL: x is used as is).
+    const uint16_t* norm_w;
+    float norm_eps;
 };
 void launch_gemv(const LinearArgs& a, cudaStream_t s);
 mt_status launch_gemm_tc(mt_ctx* ctx, const LinearArgs& a, cudaStream_t s);
@@ -123,6 +129,9 @@ enum EpiKind : int {
     EPI_SPLIT_GATE = 5,  // hi/lo = split(silu(acc1 (+ bias)) * acc2)
     EPI_F32_SILU = 6,    // y = silu(acc (+ bias))
     EPI_RED = 7,         // split-K partial: y += acc (+ bias on the first split), fp32 reductions
+    EPI_F32_SSILU = 8,   // y = acc (+ bias); hi/lo = split(silu(y))          (convolution decoder)
+    EPI_ACC_SSILU = 9,   // y += acc (+ bias); hi/lo = split(silu(y))
+    EPI_SSILU = 10,      // hi/lo = split(silu(acc (+ bias)))
 };
 
 // Epilogue/launch parameters of the tensor-core GEMM (gemm_tc.cu).
@@ -141,7 +150,7 @@ struct TcEpi {
     int kind;          // EPI_* epilogue specialisation chosen by the planner (EPI_GENERIC: runtime flags)
     int x_planes;      // 1: the x_hi map is 3-D and one copy loads both activation planes of a stage
     int ka;            // K atoms (64-wide K blocks) per pipeline stage, 1 or 2
-    int conv_cin, conv_row0;  // implicit-GEMM convolution (LinearArgs): 0 = plain GEMM
+    int conv_cin, conv_row0, conv_group;  // implicit-GEMM convolution (LinearArgs): conv_cin 0 = plain GEMM
     int split_silu;    // the hi/lo planes take silu of the output value
     float* ws; int ldws;
     unsigned int* status;

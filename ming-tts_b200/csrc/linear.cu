@@ -16,15 +16,22 @@ namespace mt {
 
 constexpr int GEMV_THREADS = 256;
 
-// acc[r] (+ acc2[r] for the gated up projection) += x[r, k0:k0+8] . w[k0:k0+8] for the rows present.
-template <int MR, bool GATED>
-__device__ __forceinline__ void gemv_chunk(float (&acc)[MR], float (&acc2)[MR], const uint4& w, const uint4& w2,
-                                           const float* x, int ldx, int rows, int k0) {
+// acc[r] (+ acc2[r] for the gated up projection) += x[r, k0:k0+8] . w[k0:k0+8] for the rows present;
+// with NORM, x is first scaled by the gain chunk g and ss[r] collects the raw x^2 (the row's RMS).
+template <int MR, bool GATED, bool NORM>
+__device__ __forceinline__ void gemv_chunk(float (&acc)[MR], float (&acc2)[MR], float (&ss)[MR], const uint4& w,
+                                           const uint4& w2, const uint4& g, const float* x, int ldx, int rows, int k0) {
 #pragma unroll
     for (int r = 0; r < MR; r++) {
         if (r < rows) {
-            const float4 x0 = *reinterpret_cast<const float4*>(x + (size_t)r * ldx + k0);
-            const float4 x1 = *reinterpret_cast<const float4*>(x + (size_t)r * ldx + k0 + 4);
+            float4 x0 = *reinterpret_cast<const float4*>(x + (size_t)r * ldx + k0);
+            float4 x1 = *reinterpret_cast<const float4*>(x + (size_t)r * ldx + k0 + 4);
+            if (NORM) {
+                ss[r] += x0.x * x0.x + x0.y * x0.y + x0.z * x0.z + x0.w * x0.w + x1.x * x1.x + x1.y * x1.y +
+                         x1.z * x1.z + x1.w * x1.w;
+                x0 = make_float4(x0.x * bf16_lo(g.x), x0.y * bf16_hi(g.x), x0.z * bf16_lo(g.y), x0.w * bf16_hi(g.y));
+                x1 = make_float4(x1.x * bf16_lo(g.z), x1.y * bf16_hi(g.z), x1.z * bf16_lo(g.w), x1.w * bf16_hi(g.w));
+            }
             acc[r] += x0.x * bf16_lo(w.x) + x0.y * bf16_hi(w.x) + x0.z * bf16_lo(w.y) + x0.w * bf16_hi(w.y) +
                       x1.x * bf16_lo(w.z) + x1.y * bf16_hi(w.z) + x1.z * bf16_lo(w.w) + x1.w * bf16_hi(w.w);
             if (GATED)
@@ -34,11 +41,12 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[MR], float (&acc2)[MR], 
     }
 }
 
-template <int MR, int G, bool GATED>
+template <int MR, int G, bool GATED, bool NORM>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(LinearArgs a) {
     constexpr int C = GEMV_THREADS / G;  // columns per block
     constexpr int U = G >= 128 ? 8 : 4;  // chunks per thread loaded ahead of the dependency wait
-    __shared__ float red[GATED ? 2 : 1][GEMV_THREADS / 32][MR];
+    constexpr int NR = 1 + (GATED ? 1 : 0) + (NORM ? 1 : 0);  // partial sums per row: dot, gated dot, x^2
+    __shared__ float red[NR][GEMV_THREADS / 32][MR];
     const int tid = threadIdx.x;
     const int group = tid / G, gl = tid % G;
     const int n = blockIdx.x * C + group;
@@ -48,26 +56,27 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(LinearArgs a)
     const uint16_t* wrow = a.w + (size_t)(live ? n : 0) * a.k;
     const uint16_t* w2row = GATED ? a.w2 + (size_t)(live ? n : 0) * a.k : nullptr;
 
-    // The weights do not depend on the previous kernel: all of this thread's first U 16-byte loads
-    // (every load when k <= 8 U G, which the group size ensures up to k = 8192) are issued before
-    // the dependency wait, so they stream while the previous kernel drains.
-    uint4 wv[U], wv2[U];
+    // The weights (and norm gains) do not depend on the previous kernel: all of this thread's first
+    // U 16-byte loads (every load when k <= 8 U G, which the group size ensures up to k = 8192) are
+    // issued before the dependency wait, so they stream while the previous kernel drains.
+    uint4 wv[U], wv2[U], gv[U];
 #pragma unroll
     for (int u = 0; u < U; u++) {
         const int c = gl + u * G;
-        wv[u] = wv2[u] = make_uint4(0, 0, 0, 0);
+        wv[u] = wv2[u] = gv[u] = make_uint4(0, 0, 0, 0);
         if (live && c < chunks) {
             wv[u] = ld_stream_u4(wrow + (size_t)c * 8);
             if (GATED) wv2[u] = ld_stream_u4(w2row + (size_t)c * 8);
+            if (NORM) gv[u] = __ldg(reinterpret_cast<const uint4*>(a.norm_w + (size_t)c * 8));
         }
     }
     pdl_wait();
     pdl_launch();
     const int rows = min(MR, a.m - row0);
 
-    float acc[MR], acc2[MR];
+    float acc[MR], acc2[MR], ss[MR];
 #pragma unroll
-    for (int r = 0; r < MR; r++) { acc[r] = 0.f; acc2[r] = 0.f; }
+    for (int r = 0; r < MR; r++) { acc[r] = 0.f; acc2[r] = 0.f; ss[r] = 0.f; }
 
     if (live) {
         const float* x = a.x + (size_t)row0 * a.ldx;
@@ -75,12 +84,13 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(LinearArgs a)
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const int c = gl + u * G;
-            if (c < chunks) gemv_chunk<MR, GATED>(acc, acc2, wv[u], wv2[u], x, a.ldx, rows, c * 8);
+            if (c < chunks) gemv_chunk<MR, GATED, NORM>(acc, acc2, ss, wv[u], wv2[u], gv[u], x, a.ldx, rows, c * 8);
         }
         for (int c = gl + U * G; c < chunks; c += G) {
             const uint4 w = ld_stream_u4(wrow + (size_t)c * 8);
             const uint4 w2 = GATED ? ld_stream_u4(w2row + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
-            gemv_chunk<MR, GATED>(acc, acc2, w, w2, x, a.ldx, rows, c * 8);
+            const uint4 g = NORM ? __ldg(reinterpret_cast<const uint4*>(a.norm_w + (size_t)c * 8)) : make_uint4(0, 0, 0, 0);
+            gemv_chunk<MR, GATED, NORM>(acc, acc2, ss, w, w2, g, x, a.ldx, rows, c * 8);
         }
     }
 
@@ -92,6 +102,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(LinearArgs a)
         for (int o = WG / 2; o > 0; o >>= 1) {
             acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
             if (GATED) acc2[r] += __shfl_xor_sync(0xffffffffu, acc2[r], o);
+            if (NORM) ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], o);
         }
     }
     if (G > 32) {
@@ -100,7 +111,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(LinearArgs a)
 #pragma unroll
             for (int r = 0; r < MR; r++) {
                 red[0][warp][r] = acc[r];
-                if (GATED) red[GATED ? 1 : 0][warp][r] = acc2[r];
+                if (GATED) red[1][warp][r] = acc2[r];
+                if (NORM) red[NR - 1][warp][r] = ss[r];
             }
         }
         __syncthreads();
@@ -108,13 +120,15 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(LinearArgs a)
         const int w0 = group * (G / 32);
 #pragma unroll
         for (int r = 0; r < MR; r++) {
-            float s = 0.f, s2 = 0.f;
+            float s = 0.f, s2 = 0.f, s3 = 0.f;
             for (int w = 0; w < G / 32; w++) {
                 s += red[0][w0 + w][r];
                 if (GATED) s2 += red[GATED ? 1 : 0][w0 + w][r];
+                if (NORM) s3 += red[NR - 1][w0 + w][r];
             }
             acc[r] = s;
             acc2[r] = s2;
+            ss[r] = s3;
         }
     } else if (gl != 0) {
         return;
@@ -125,8 +139,14 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(LinearArgs a)
 #pragma unroll
     for (int r = 0; r < MR; r++) {
         if (r < rows) {
-            float v = acc[r] + bval;
-            if (GATED) v = silu(v) * acc2[r];
+            float v = acc[r], v2 = acc2[r];
+            if (NORM) {
+                const float rs = rsqrtf(ss[r] / (float)a.k + a.norm_eps);
+                v *= rs;
+                v2 *= rs;
+            }
+            v += bval;
+            if (GATED) v = silu(v) * v2;
             if (a.flags & MT_LINEAR_GELU) v = gelu_tanh(v);
             if (a.flags & MT_LINEAR_SILU) v = silu(v);
             float* yp = a.y + (size_t)(row0 + r) * a.ldy + n;
@@ -136,16 +156,27 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(LinearArgs a)
     }
 }
 
-template <int MR, bool GATED>
+template <int MR, bool GATED, bool NORM>
 static void launch_gemv_g(const LinearArgs& a, int G, cudaStream_t s) {
     const int C = GEMV_THREADS / G;
     dim3 grid((a.n + C - 1) / C, (a.m + MR - 1) / MR);
     switch (G) {
-        case 8: launch_k(gemv_stream_kernel<MR, 8, GATED>, grid, GEMV_THREADS, 0, s, a); break;
-        case 16: launch_k(gemv_stream_kernel<MR, 16, GATED>, grid, GEMV_THREADS, 0, s, a); break;
-        case 32: launch_k(gemv_stream_kernel<MR, 32, GATED>, grid, GEMV_THREADS, 0, s, a); break;
-        case 64: launch_k(gemv_stream_kernel<MR, 64, GATED>, grid, GEMV_THREADS, 0, s, a); break;
-        default: launch_k(gemv_stream_kernel<MR, 128, GATED>, grid, GEMV_THREADS, 0, s, a); break;
+        case 8: launch_k(gemv_stream_kernel<MR, 8, GATED, NORM>, grid, GEMV_THREADS, 0, s, a); break;
+        case 16: launch_k(gemv_stream_kernel<MR, 16, GATED, NORM>, grid, GEMV_THREADS, 0, s, a); break;
+        case 32: launch_k(gemv_stream_kernel<MR, 32, GATED, NORM>, grid, GEMV_THREADS, 0, s, a); break;
+        case 64: launch_k(gemv_stream_kernel<MR, 64, GATED, NORM>, grid, GEMV_THREADS, 0, s, a); break;
+        default: launch_k(gemv_stream_kernel<MR, 128, GATED, NORM>, grid, GEMV_THREADS, 0, s, a); break;
+    }
+}
+
+template <int MR>
+static void launch_gemv_mr(const LinearArgs& a, int G, bool gated, cudaStream_t s) {
+    if (a.norm_w) {
+        if (gated) launch_gemv_g<MR, true, true>(a, G, s);
+        else launch_gemv_g<MR, false, true>(a, G, s);
+    } else {
+        if (gated) launch_gemv_g<MR, true, false>(a, G, s);
+        else launch_gemv_g<MR, false, false>(a, G, s);
     }
 }
 
@@ -217,27 +248,18 @@ __global__ void __launch_bounds__(256) gemv_narrow_kernel(LinearArgs a) {
 }
 
 void launch_gemv(const LinearArgs& a, cudaStream_t s) {
-    if (a.n <= NARROW_MAX_N && a.k % 128 == 0 && !(a.flags & MT_LINEAR_SILU_GATE) && a.ldx % 4 == 0) {
+    if (a.n <= NARROW_MAX_N && a.k % 128 == 0 && !(a.flags & MT_LINEAR_SILU_GATE) && a.ldx % 4 == 0 && !a.norm_w) {
         launch_k(gemv_narrow_kernel, (a.m + 7) / 8, 256, 0, s, a);
         return;
     }
     const int G = gemv_group(a.k);
     const bool gated = (a.flags & MT_LINEAR_SILU_GATE) != 0;
     const int mr = a.m <= 1 ? 1 : a.m <= 2 ? 2 : a.m <= 4 ? 4 : 8;
-    if (gated) {
-        switch (mr) {
-            case 1: launch_gemv_g<1, true>(a, G, s); break;
-            case 2: launch_gemv_g<2, true>(a, G, s); break;
-            case 4: launch_gemv_g<4, true>(a, G, s); break;
-            default: launch_gemv_g<8, true>(a, G, s); break;
-        }
-    } else {
-        switch (mr) {
-            case 1: launch_gemv_g<1, false>(a, G, s); break;
-            case 2: launch_gemv_g<2, false>(a, G, s); break;
-            case 4: launch_gemv_g<4, false>(a, G, s); break;
-            default: launch_gemv_g<8, false>(a, G, s); break;
-        }
+    switch (mr) {
+        case 1: launch_gemv_mr<1>(a, G, gated, s); break;
+        case 2: launch_gemv_mr<2>(a, G, gated, s); break;
+        case 4: launch_gemv_mr<4>(a, G, gated, s); break;
+        default: launch_gemv_mr<8>(a, G, gated, s); break;
     }
 }
 
