@@ -76,46 +76,40 @@ __global__ void repack_upconv_kernel(const uint16_t* __restrict__ w, const uint1
 
 // pcm[t] = tanh(b + sum_k d_k[t + k - (K - 1) / 2]) with d_k[r] = sum_c w[c][k] silu(x[r][c]) over
 // channels-last fp32 x (rows outside [0, frames) read as zero, the convolution's padding; silu(0) =
-// 0). A block stages silu of its rows (its samples plus the kernel's reach) with coalesced loads
-// into a padded tile, gives each row one thread that forms all K tap sums, then one thread per
-// sample adds K of them.
+// 0). A block gives each of its rows (its samples plus the kernel's reach) one thread that reads the
+// row once (through L1) and forms all K tap sums, then one thread per sample adds K of them.
+// (Staging the rows in shared memory with coalesced loads first measured slower: 106 vs 67 us.)
 constexpr int kOutTile = 256;
 constexpr int kOutMaxK = 7;
 __global__ void __launch_bounds__(256) conv_out_tanh_kernel(const float* __restrict__ x_pad, int frames, int C, int K,
                                                             const uint16_t* __restrict__ w, const uint16_t* __restrict__ b,
                                                             float* __restrict__ pcm) {
     extern __shared__ float sm[];
-    const int rows = kOutTile + K - 1, ldx = C + 1;
     float* ws = sm;                               // [C][K]
-    float* d = ws + (size_t)C * K;                // [rows][kOutMaxK]
-    float* xs = d + (size_t)rows * kOutMaxK;      // [rows][C + 1]
+    float* d = sm + (size_t)C * K;                // [kOutTile + K - 1][kOutMaxK]
     pdl_wait();
     const int t0 = blockIdx.x * kOutTile, half = (K - 1) / 2;
+    const int rows = kOutTile + K - 1;
     for (int i = threadIdx.x; i < K * C; i += blockDim.x) ws[i] = bf16f(w[i]);  // [1][C][K] as [c][k]
-    const int per = C / 4;
-    for (int i = threadIdx.x; i < rows * per; i += blockDim.x) {
-        const int rr = i / per, c4 = i - rr * per;
-        const int t = t0 + rr - half;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t >= 0 && t < frames) v = __ldg(reinterpret_cast<const float4*>(x_pad + (size_t)(t + kHalo) * C) + c4);
-        float* xr = xs + (size_t)rr * ldx + 4 * c4;
-        xr[0] = silu(v.x);
-        xr[1] = silu(v.y);
-        xr[2] = silu(v.z);
-        xr[3] = silu(v.w);
-    }
     __syncthreads();
     for (int rr = threadIdx.x; rr < rows; rr += blockDim.x) {
+        const int t = t0 + rr - half;  // time index of the row
         float acc[kOutMaxK];
 #pragma unroll
         for (int k = 0; k < kOutMaxK; k++) acc[k] = 0.f;
-        const float* xr = xs + (size_t)rr * ldx;
-        for (int c = 0; c < C; c++) {
-            const float v = xr[c];
-            const float* wr = ws + (size_t)c * K;
+        if (t >= 0 && t < frames) {
+            const float4* xr = reinterpret_cast<const float4*>(x_pad + (size_t)(t + kHalo) * C);
+            for (int c4 = 0; c4 < C / 4; c4++) {
+                const float4 v = __ldg(xr + c4);
+                const float sv[4] = {silu(v.x), silu(v.y), silu(v.z), silu(v.w)};
 #pragma unroll
-            for (int k = 0; k < kOutMaxK; k++)
-                if (k < K) acc[k] = fmaf(wr[k], v, acc[k]);
+                for (int u = 0; u < 4; u++) {
+                    const float* wr = ws + (size_t)(4 * c4 + u) * K;
+#pragma unroll
+                    for (int k = 0; k < kOutMaxK; k++)
+                        if (k < K) acc[k] = fmaf(wr[k], sv[u], acc[k]);
+                }
+            }
         }
 #pragma unroll
         for (int k = 0; k < kOutMaxK; k++) d[(size_t)rr * kOutMaxK + k] = acc[k];
@@ -278,8 +272,7 @@ mt_status build_plans(mt_convdec* d, int frames) {
 }
 
 size_t out_smem(const mt_convdec_config& c) {
-    const size_t rows = (size_t)kOutTile + c.kernel - 1;
-    return ((size_t)c.channels[4] * c.kernel + rows * kOutMaxK + rows * (c.channels[4] + 1)) * sizeof(float);
+    return ((size_t)c.channels[4] * c.kernel + (size_t)(kOutTile + c.kernel - 1) * kOutMaxK) * sizeof(float);
 }
 
 }  // namespace
