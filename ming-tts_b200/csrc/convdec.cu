@@ -262,9 +262,13 @@ mt_status build_plans(mt_convdec* d, int frames) {
         b.flags |= MT_LINEAR_ACCUM;
         b.y = dst.f + (size_t)H * co;
         b.ldy = G * co;
-        b.y_hi = dst.hi + (size_t)H * co;
-        b.y_lo = dst.lo + (size_t)H * co;
-        b.ld_ysplit = G * co;
+        if (i < 3) {  // the next stage's transposed convolution reads silu(x); the head reads x itself
+            b.y_hi = dst.hi + (size_t)H * co;
+            b.y_lo = dst.lo + (size_t)H * co;
+            b.ld_ysplit = G * co;
+        } else {
+            b.split_silu = 0;
+        }
         CD_TRY(make_gemm_plan(d->ctx, b, &d->b_plan[i]));
     }
     d->plan_frames = frames;
