@@ -211,17 +211,35 @@ mt_status dit_alloc(mt_engine* e, DitBufs* d, const mt_dit_config& c, size_t row
 }
 
 // A linear over m rows of x: CUDA-core GEMV (fp32 x.f) for m <= 8, else a tcgen05 plan (x.hi/lo).
+// Route of a linear over m <= kGemvMax rows, measured with isolated launches whose weights stream
+// from DRAM: the CUDA-core GEMV's time grows with the rows (it is instruction-bound past a few rows:
+// W[9728x896] 9.0 / 14.0 / 19.5 / 24.7 us at 2 / 4 / 6 / 8 rows), the tensor-core GEMM costs about
+// 6-7 us flat while K <= 1024 (16-19 us at K >= 4096 without split-K). n_eff counts both matrices
+// of a gated linear.
+bool small_rows_tc(int m, long long n_eff, int k) {
+    if (m > kGemvMax) return true;
+    if (k > 2048) return false;
+    const long long nk = n_eff * k;
+    if (nk >= 8000000) return m >= 2;
+    if (nk >= 3000000) return m >= 4;
+    if (nk >= 1000000) return m >= 6;
+    return false;
+}
+
 // `y` receives fp32 output; `ys` (optional) receives the activation for a following linear in the
-// representation that linear's route reads.
+// representation that linear's route reads (ys_tc: bf16 hi/lo planes, else fp32).
+// route: 1 tensor cores, 0 CUDA-core GEMV, -1 by the row count alone (tensor cores above kGemvMax).
 // Tensor-core linears split K automatically to fill the SMs; a nonlinear epilogue then reduces
 // through the stream's fp32 workspace (ws, ws_floats) when it is large enough.
 mt_status make_lin(mt_engine* e, Lin* L, const Act& x, int m, const mt_bf16* w, const mt_bf16* w2,
                    const mt_bf16* bias, int n, int k, float* y, int ldy, const Act* ys, uint32_t flags,
-                   float* ws = nullptr, size_t ws_floats = 0) {
+                   float* ws = nullptr, size_t ws_floats = 0, int route = -1, int ys_tc = -1) {
     LinearArgs a{};
     a.m = m; a.n = n; a.k = k; a.w = w; a.w2 = w2; a.bias = bias; a.flags = flags | (bias ? MT_LINEAR_BIAS : 0);
     a.split_k = 1;
-    L->tc = m > kGemvMax;
+    L->tc = route >= 0 ? route == 1 : m > kGemvMax;
+    const bool planes_out = ys && (ys_tc >= 0 ? ys_tc == 1 : m > kGemvMax);
+    MT_REQUIRE(e->ctx, L->tc || !planes_out, MT_ERR_SHAPE, "engine: a CUDA-core linear cannot feed a tensor-core one");
     if (!L->tc) {
         a.x = x.f; a.ldx = x.ld;
         a.y = ys ? ys->f : y;
@@ -230,8 +248,10 @@ mt_status make_lin(mt_engine* e, Lin* L, const Act& x, int m, const mt_bf16* w, 
         return MT_OK;
     }
     a.x_hi = x.hi; a.x_lo = x.lo; a.ld_split = x.ld;
-    if (ys) {
+    if (planes_out) {
         a.y_hi = ys->hi; a.y_lo = ys->lo; a.ld_ysplit = ys->ld;
+    } else if (ys) {
+        a.y = ys->f; a.ldy = ys->ld;
     } else {
         a.y = y; a.ldy = ldy;
     }
@@ -246,17 +266,30 @@ inline void run(const Lin& L, cudaStream_t s) {
     else launch_gemv(L.g, s);
 }
 
-// RMSNorm of `rows` rows into the representation the consumer route (rows_consumer) reads; fp32
-// also when keep_f32.
-void norm(const float* x, int ldx, int rows, int width, const mt_bf16* w, float eps, const Act& out, int rows_consumer,
-          bool keep_f32, cudaStream_t s) {
+// RMSNorm of `rows` rows into the representation the consumer route reads (consumer_tc: bf16
+// hi/lo planes, else fp32); fp32 also when keep_f32.
+void norm_to(const float* x, int ldx, int rows, int width, const mt_bf16* w, float eps, const Act& out,
+             bool consumer_tc, bool keep_f32, cudaStream_t s) {
     RmsArgs a{};
     a.x = x; a.ldx = ldx; a.rows = rows; a.width = width; a.w = w; a.eps = eps;
-    const bool tc = rows_consumer > kGemvMax;
-    if (!tc || keep_f32) { a.y = out.f; a.ldy = out.ld; }
-    if (tc) { a.y_hi = out.hi; a.y_lo = out.lo; a.ld_split = out.ld; }
+    if (!consumer_tc || keep_f32) { a.y = out.f; a.ldy = out.ld; }
+    if (consumer_tc) { a.y_hi = out.hi; a.y_lo = out.lo; a.ld_split = out.ld; }
     launch_rmsnorm(a, s);
     g_kernels++;
+}
+
+// The same for a consumer routed by its row count alone.
+void norm(const float* x, int ldx, int rows, int width, const mt_bf16* w, float eps, const Act& out, int rows_consumer,
+          bool keep_f32, cudaStream_t s) {
+    norm_to(x, ldx, rows, width, w, eps, out, rows_consumer > kGemvMax, keep_f32, s);
+}
+
+// The norm before a linear: folded into a CUDA-core linear (nothing to launch), else in the
+// representation its route reads.
+void norm_for(const Lin& L, const float* x, int ld, int rows, const mt_bf16* g, float eps, const Act& out,
+              cudaStream_t s) {
+    if (!L.tc && L.g.norm_w) return;
+    norm_to(x, ld, rows, ld, g, eps, out, L.tc, false, s);
 }
 
 // Rows up to which a CUDA-core linear folds the RMSNorm before it: measured on the config-2 decode
@@ -280,15 +313,20 @@ mt_status plan_qwen(mt_engine* e, std::vector<QwenLayerPlans>& plans, const mt_q
     const mt_qwen_config& c = W.cfg;
     const int qkvw = (c.heads + 2 * c.kv_heads) * 64;
     plans.resize(c.layers);
+    const int A = c.heads * 64;
+    const int r_qkv = small_rows_tc(rows, qkvw, c.hidden), r_o = small_rows_tc(rows, c.hidden, A);
+    const int r_gu = small_rows_tc(rows, 2LL * c.intermediate, c.hidden);
+    const int r_down = small_rows_tc(rows, c.hidden, c.intermediate);
     for (int l = 0; l < c.layers; l++) {
         const mt_qwen_layer& L = W.layers[l];
-        TRY(make_lin(e, &plans[l].qkv, b.norm, rows, L.qkv_w, nullptr, L.qkv_b, qkvw, c.hidden, b.qkv, qkvw, nullptr, 0));
-        TRY(make_lin(e, &plans[l].o, b.attn, rows, L.o_w, nullptr, nullptr, c.hidden, c.heads * 64, b.x, c.hidden,
-                     nullptr, MT_LINEAR_ACCUM));
+        TRY(make_lin(e, &plans[l].qkv, b.norm, rows, L.qkv_w, nullptr, L.qkv_b, qkvw, c.hidden, b.qkv, qkvw, nullptr, 0,
+                     nullptr, 0, r_qkv));
+        TRY(make_lin(e, &plans[l].o, b.attn, rows, L.o_w, nullptr, nullptr, c.hidden, A, b.x, c.hidden,
+                     nullptr, MT_LINEAR_ACCUM, nullptr, 0, r_o));
         TRY(make_lin(e, &plans[l].gu, b.norm, rows, L.gate_w, L.up_w, nullptr, c.intermediate, c.hidden, nullptr, 0,
-                     &b.mlp, MT_LINEAR_SILU_GATE, ws, ws_floats));
+                     &b.mlp, MT_LINEAR_SILU_GATE, ws, ws_floats, r_gu, r_down));
         TRY(make_lin(e, &plans[l].down, b.mlp, rows, L.down_w, nullptr, nullptr, c.hidden, c.intermediate, b.x,
-                     c.hidden, nullptr, MT_LINEAR_ACCUM));
+                     c.hidden, nullptr, MT_LINEAR_ACCUM, nullptr, 0, r_down));
         fold_norm(&plans[l].qkv, b.x, c.hidden, L.norm1, c.eps);
         fold_norm(&plans[l].gu, b.x, c.hidden, L.norm2, c.eps);
     }
@@ -299,16 +337,18 @@ mt_status plan_dit(mt_engine* e, std::vector<DitBlockPlans>& plans, const mt_dit
                    float* ws, size_t ws_floats) {
     const mt_dit_config& c = W.cfg;
     plans.resize(c.depth);
+    const int r_qkv = small_rows_tc(rows, 3LL * c.hidden, c.hidden), r_out = small_rows_tc(rows, c.hidden, c.hidden);
+    const int r_ff1 = small_rows_tc(rows, c.ff, c.hidden), r_ff2 = small_rows_tc(rows, c.hidden, c.ff);
     for (int i = 0; i < c.depth; i++) {
         const mt_dit_block& B = W.blocks[i];
         TRY(make_lin(e, &plans[i].qkv, b.norm, rows, B.qkv_w, nullptr, B.qkv_b, 3 * c.hidden, c.hidden, b.qkv,
-                     3 * c.hidden, nullptr, 0));
+                     3 * c.hidden, nullptr, 0, nullptr, 0, r_qkv));
         TRY(make_lin(e, &plans[i].out, b.attn, rows, B.out_w, nullptr, B.out_b, c.hidden, c.hidden, b.x, c.hidden,
-                     nullptr, MT_LINEAR_ACCUM));
+                     nullptr, MT_LINEAR_ACCUM, nullptr, 0, r_out));
         TRY(make_lin(e, &plans[i].ff1, b.norm, rows, B.ff1_w, nullptr, B.ff1_b, c.ff, c.hidden, nullptr, 0, &b.ff,
-                     MT_LINEAR_GELU, ws, ws_floats));
+                     MT_LINEAR_GELU, ws, ws_floats, r_ff1, r_ff2));
         TRY(make_lin(e, &plans[i].ff2, b.ff, rows, B.ff2_w, nullptr, B.ff2_b, c.hidden, c.ff, b.x, c.hidden, nullptr,
-                     MT_LINEAR_ACCUM));
+                     MT_LINEAR_ACCUM, nullptr, 0, r_ff2));
         fold_norm(&plans[i].qkv, b.x, c.hidden, B.norm1, c.eps);
         fold_norm(&plans[i].ff1, b.x, c.hidden, B.norm2, c.eps);
     }
@@ -483,12 +523,12 @@ void qwen_forward(mt_engine* e, const mt_qwen_weights& W, QwenBufs& b, std::vect
     const int qkvw = (c.heads + 2 * c.kv_heads) * 64;
     const size_t tensor = (size_t)c.kv_heads * b.cap * 64;
     const long long req_stride = (long long)c.layers * 2 * tensor;
-    const bool tc = rows > kGemvMax;
     for (int l = 0; l < c.layers; l++) {
         const mt_qwen_layer& L = W.layers[l];
         float* kc = b.kv + (size_t)(2 * l) * tensor;
         float* vc = kc + tensor;
-        if (!folds_norm(rows) || tc) norm(b.x, c.hidden, rows, c.hidden, L.norm1, c.eps, b.norm, rows, false, s);
+        const bool tc = plans[l].o.tc;  // the attention rows' consumer
+        norm_for(plans[l].qkv, b.x, c.hidden, rows, L.norm1, c.eps, b.norm, s);
         run(plans[l].qkv, s);
         if (attention_decode_supported(rows_per_req, c.heads, c.kv_heads)) {
             // Decode: every row of a request in one block, RoPE and the KV append fused in.
@@ -501,7 +541,7 @@ void qwen_forward(mt_engine* e, const mt_qwen_weights& W, QwenBufs& b, std::vect
             da.max_keys = max_keys; da.status = e->ctx->d_status;
             launch_attention_decode(da, s); g_kernels++;
             run(plans[l].o, s);
-            if (!folds_norm(rows) || tc) norm(b.x, c.hidden, rows, c.hidden, L.norm2, c.eps, b.norm, rows, false, s);
+            norm_for(plans[l].gu, b.x, c.hidden, rows, L.norm2, c.eps, b.norm, s);
             run(plans[l].gu, s);
             run(plans[l].down, s);
             continue;
@@ -519,7 +559,7 @@ void qwen_forward(mt_engine* e, const mt_qwen_weights& W, QwenBufs& b, std::vect
         else { aa.out = b.attn.f; aa.ldo = b.attn.ld; }
         launch_attention(aa, s); g_kernels++;
         run(plans[l].o, s);
-        if (!folds_norm(rows) || tc) norm(b.x, c.hidden, rows, c.hidden, L.norm2, c.eps, b.norm, rows, false, s);
+        norm_for(plans[l].gu, b.x, c.hidden, rows, L.norm2, c.eps, b.norm, s);
         run(plans[l].gu, s);
         run(plans[l].down, s);
     }
@@ -531,10 +571,10 @@ void dit_blocks(mt_engine* e, const mt_dit_weights& W, DitBufs& b, std::vector<D
                 int seq, cudaStream_t s) {
     const mt_dit_config& c = W.cfg;
     const int rows = batch * seq;
-    const bool tc = rows > kGemvMax;
     for (int i = 0; i < c.depth; i++) {
         const mt_dit_block& B = W.blocks[i];
-        if (!folds_norm(rows) || tc) norm(b.x, c.hidden, rows, c.hidden, B.norm1, c.eps, b.norm, rows, false, s);
+        const bool tc = plans[i].out.tc;  // the attention rows' consumer
+        norm_for(plans[i].qkv, b.x, c.hidden, rows, B.norm1, c.eps, b.norm, s);
         run(plans[i].qkv, s);
         DitAttnArgs da{};
         da.qkv = b.qkv; da.ld = 3 * c.hidden; da.batch = batch; da.seq = seq; da.heads = c.heads;
@@ -543,7 +583,7 @@ void dit_blocks(mt_engine* e, const mt_dit_weights& W, DitBufs& b, std::vector<D
         else { da.out = b.attn.f; da.ldo = b.attn.ld; }
         launch_dit_attention(da, s); g_kernels++;
         run(plans[i].out, s);
-        if (!folds_norm(rows) || tc) norm(b.x, c.hidden, rows, c.hidden, B.norm2, c.eps, b.norm, rows, false, s);
+        norm_for(plans[i].ff1, b.x, c.hidden, rows, B.norm2, c.eps, b.norm, s);
         run(plans[i].ff1, s);
         run(plans[i].ff2, s);
     }
