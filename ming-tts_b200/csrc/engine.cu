@@ -216,8 +216,11 @@ mt_status dit_alloc(mt_engine* e, DitBufs* d, const mt_dit_config& c, size_t row
 // W[9728x896] 9.0 / 14.0 / 19.5 / 24.7 us at 2 / 4 / 6 / 8 rows), the tensor-core GEMM costs about
 // 6-7 us flat while K <= 1024 (16-19 us at K >= 4096 without split-K). n_eff counts both matrices
 // of a gated linear.
-bool small_rows_tc(int m, long long n_eff, int k) {
+// An accumulating linear (the residual projections) splits K on the tensor-core route and wins from
+// 2 rows (W[1024x4096] 4.9 / 7.2 / 12.1 us on the GEMV at 2 / 4 / 8 rows against 4.5-4.9 us).
+bool small_rows_tc(int m, long long n_eff, int k, bool accum = false) {
     if (m > kGemvMax) return true;
+    if (accum) return m >= 2;
     if (k > 2048) return false;
     const long long nk = n_eff * k;
     if (nk >= 8000000) return m >= 2;
@@ -227,7 +230,8 @@ bool small_rows_tc(int m, long long n_eff, int k) {
 }
 
 // `y` receives fp32 output; `ys` (optional) receives the activation for a following linear in the
-// representation that linear's route reads (ys_tc: bf16 hi/lo planes, else fp32).
+// representation that linear's route reads (ys_tc: bf16 hi/lo planes, else fp32; either route can
+// write either).
 // route: 1 tensor cores, 0 CUDA-core GEMV, -1 by the row count alone (tensor cores above kGemvMax).
 // Tensor-core linears split K automatically to fill the SMs; a nonlinear epilogue then reduces
 // through the stream's fp32 workspace (ws, ws_floats) when it is large enough.
@@ -239,11 +243,14 @@ mt_status make_lin(mt_engine* e, Lin* L, const Act& x, int m, const mt_bf16* w, 
     a.split_k = 1;
     L->tc = route >= 0 ? route == 1 : m > kGemvMax;
     const bool planes_out = ys && (ys_tc >= 0 ? ys_tc == 1 : m > kGemvMax);
-    MT_REQUIRE(e->ctx, L->tc || !planes_out, MT_ERR_SHAPE, "engine: a CUDA-core linear cannot feed a tensor-core one");
     if (!L->tc) {
         a.x = x.f; a.ldx = x.ld;
-        a.y = ys ? ys->f : y;
-        a.ldy = ys ? ys->ld : ldy;
+        if (planes_out) {  // the GEMV epilogue writes the planes a tensor-core consumer reads
+            a.y_hi = ys->hi; a.y_lo = ys->lo; a.ld_ysplit = ys->ld;
+        } else {
+            a.y = ys ? ys->f : y;
+            a.ldy = ys ? ys->ld : ldy;
+        }
         L->g = a;
         return MT_OK;
     }
@@ -314,9 +321,9 @@ mt_status plan_qwen(mt_engine* e, std::vector<QwenLayerPlans>& plans, const mt_q
     const int qkvw = (c.heads + 2 * c.kv_heads) * 64;
     plans.resize(c.layers);
     const int A = c.heads * 64;
-    const int r_qkv = small_rows_tc(rows, qkvw, c.hidden), r_o = small_rows_tc(rows, c.hidden, A);
+    const int r_qkv = small_rows_tc(rows, qkvw, c.hidden), r_o = small_rows_tc(rows, c.hidden, A, true);
     const int r_gu = small_rows_tc(rows, 2LL * c.intermediate, c.hidden);
-    const int r_down = small_rows_tc(rows, c.hidden, c.intermediate);
+    const int r_down = small_rows_tc(rows, c.hidden, c.intermediate, true);
     for (int l = 0; l < c.layers; l++) {
         const mt_qwen_layer& L = W.layers[l];
         TRY(make_lin(e, &plans[l].qkv, b.norm, rows, L.qkv_w, nullptr, L.qkv_b, qkvw, c.hidden, b.qkv, qkvw, nullptr, 0,
@@ -337,8 +344,9 @@ mt_status plan_dit(mt_engine* e, std::vector<DitBlockPlans>& plans, const mt_dit
                    float* ws, size_t ws_floats) {
     const mt_dit_config& c = W.cfg;
     plans.resize(c.depth);
-    const int r_qkv = small_rows_tc(rows, 3LL * c.hidden, c.hidden), r_out = small_rows_tc(rows, c.hidden, c.hidden);
-    const int r_ff1 = small_rows_tc(rows, c.ff, c.hidden), r_ff2 = small_rows_tc(rows, c.hidden, c.ff);
+    const int r_qkv = small_rows_tc(rows, 3LL * c.hidden, c.hidden);
+    const int r_out = small_rows_tc(rows, c.hidden, c.hidden, true);
+    const int r_ff1 = small_rows_tc(rows, c.ff, c.hidden), r_ff2 = small_rows_tc(rows, c.hidden, c.ff, true);
     for (int i = 0; i < c.depth; i++) {
         const mt_dit_block& B = W.blocks[i];
         TRY(make_lin(e, &plans[i].qkv, b.norm, rows, B.qkv_w, nullptr, B.qkv_b, 3 * c.hidden, c.hidden, b.qkv,

@@ -149,9 +149,17 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(LinearArgs a)
             if (GATED) v = silu(v) * v2;
             if (a.flags & MT_LINEAR_GELU) v = gelu_tanh(v);
             if (a.flags & MT_LINEAR_SILU) v = silu(v);
-            float* yp = a.y + (size_t)(row0 + r) * a.ldy + n;
-            if (a.flags & MT_LINEAR_ACCUM) v += *yp;
-            *yp = v;
+            if (a.y) {
+                float* yp = a.y + (size_t)(row0 + r) * a.ldy + n;
+                if (a.flags & MT_LINEAR_ACCUM) v += *yp;
+                *yp = v;
+            }
+            if (a.y_hi) {  // bf16 hi/lo planes for a tensor-core consumer
+                uint16_t h, l;
+                split_bf16(v, h, l);
+                a.y_hi[(size_t)(row0 + r) * a.ld_ysplit + n] = h;
+                a.y_lo[(size_t)(row0 + r) * a.ld_ysplit + n] = l;
+            }
         }
     }
 }
@@ -248,7 +256,7 @@ __global__ void __launch_bounds__(256) gemv_narrow_kernel(LinearArgs a) {
 }
 
 void launch_gemv(const LinearArgs& a, cudaStream_t s) {
-    if (a.n <= NARROW_MAX_N && a.k % 128 == 0 && !(a.flags & MT_LINEAR_SILU_GATE) && a.ldx % 4 == 0 && !a.norm_w) {
+    if (a.n <= NARROW_MAX_N && a.k % 128 == 0 && !(a.flags & MT_LINEAR_SILU_GATE) && a.ldx % 4 == 0 && !a.norm_w && !a.y_hi) {
         launch_k(gemv_narrow_kernel, (a.m + 7) / 8, 256, 0, s, a);
         return;
     }
