@@ -7,6 +7,9 @@
 #include "common.cuh"
 #include "kernels.cuh"
 
+#include <cooperative_groups.h>
+namespace cg = cooperative_groups;
+
 namespace mt {
 
 // ------------------------------------------------------------------------------------------------
@@ -275,6 +278,11 @@ void launch_attention(const AttnArgs& a, cudaStream_t s) {
 // waits, new keys come from the block's own rotation. Scores use a skewed float4 walk over the
 // 64 dims so the 32 keys a warp touches fall in distinct bank groups; softmax is online across
 // chunks; thread groups of P own (row-head, 4 dims) accumulators for P.V.
+// With few (request, kv head) units the key range is split over gridDim.z blocks that form one
+// thread-block cluster: each split keeps its own online-softmax state, and cluster rank 0 merges
+// the partials through distributed shared memory between two cluster barriers (the flash-decoding
+// split: O = sum_z e^(m_z - M) O_z / sum_z e^(m_z - M) l_z, M = max_z m_z). Only split 0 appends
+// the new keys and values to the cache; every split stashes them for its own chunks.
 // ------------------------------------------------------------------------------------------------
 constexpr int AD_THREADS = 256;
 constexpr int AD_MAX_RG = ATTN_DECODE_MAX_ROWS * 8;  // rows x query heads per kv head
@@ -288,8 +296,9 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
     __shared__ __align__(8) uint64_t bar[2];
     __shared__ float m_run[AD_MAX_RG], l_run[AD_MAX_RG], alpha[AD_MAX_RG];
     __shared__ float rot_c[ATTN_DECODE_MAX_ROWS][32], rot_s[ATTN_DECODE_MAX_ROWS][32];
-    __shared__ int abort_flag;
+    __shared__ int abort_flag, split_ok;
     const int r = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = gridDim.z, z = blockIdx.z;  // key splits of this unit; this block's split
     const int G = a.hq / a.hkv, nrows = a.rows_per_req, nrg = nrows * G;
     float* Ks = sm;
     float* Vs = Ks + (size_t)SC * 64;
@@ -305,8 +314,13 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
     const int p_first = base, p_end = base + nrows;  // new keys [p_first, p_end)
     const int W = a.window;
     const int jS = W > 0 ? max(0, p_first + 1 - W) : 0;
-    const int nk = p_end - jS;
-    const int chunks = (nk + SC - 1) / SC;
+    int s0 = jS, s1 = p_end;  // this split's keys [s0, s1)
+    if (S > 1) {
+        const int per = ((p_end - jS + S - 1) / S + 15) & ~15;
+        s0 = min(p_end, jS + z * per);
+        s1 = min(p_end, s0 + per);
+    }
+    const int chunks = (s1 - s0 + SC - 1) / SC;
     float* kc = a.kc + (size_t)r * a.req_stride + (size_t)h * a.cap * 64;
     float* vc = a.vc + (size_t)r * a.req_stride + (size_t)h * a.cap * 64;
     // Old keys of chunk c: [c0, min(c1, p_first)). Thread 0 arms both barriers for the chunk's
@@ -314,7 +328,7 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
     // thread's bulk copies stream one after another at a few bytes per clock from DRAM, so the
     // slices of eight warps keep eight times as many bytes in flight.
     auto old_keys = [&](int c) {
-        const int c0 = jS + c * SC, c1 = min(c0 + SC, p_end);
+        const int c0 = s0 + c * SC, c1 = min(c0 + SC, s1);
         return max(0, min(c1, p_first) - c0);
     };
     auto arm = [&](int c) {
@@ -327,10 +341,10 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
         const int per = (nold + AD_THREADS / 32 - 1) / (AD_THREADS / 32);
         const int k0 = warp * per, k1 = min(nold, k0 + per);
         if (k0 >= k1) return;
-        const int s0 = (jS + c * SC + k0) % a.cap;  // ring slot of this slice's first key
-        const int len1 = min(k1 - k0, a.cap - s0);
-        bulk_load(Ks + (size_t)k0 * 64, kc + (size_t)s0 * 64, (uint32_t)len1 * 256u, &bar[0]);
-        bulk_load(Vs + (size_t)k0 * 64, vc + (size_t)s0 * 64, (uint32_t)len1 * 256u, &bar[1]);
+        const int slot = (s0 + c * SC + k0) % a.cap;  // ring slot of this slice's first key
+        const int len1 = min(k1 - k0, a.cap - slot);
+        bulk_load(Ks + (size_t)k0 * 64, kc + (size_t)slot * 64, (uint32_t)len1 * 256u, &bar[0]);
+        bulk_load(Vs + (size_t)k0 * 64, vc + (size_t)slot * 64, (uint32_t)len1 * 256u, &bar[1]);
         if (k0 + len1 < k1) {  // the slice wraps around the ring
             const uint32_t rest = (uint32_t)(k1 - k0 - len1) * 256u;
             bulk_load(Ks + (size_t)(k0 + len1) * 64, kc, rest, &bar[0]);
@@ -392,9 +406,11 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
                 qs[(i * G + slot) * 64 + l] = v0;
                 qs[(i * G + slot) * 64 + l + 32] = v1;
             } else {
-                float* dst = (slot == G ? kc : vc) + (size_t)((base + i) % a.cap) * 64;
-                dst[l] = v0;
-                dst[l + 32] = v1;
+                if (z == 0) {
+                    float* dst = (slot == G ? kc : vc) + (size_t)((base + i) % a.cap) * 64;
+                    dst[l] = v0;
+                    dst[l + 32] = v1;
+                }
                 float* st = nw + (i * 2 + (slot - G)) * 64;
                 st[l] = v0;
                 st[l + 32] = v1;
@@ -414,7 +430,7 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
 
     bool ok = true;
     for (int c = 0; c < chunks && ok; c++) {
-        const int c0 = jS + c * SC, c1 = min(c0 + SC, p_end), cn = c1 - c0;
+        const int c0 = s0 + c * SC, c1 = min(c0 + SC, s1), cn = c1 - c0;
         const int old_end = min(c1, p_first);
         const int nold = max(0, old_end - c0);
         __syncthreads();  // the previous chunk's readers are done with Ks, Vs and sc
@@ -518,25 +534,18 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
             }
         }
     }
-    if (!ok) return;
-    // Reduce the PP partial sums through shared memory (the K/V chunk area is free now), then
-    // normalise and write: output task = (row i, head g, d4).
+    // Reduce the PP partial sums through shared memory (the K/V chunk area is free now); output
+    // task t = (row-head rg, 4 dims dd).
     __syncthreads();
     float4* part4 = reinterpret_cast<float4*>(Ks);  // [PP][nrows][G][16]
-    if (pv_live) {
+    if (ok && pv_live) {
 #pragma unroll
         for (int g = 0; g < 8; g++)
             if (g < G) part4[((pv_part * nrows + pv_i) * G + g) * 16 + d4] = acc[g];
     }
     __syncthreads();
-    for (int t = tid; t < nrg * 16; t += AD_THREADS) {
+    auto write_out = [&](int t, float4 o, float inv) {
         const int dd = t & 15, rg = t >> 4, i = rg / G, g = rg % G;
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int q = 0; q < PP; q++) {
-            const float4 v = part4[((q * nrows + i) * G + g) * 16 + dd];
-            o.x += v.x; o.y += v.y; o.z += v.z; o.w += v.w;
-        }
-        const float inv = 1.0f / l_run[rg];
         const float o0 = o.x * inv, o1 = o.y * inv, o2 = o.z * inv, o3 = o.w * inv;
         const size_t row = (size_t)(r * nrows + i);
         const int head = h * G + g;
@@ -549,7 +558,52 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
             *reinterpret_cast<uint2*>(a.out_hi + so) = make_uint2(h01, h23);
             *reinterpret_cast<uint2*>(a.out_lo + so) = make_uint2(l01, l23);
         }
+    };
+    auto part_sum = [&](int t) {
+        const int dd = t & 15, rg = t >> 4, i = rg / G, g = rg % G;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < PP; q++) {
+            const float4 v = part4[((q * nrows + i) * G + g) * 16 + dd];
+            o.x += v.x; o.y += v.y; o.z += v.z; o.w += v.w;
+        }
+        return o;
+    };
+    if (S == 1) {
+        if (!ok) return;
+        for (int t = tid; t < nrg * 16; t += AD_THREADS) write_out(t, part_sum(t), 1.0f / l_run[t >> 4]);
+        return;
     }
+    // Split: this block's unnormalised sums go to the q area ([nrg][16] float4, free after the
+    // key loop); every block of the cluster passes both barriers, failed or not.
+    float4* fin4 = reinterpret_cast<float4*>(qs);
+    if (ok)
+        for (int t = tid; t < nrg * 16; t += AD_THREADS) fin4[t] = part_sum(t);
+    if (tid == 0) split_ok = ok ? 1 : 0;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (cluster.block_rank() == 0) {
+        bool all_ok = true;
+        for (int q = 0; q < S; q++) all_ok = all_ok && *cluster.map_shared_rank(&split_ok, q) != 0;
+        if (all_ok) {
+            for (int t = tid; t < nrg * 16; t += AD_THREADS) {
+                const int rg = t >> 4;
+                float M = -INFINITY;
+                for (int q = 0; q < S; q++) M = fmaxf(M, cluster.map_shared_rank(m_run, q)[rg]);
+                float L = 0.f;
+                float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int q = 0; q < S; q++) {
+                    const float mq = cluster.map_shared_rank(m_run, q)[rg];
+                    if (mq == -INFINITY) continue;  // a split that holds no key of this row
+                    const float wq = expf(mq - M);
+                    L += cluster.map_shared_rank(l_run, q)[rg] * wq;
+                    const float4 v = cluster.map_shared_rank(fin4, q)[t];
+                    o.x += v.x * wq; o.y += v.y * wq; o.z += v.z * wq; o.w += v.w * wq;
+                }
+                write_out(t, o, 1.0f / L);
+            }
+        }
+    }
+    cluster.sync();  // no block leaves while rank 0 reads its shared memory
 }
 
 bool attention_decode_supported(int rows_per_req, int hq, int hkv) {
@@ -560,13 +614,33 @@ void launch_attention_decode(const AttnDecodeArgs& a, cudaStream_t s) {
     const int G = a.hq / a.hkv, nrg = a.rows_per_req * G;
     const int nk_max = a.window > 0 ? min(a.window + a.rows_per_req - 1, a.cap) : a.max_keys;
     constexpr size_t kBudget = 223 * 1024;  // dynamic shared memory: 227 KB per block less the static part
-    int SC = (nk_max + 15) & ~15;
+    // Key splits: with fewer units than a quarter of the SMs, up to 8 splits of at least 32 keys,
+    // as one cluster per unit.
+    const int units = a.requests * a.hkv;
+    int S = 1;
+    if (units * 4 <= 148) S = max(1, min(min(8, 148 / units), (nk_max + 31) / 32));
+    const int per_max = ((nk_max + S - 1) / S + 15) & ~15;
+    int SC = per_max;
     if (a.chunk_keys > 0 && a.chunk_keys < SC) SC = (a.chunk_keys + 15) & ~15;
     if (SC < 8 * G) SC = 8 * G;  // the final reduction reuses the K/V area: 16 x G x 256 bytes
     while (SC > 16 && ad_dyn_bytes(SC, a.rows_per_req, nrg) > kBudget) SC -= 16;
     static PerDeviceOnce once;  // per device, on the first (eager) call, before any graph capture
     once([] { cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBudget); });
-    launch_k(attention_decode_kernel, dim3(a.requests, a.hkv), AD_THREADS, ad_dyn_bytes(SC, a.rows_per_req, nrg), s, a, SC);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.requests, a.hkv, S);
+    cfg.blockDim = dim3(AD_THREADS);
+    cfg.dynamicSmemBytes = ad_dyn_bytes(SC, a.rows_per_req, nrg);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = S;
+    cfg.attrs = attr;
+    cfg.numAttrs = S > 1 ? 2 : 1;
+    cudaLaunchKernelEx(&cfg, attention_decode_kernel, a, SC);
 }
 
 // ------------------------------------------------------------------------------------------------
