@@ -286,6 +286,7 @@ void launch_attention(const AttnArgs& a, cudaStream_t s) {
 // ------------------------------------------------------------------------------------------------
 constexpr int AD_THREADS = 256;
 constexpr int AD_MAX_RG = ATTN_DECODE_MAX_ROWS * 8;  // rows x query heads per kv head
+constexpr int AD_MAX_SPLITS = 8;                     // key splits per unit: one portable cluster
 
 static size_t ad_dyn_bytes(int SC, int nrows, int nrg) {
     return sizeof(float) * ((size_t)SC * 64 * 2 + (size_t)nrg * 64 + (size_t)nrows * 128 + (size_t)nrg * SC);
@@ -448,45 +449,36 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
             issue(c);
         }
         if (!mbar_wait(&bar[0], c & 1, a.status, 20, abort)) { ok = false; break; }
-        // Scores: item (key pair p, row i) scores keys k0 and k0 + 8 (same 16-byte skew s = p & 7,
-        // so the eight lanes of a shared-memory phase read eight distinct bank groups of K and one
-        // q chunk serves both keys) against the G heads of row i.
+        // Scores: item (key pair p, row-head rg) scores keys k0 and k0 + 8 (same 16-byte skew
+        // s = p & 7, so the eight lanes of a shared-memory phase read eight distinct bank groups of
+        // K and one q chunk serves both keys). One head per item keeps every warp busy when a
+        // block holds few keys (a split's 32-64): items per head would leave one warp doing all
+        // G heads while the others wait at the barrier.
         const float4* K4 = reinterpret_cast<const float4*>(Ks);
         const float4* Q4 = reinterpret_cast<const float4*>(qs);
         const int npairs = ((cn + 15) / 16) * 8;
-        for (int it = tid; it < npairs * nrows; it += AD_THREADS) {
-            const int pr = it % npairs, i = it / npairs;
+        for (int it = tid; it < npairs * nrg; it += AD_THREADS) {
+            const int pr = it % npairs, rg = it / npairs, i = rg / G;
             const int k0 = (pr >> 3) * 16 + (pr & 7), k1 = k0 + 8;
             const int sk = pr & 7;
             const bool l0 = k0 < cn, l1 = k1 < cn;
-            float s0[8], s1[8];
+            const float4* q = Q4 + rg * 16;
+            float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-            for (int g = 0; g < 8; g++) { s0[g] = 0.f; s1[g] = 0.f; }
-#pragma unroll 4
             for (int t = 0; t < 16; t++) {
                 const int ch = (t + sk) & 15;
+                const float4 q4 = q[ch];
                 const float4 ka = l0 ? K4[k0 * 16 + ch] : make_float4(0.f, 0.f, 0.f, 0.f);
                 const float4 kb = l1 ? K4[k1 * 16 + ch] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int g = 0; g < 8; g++) {
-                    if (g < G) {
-                        const float4 q4 = Q4[(i * G + g) * 16 + ch];
-                        s0[g] += q4.x * ka.x + q4.y * ka.y + q4.z * ka.z + q4.w * ka.w;
-                        s1[g] += q4.x * kb.x + q4.y * kb.y + q4.z * kb.z + q4.w * kb.w;
-                    }
-                }
+                s0 += q4.x * ka.x + q4.y * ka.y + q4.z * ka.z + q4.w * ka.w;
+                s1 += q4.x * kb.x + q4.y * kb.y + q4.z * kb.z + q4.w * kb.w;
             }
             const int pos = base + i;
             const int j0 = c0 + k0, j1 = c0 + k1;
             const bool v0 = j0 <= pos && (W == 0 || j0 > pos - W);
             const bool v1 = j1 <= pos && (W == 0 || j1 > pos - W);
-#pragma unroll
-            for (int g = 0; g < 8; g++) {
-                if (g < G) {
-                    if (l0) sc[(size_t)(i * G + g) * SC + k0] = v0 ? s0[g] * 0.125f : -INFINITY;
-                    if (l1) sc[(size_t)(i * G + g) * SC + k1] = v1 ? s1[g] * 0.125f : -INFINITY;
-                }
-            }
+            if (l0) sc[(size_t)rg * SC + k0] = v0 ? s0 * 0.125f : -INFINITY;
+            if (l1) sc[(size_t)rg * SC + k1] = v1 ? s1 * 0.125f : -INFINITY;
         }
         __syncthreads();
         // Online softmax statistics; scores become weights relative to the running maximum.
@@ -582,22 +574,37 @@ __global__ void __launch_bounds__(AD_THREADS) attention_decode_kernel(AttnDecode
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     if (cluster.block_rank() == 0) {
-        bool all_ok = true;
-        for (int q = 0; q < S; q++) all_ok = all_ok && *cluster.map_shared_rank(&split_ok, q) != 0;
-        if (all_ok) {
+        // Every remote load of a task is issued before any is used (S <= AD_MAX_SPLITS).
+        int n_ok = 0;
+#pragma unroll
+        for (int q = 0; q < AD_MAX_SPLITS; q++)
+            if (q < S) n_ok += *cluster.map_shared_rank(&split_ok, q);
+        if (n_ok == S) {
             for (int t = tid; t < nrg * 16; t += AD_THREADS) {
                 const int rg = t >> 4;
+                float mq[AD_MAX_SPLITS], lq[AD_MAX_SPLITS];
+                float4 vq[AD_MAX_SPLITS];
+#pragma unroll
+                for (int q = 0; q < AD_MAX_SPLITS; q++) {
+                    if (q < S) {
+                        mq[q] = cluster.map_shared_rank(m_run, q)[rg];
+                        lq[q] = cluster.map_shared_rank(l_run, q)[rg];
+                        vq[q] = cluster.map_shared_rank(fin4, q)[t];
+                    }
+                }
                 float M = -INFINITY;
-                for (int q = 0; q < S; q++) M = fmaxf(M, cluster.map_shared_rank(m_run, q)[rg]);
+#pragma unroll
+                for (int q = 0; q < AD_MAX_SPLITS; q++)
+                    if (q < S) M = fmaxf(M, mq[q]);
                 float L = 0.f;
                 float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int q = 0; q < S; q++) {
-                    const float mq = cluster.map_shared_rank(m_run, q)[rg];
-                    if (mq == -INFINITY) continue;  // a split that holds no key of this row
-                    const float wq = expf(mq - M);
-                    L += cluster.map_shared_rank(l_run, q)[rg] * wq;
-                    const float4 v = cluster.map_shared_rank(fin4, q)[t];
-                    o.x += v.x * wq; o.y += v.y * wq; o.z += v.z * wq; o.w += v.w * wq;
+#pragma unroll
+                for (int q = 0; q < AD_MAX_SPLITS; q++) {
+                    if (q < S && mq[q] != -INFINITY) {  // a split that holds no key of this row adds nothing
+                        const float wq = expf(mq[q] - M);
+                        L += lq[q] * wq;
+                        o.x += vq[q].x * wq; o.y += vq[q].y * wq; o.z += vq[q].z * wq; o.w += vq[q].w * wq;
+                    }
                 }
                 write_out(t, o, 1.0f / L);
             }
@@ -618,7 +625,7 @@ void launch_attention_decode(const AttnDecodeArgs& a, cudaStream_t s) {
     // as one cluster per unit.
     const int units = a.requests * a.hkv;
     int S = 1;
-    if (units * 4 <= 148) S = max(1, min(min(8, 148 / units), (nk_max + 31) / 32));
+    if (units * 4 <= 148) S = max(1, min(min(AD_MAX_SPLITS, 148 / units), (nk_max + 31) / 32));
     const int per_max = ((nk_max + S - 1) / S + 15) & ~15;
     int SC = per_max;
     if (a.chunk_keys > 0 && a.chunk_keys < SC) SC = (a.chunk_keys + 15) & ~15;
