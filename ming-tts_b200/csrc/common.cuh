@@ -150,6 +150,14 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Launches `kernel` with the programmatic-stream-serialization attribute (see pdl_wait).
+// Scheduling priority given to the kernels this thread launches (0: none, the stream's own). The
+// engine raises its critical path (LLM token, flow, aggregator) above the concurrent VAE decode;
+// captured launches keep it as a graph-node attribute.
+inline int& launch_priority() {
+    static thread_local int p = 0;
+    return p;
+}
+
 template <typename... KArgs, typename... Args>
 inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                      Args&&... args) {
@@ -158,11 +166,16 @@ inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (launch_priority() != 0) {
+        attr[1].id = cudaLaunchAttributePriority;
+        attr[1].val.priority = launch_priority();
+        cfg.numAttrs = 2;
+    }
     cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
@@ -175,7 +188,7 @@ inline void launch_k_pair(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[3];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     attr[1].id = cudaLaunchAttributeClusterDimension;
@@ -184,6 +197,11 @@ inline void launch_k_pair(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
+    if (launch_priority() != 0) {
+        attr[2].id = cudaLaunchAttributePriority;
+        attr[2].val.priority = launch_priority();
+        cfg.numAttrs = 3;
+    }
     cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 

@@ -101,12 +101,11 @@ void norm(const float* x, int ld, int rows, int width, const uint16_t* g, float 
     launch_rmsnorm(a, s);
 }
 
-// RMSNorm(x) * g, then the linear: folded into the GEMV for up to 6 rows when the gain is 16-byte
-// aligned (it loads as 16-byte vectors; with more rows the fold's per-chunk work makes the GEMV
-// compute-bound), else the norm's own launch into `normed` first.
+// RMSNorm(x) * g, then the linear: folded into the GEMV (every row count it takes) when the gain
+// is 16-byte aligned (it loads as 16-byte vectors), else the norm's own launch into `normed` first.
 void norm_gemv(const float* x, int H, int m, const uint16_t* g, float eps, float* normed, const uint16_t* w,
                const uint16_t* w2, const uint16_t* bias, int n, float* y, int ldy, uint32_t flags, cudaStream_t s) {
-    if (m <= 6 && ((uintptr_t)g & 15u) == 0) {
+    if (m <= 8 && ((uintptr_t)g & 15u) == 0) {
         gemv(x, H, m, w, w2, bias, n, H, y, ldy, flags, s, g, eps);
     } else {
         norm(x, H, m, H, g, eps, normed, s);

@@ -96,6 +96,7 @@ struct mt_engine {
     mt_engine_options opt{};
     std::vector<void*> allocs;
     std::vector<float> timesteps;
+    int prio_hi = 0;  // launch priority of the step's critical path (the device's highest)
 
     // Buffers.
     QwenBufs llm, vae;
@@ -211,13 +212,16 @@ mt_status dit_alloc(mt_engine* e, DitBufs* d, const mt_dit_config& c, size_t row
 }
 
 // A linear over m rows of x: CUDA-core GEMV (fp32 x.f) for m <= 8, else a tcgen05 plan (x.hi/lo).
-// Route of a linear over m <= kGemvMax rows, measured with isolated launches whose weights stream
-// from DRAM: the CUDA-core GEMV's time grows with the rows (it is instruction-bound past a few rows:
-// W[9728x896] 9.0 / 14.0 / 19.5 / 24.7 us at 2 / 4 / 6 / 8 rows), the tensor-core GEMM costs about
-// 6-7 us flat while K <= 1024 (16-19 us at K >= 4096 without split-K). n_eff counts both matrices
-// of a gated linear.
+// Route of a linear over m <= kGemvMax rows, measured with isolated graph-replayed launches whose
+// weights stream from DRAM. The GEMV grows about 1 us per row (2 / 4 / 6 / 8 rows: W[3072x1024]
+// 5.0 / 7.3 / 8.3 / 9.8 us, gated W[2 x 4864x896] 8.4 / 10.2 / 14.3 / 16.7 us); the tensor-core GEMM
+// is flat (5.7 and 9.0 us) but needs its input as bf16 planes, i.e. the RMSNorm in front as its own
+// launch (~2.6 us), which the GEMV folds in. Isolated, that puts the crossovers at 5 rows (gated)
+// and 7 rows (W[3072x1024]); in the engine step the GEMV's blocks (two per SM, every register)
+// also delay the concurrent stream's kernels, and the single-request step measured faster with
+// the tensor cores from the thresholds below. n_eff counts both matrices of a gated linear.
 // An accumulating linear (the residual projections) splits K on the tensor-core route and wins from
-// 2 rows (W[1024x4096] 4.9 / 7.2 / 12.1 us on the GEMV at 2 / 4 / 8 rows against 4.5-4.9 us).
+// 2 rows (W[1024x4096] 5.2 / 7.5 / 10.0 us on the GEMV at 2 / 4 / 8 rows against 4.3-4.4 us).
 bool small_rows_tc(int m, long long n_eff, int k, bool accum = false) {
     if (m > kGemvMax) return true;
     if (accum) return m >= 2;
@@ -299,10 +303,10 @@ void norm_for(const Lin& L, const float* x, int ld, int rows, const mt_bf16* g, 
     norm_to(x, ld, rows, ld, g, eps, out, L.tc, false, s);
 }
 
-// Rows up to which a CUDA-core linear folds the RMSNorm before it: measured on the config-2 decode
-// step, one row gains 3%, eight rows lose 11% (the per-chunk gain and x^2 work makes the GEMV
-// compute-bound); the flow DiT's six rows gain 3%.
-constexpr int kFoldNormMax = 6;
+// Rows up to which a CUDA-core linear folds the RMSNorm before it: every row count of the GEMV
+// route (the 2..8-row GEMV stages x once per block, so the gain and x^2 work is small; the fold
+// saves the norm's launch, about 2.6 us in a graph).
+constexpr int kFoldNormMax = 8;
 
 // A linear after an RMSNorm, on the CUDA-core route with few rows: it reads the residual rows and
 // folds the norm in (gain as x loads, 1/rms on the dot product), so the norm has no launch.
@@ -781,6 +785,10 @@ void enqueue_step(mt_engine* e, cudaStream_t s, bool with_llm, bool with_decode,
         if (timed) cudaEventRecord(ev[5], e->sb);
         cudaEventRecord(e->ev_join, e->sb);
     }
+    // The groups' chain (LLM token -> flow -> aggregator) is the step's critical path; its kernels
+    // go first when the concurrent VAE decode's blocks compete for SMs.
+    const int prio_saved = launch_priority();
+    launch_priority() = e->prio_hi;
     for (int i = 0; i < e->G; i++) {
         Group& g = e->groups[i];
         cudaStream_t gs = i == 0 ? s : g.s;
@@ -794,6 +802,7 @@ void enqueue_step(mt_engine* e, cudaStream_t s, bool with_llm, bool with_decode,
         vae_fc1(e, g, gs);
         if (i > 0) cudaEventRecord(g.done, gs);
     }
+    launch_priority() = prio_saved;
     for (int i = 1; i < e->G; i++) cudaStreamWaitEvent(s, e->groups[i].done, 0);
     if (with_decode && !serial_decode) cudaStreamWaitEvent(s, e->ev_join, 0);
 }
@@ -886,8 +895,14 @@ mt_status mt_engine_create(mt_ctx* ctx, const mt_model* model, const mt_engine_o
             return cleanup(fail(ctx, MT_ERR_CUDA, "engine: events"));
     for (int i = 0; i < 6; i++)
         if (cudaEventCreate(&e->stage_ev[i]) != cudaSuccess) return cleanup(fail(ctx, MT_ERR_CUDA, "engine: events"));
-    // One priority for every stream: a lower-priority VAE stream was measured to slow the VAE
-    // decode (1.8 -> 2.5 ms) without shortening the LLM stage it overlaps.
+    // One priority for every stream (a lower-priority VAE stream was measured to slow the VAE
+    // decode, 1.8 -> 2.5 ms, without shortening the LLM stage it overlaps); the groups' kernels
+    // carry the device's highest priority as a launch attribute instead (enqueue_step).
+    {
+        int least = 0, greatest = 0;
+        cudaDeviceGetStreamPriorityRange(&least, &greatest);
+        e->prio_hi = greatest;
+    }
     if (cudaStreamCreateWithFlags(&e->sa, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&e->sb, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
@@ -1033,7 +1048,7 @@ mt_status mt_engine_step(mt_engine* e, void* stream, int* pcm_count) {
             e->graph_kernels = g_kernels;
             err = cudaStreamEndCapture(s, &e->graph[slot]);
             if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph capture: %s", cudaGetErrorString(err));
-            err = cudaGraphInstantiate(&e->graph_exec[slot], e->graph[slot], 0);
+            err = cudaGraphInstantiate(&e->graph_exec[slot], e->graph[slot], cudaGraphInstantiateFlagUseNodePriority);
             if (err != cudaSuccess) return fail(ctx, MT_ERR_CUDA, "step graph instantiate: %s", cudaGetErrorString(err));
         }
         cudaGraphLaunch(e->graph_exec[slot], s);

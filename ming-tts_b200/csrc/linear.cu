@@ -198,6 +198,259 @@ static int gemv_group(int k) {
     return g;
 }
 
+// GEMV for 2..8 rows. A warp owns 4 output columns; the 8 lanes of a column read 8 consecutive
+// 16-byte pieces of its weight row (one 128-byte line per column per load: full coalescing), and
+// each lane's 8 K values of x serve all 4 columns. The column-group GEMV above re-reads every row
+// of x once per column group (16 bytes of x per weight byte at 8 rows, which bounds it by L1 at
+// these row counts); one column per lane instead made each load touch 32 lines. The block's x
+// range (and norm gains) is staged in shared memory once, in a lane-interleaved order so that the
+// 8 lanes of a load read one contiguous 128 bytes. Warps split a block's columns (WC = 8 / KW
+// groups of 4) and its K range (KW parts, met in shared memory); blockIdx.y splits K across blocks
+// for plain accumulating linears (partial sums added to y atomically).
+constexpr int GQ_WARPS = 8;
+constexpr int GQ_MAX_KLEN = 1024;  // K elements staged per block
+
+template <int MR, bool GATED, bool NORM>
+__global__ void __launch_bounds__(GQ_WARPS * 32) gemv_quad_kernel(LinearArgs a, int KW, int ks_steps) {
+    constexpr int U = GATED ? 8 : 16;  // 64-wide K steps per lane loaded together
+    constexpr int NR = GATED ? 2 : 1;
+    __shared__ float red[GQ_WARPS][NR][MR][4];
+    __shared__ float ssm[MR];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int col = lane >> 3, kl = lane & 7;
+    const int WC = GQ_WARPS / KW, wc = warp % WC, wk = warp / WC;
+    const int cpb = 4 * WC;
+    const int n = blockIdx.x * cpb + wc * 4 + col;
+    const bool live = n < a.n;
+    const int steps_all = a.k >> 6;
+    const int b0 = blockIdx.y * ks_steps, b1 = min(steps_all, b0 + ks_steps);
+    const int per = (b1 - b0 + KW - 1) / KW;
+    const int s0 = b0 + wk * per, s1 = min(b1, s0 + per);  // this warp's steps (possibly none)
+    const uint16_t* wrow = a.w + (size_t)(live ? n : 0) * a.k + kl * 8;
+    const uint16_t* w2row = GATED ? a.w2 + (size_t)(live ? n : 0) * a.k + kl * 8 : nullptr;
+
+    uint4 wv[U], wv2[U];
+    auto load = [&](int sb) {
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int st = sb + u;
+            wv[u] = wv2[u] = make_uint4(0, 0, 0, 0);
+            if (live && st < s1) {
+                wv[u] = ld_stream_u4(wrow + (size_t)st * 64);
+                if (GATED) wv2[u] = ld_stream_u4(w2row + (size_t)st * 64);
+            }
+        }
+    };
+    load(s0);  // weights never depend on the previous kernel
+    pdl_wait();
+    pdl_launch();
+    const int rows = min(MR, a.m);
+
+    // Stage x (and the gains): float4 f of a 64-wide step (lane f / 2, half f % 2) goes to slot
+    // 8 (f % 2) + f / 2, so lane l's halves sit at slots l and 8 + l.
+    extern __shared__ __align__(16) float xs[];  // [rows][klen], then the gains [klen]
+    const int k0 = b0 * 64, klen = (b1 - b0) * 64, q4 = klen >> 2;
+    float4* xs4 = reinterpret_cast<float4*>(xs);
+    float4* gs4 = xs4 + (size_t)MR * q4;
+    constexpr int SV = MR;  // float4s per thread in flight: all of them for klen <= GQ_MAX_KLEN
+    for (int i0 = threadIdx.x; i0 < rows * q4; i0 += GQ_WARPS * 32 * SV) {
+        float4 v[SV];
+#pragma unroll
+        for (int u = 0; u < SV; u++) {
+            const int i = i0 + u * GQ_WARPS * 32;
+            if (i < rows * q4) {
+                const int rr = i / q4, f = i - rr * q4;
+                v[u] = *reinterpret_cast<const float4*>(a.x + (size_t)rr * a.ldx + k0 + 4 * f);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < SV; u++) {
+            const int i = i0 + u * GQ_WARPS * 32;
+            if (i < rows * q4) {
+                const int rr = i / q4, f = i - rr * q4;
+                xs4[rr * q4 + (f & ~15) + 8 * (f & 1) + ((f & 15) >> 1)] = v[u];
+            }
+        }
+    }
+    if (NORM) {
+        for (int i = threadIdx.x; i < (klen >> 3); i += GQ_WARPS * 32) {
+            const uint4 g = *reinterpret_cast<const uint4*>(a.norm_w + k0 + 8 * i);
+            const int f = 2 * i;  // float4s f and f + 1: lane (f % 16) / 2, halves 0 and 1
+            const int slot = (f & ~15) + ((f & 15) >> 1);
+            gs4[slot] = make_float4(bf16_lo(g.x), bf16_hi(g.x), bf16_lo(g.y), bf16_hi(g.y));
+            gs4[slot + 8] = make_float4(bf16_lo(g.z), bf16_hi(g.z), bf16_lo(g.w), bf16_hi(g.w));
+        }
+    }
+    __syncthreads();
+    if (NORM && warp < rows) {  // sum of squares of each row over the block's range (= all of K)
+        float q = 0.f;
+        for (int i = lane; i < q4; i += 32) {
+            const float4 v = xs4[warp * q4 + i];
+            q += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+        q = warp_sum(q);
+        if (lane == 0) ssm[warp] = q;
+    }
+
+    float acc[MR], acc2[MR];
+#pragma unroll
+    for (int r = 0; r < MR; r++) { acc[r] = 0.f; acc2[r] = 0.f; }
+    for (int sb = s0; sb < s1; sb += U) {
+        if (sb != s0) load(sb);
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int st = sb + u;
+            if (st >= s1) break;  // warp-uniform
+            float wf[8], wf2[8];
+            const uint32_t* wp = reinterpret_cast<const uint32_t*>(&wv[u]);
+            const uint32_t* wp2 = reinterpret_cast<const uint32_t*>(&wv2[u]);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                wf[2 * j] = bf16_lo(wp[j]);
+                wf[2 * j + 1] = bf16_hi(wp[j]);
+                if (GATED) {
+                    wf2[2 * j] = bf16_lo(wp2[j]);
+                    wf2[2 * j + 1] = bf16_hi(wp2[j]);
+                }
+            }
+            const int base = (st - b0) * 16 + kl;
+            if (NORM) {
+                const float4 g0 = gs4[base], g1 = gs4[base + 8];
+                const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    wf[j] *= g[j];
+                    if (GATED) wf2[j] *= g[j];
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < MR; r++) {
+                if (r < rows) {
+                    const float4 x0 = xs4[r * q4 + base], x1 = xs4[r * q4 + base + 8];
+                    acc[r] += x0.x * wf[0] + x0.y * wf[1] + x0.z * wf[2] + x0.w * wf[3] + x1.x * wf[4] + x1.y * wf[5] +
+                              x1.z * wf[6] + x1.w * wf[7];
+                    if (GATED)
+                        acc2[r] += x0.x * wf2[0] + x0.y * wf2[1] + x0.z * wf2[2] + x0.w * wf2[3] + x1.x * wf2[4] +
+                                   x1.y * wf2[5] + x1.z * wf2[6] + x1.w * wf2[7];
+                }
+            }
+        }
+    }
+    // Sum over the 8 lanes of each column; lane kl then serves row kl.
+#pragma unroll
+    for (int r = 0; r < MR; r++) {
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+            if (GATED) acc2[r] += __shfl_xor_sync(0xffffffffu, acc2[r], o);
+        }
+    }
+    float v = 0.f, v2 = 0.f;
+#pragma unroll
+    for (int r = 0; r < MR; r++)
+        if (kl == r) { v = acc[r]; v2 = acc2[r]; }
+    int r = kl, nn = n;
+    if (KW > 1) {  // the KW warps of a column group meet in shared memory
+        if (kl < MR) {
+            red[warp][0][kl][col] = v;
+            if (GATED) red[warp][GATED ? 1 : 0][kl][col] = v2;
+        }
+        __syncthreads();
+        const int t = threadIdx.x;  // task (row r, block column cb)
+        if (t >= MR * cpb) return;
+        r = t / cpb;
+        const int cb = t - r * cpb, cw = cb >> 2, cc = cb & 3;
+        v = v2 = 0.f;
+        for (int q = 0; q < KW; q++) {
+            v += red[q * WC + cw][0][r][cc];
+            if (GATED) v2 += red[q * WC + cw][GATED ? 1 : 0][r][cc];
+        }
+        nn = blockIdx.x * cpb + cb;
+    } else if (NORM) {
+        __syncthreads();  // ssm
+    }
+    if (r >= rows || nn >= a.n) return;
+    if (NORM) {
+        const float rs = rsqrtf(ssm[r] / (float)a.k + a.norm_eps);
+        v *= rs;
+        v2 *= rs;
+    }
+    if ((a.flags & MT_LINEAR_BIAS) && blockIdx.y == 0) v += bf16f(a.bias[nn]);
+    if (GATED) v = silu(v) * v2;
+    if (a.flags & MT_LINEAR_GELU) v = gelu_tanh(v);
+    if (a.flags & MT_LINEAR_SILU) v = silu(v);
+    if (a.y) {
+        float* yp = a.y + (size_t)r * a.ldy + nn;
+        if (gridDim.y > 1) {
+            atomicAdd(yp, v);  // K split across blocks: plain accumulating epilogue only
+        } else {
+            if (a.flags & MT_LINEAR_ACCUM) v += *yp;
+            *yp = v;
+        }
+    }
+    if (a.y_hi) {
+        uint16_t h, l;
+        split_bf16(v, h, l);
+        a.y_hi[(size_t)r * a.ld_ysplit + nn] = h;
+        a.y_lo[(size_t)r * a.ld_ysplit + nn] = l;
+    }
+}
+
+// Launch shape of the 2..8-row GEMV: K steps per block (split across blocks only for plain
+// accumulating epilogues, so that a block stages at most GQ_MAX_KLEN values of each x row) and KW,
+// the warps per column group: the smallest that gives about a wave of blocks.
+struct GemvQuadShape { int ks_steps, ks, kw; };
+static GemvQuadShape gemv_quad_shape(const LinearArgs& a, bool gated) {
+    const int steps = a.k / 64;
+    const bool plain_accum = (a.flags & MT_LINEAR_ACCUM) && !(a.flags & (MT_LINEAR_GELU | MT_LINEAR_SILU)) && !gated &&
+                             !a.norm_w && !a.y_hi;
+    GemvQuadShape sh;
+    int ks = plain_accum ? (steps * 64 + GQ_MAX_KLEN - 1) / GQ_MAX_KLEN : 1;
+    sh.ks_steps = (steps + ks - 1) / ks;
+    sh.ks = (steps + sh.ks_steps - 1) / sh.ks_steps;
+    sh.kw = 1;
+    while (sh.kw < GQ_WARPS && sh.kw < sh.ks_steps &&
+           (long long)((a.n + 4 * (GQ_WARPS / sh.kw) - 1) / (4 * (GQ_WARPS / sh.kw))) * sh.ks < 148)
+        sh.kw *= 2;
+    if (sh.kw > sh.ks_steps) sh.kw = 1;
+    return sh;
+}
+
+static size_t gemv_quad_smem(const LinearArgs& a, int mr, int ks_steps) {
+    return (size_t)ks_steps * 64 * sizeof(float) * (mr + (a.norm_w ? 1 : 0));
+}
+
+template <int MR, bool GATED, bool NORM>
+static void launch_gemv_quad_g(const LinearArgs& a, cudaStream_t s) {
+    const GemvQuadShape sh = gemv_quad_shape(a, GATED);
+    const int cpb = 4 * (GQ_WARPS / sh.kw);
+    launch_k(gemv_quad_kernel<MR, GATED, NORM>, dim3((a.n + cpb - 1) / cpb, sh.ks), GQ_WARPS * 32,
+             gemv_quad_smem(a, MR, sh.ks_steps), s, a, sh.kw, sh.ks_steps);
+}
+
+template <int MR>
+static void launch_gemv_quad(const LinearArgs& a, bool gated, cudaStream_t s) {
+    if (a.norm_w) {
+        if (gated) launch_gemv_quad_g<MR, true, true>(a, s);
+        else launch_gemv_quad_g<MR, false, true>(a, s);
+    } else {
+        if (gated) launch_gemv_quad_g<MR, true, false>(a, s);
+        else launch_gemv_quad_g<MR, false, false>(a, s);
+    }
+}
+
+static bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// The 2..8-row kernel takes K a multiple of 64, 16-byte aligned rows, and a staged x range within
+// the default 48 KB of dynamic shared memory.
+static bool gemv_quad_fits(const LinearArgs& a, bool gated) {
+    if (!(a.m >= 2 && a.m <= 8 && a.k % 64 == 0 && a.ldx % 4 == 0 && al16(a.x) && al16(a.w) &&
+          (!gated || al16(a.w2)) && (!a.norm_w || al16(a.norm_w))))
+        return false;
+    const int mr = a.m <= 2 ? 2 : a.m <= 4 ? 4 : 8;
+    return gemv_quad_smem(a, mr, gemv_quad_shape(a, gated).ks_steps) <= 48 * 1024;
+}
+
 // Few outputs (n <= 4, e.g. the 2-logit stop head): one warp per row of x; lane l covers k
 // columns 4l + 128t and every output's dot product, so x is read once and all loads of a warp are
 // in flight together. Weights are read before the dependency wait.
@@ -263,6 +516,14 @@ void launch_gemv(const LinearArgs& a, cudaStream_t s) {
     const int G = gemv_group(a.k);
     const bool gated = (a.flags & MT_LINEAR_SILU_GATE) != 0;
     const int mr = a.m <= 1 ? 1 : a.m <= 2 ? 2 : a.m <= 4 ? 4 : 8;
+    if (mr > 1 && gemv_quad_fits(a, gated)) {
+        switch (mr) {
+            case 2: launch_gemv_quad<2>(a, gated, s); break;
+            case 4: launch_gemv_quad<4>(a, gated, s); break;
+            default: launch_gemv_quad<8>(a, gated, s); break;
+        }
+        return;
+    }
     switch (mr) {
         case 1: launch_gemv_mr<1>(a, G, gated, s); break;
         case 2: launch_gemv_mr<2>(a, G, gated, s); break;

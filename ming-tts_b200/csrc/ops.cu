@@ -638,15 +638,22 @@ void launch_attention_decode(const AttnDecodeArgs& a, cudaStream_t s) {
     cfg.blockDim = dim3(AD_THREADS);
     cfg.dynamicSmemBytes = ad_dyn_bytes(SC, a.rows_per_req, nrg);
     cfg.stream = s;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = 1;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = S;
+    cudaLaunchAttribute attr[3];
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na++].val.programmaticStreamSerializationAllowed = 1;
+    if (S > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = 1;
+        attr[na++].val.clusterDim.z = S;
+    }
+    if (launch_priority() != 0) {
+        attr[na].id = cudaLaunchAttributePriority;
+        attr[na++].val.priority = launch_priority();
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = S > 1 ? 2 : 1;
+    cfg.numAttrs = na;
     cudaLaunchKernelEx(&cfg, attention_decode_kernel, a, SC);
 }
 
