@@ -516,7 +516,11 @@ void launch_gemv(const LinearArgs& a, cudaStream_t s) {
     const int G = gemv_group(a.k);
     const bool gated = (a.flags & MT_LINEAR_SILU_GATE) != 0;
     const int mr = a.m <= 1 ? 1 : a.m <= 2 ? 2 : a.m <= 4 ? 4 : 8;
-    if (mr > 1 && gemv_quad_fits(a, gated)) {
+    // Two plain rows stay on the column-group kernel (graph replay, weights from DRAM: W[4864x896]
+    // 5.28 vs 5.83 us, W[896x4864] 5.52 vs 7.93 us); with a folded norm or an accumulating
+    // epilogue the 2..8-row kernel wins at two rows too (config-2 pass at M = 2: 704 vs 765 us).
+    const bool quad = mr > 2 || a.norm_w || (a.flags & MT_LINEAR_ACCUM);
+    if (mr > 1 && quad && gemv_quad_fits(a, gated)) {
         switch (mr) {
             case 2: launch_gemv_quad<2>(a, gated, s); break;
             case 4: launch_gemv_quad<4>(a, gated, s); break;
