@@ -9,6 +9,8 @@
 // of G threads (8..128, a power of two) owns one output column for all MR rows, G sized so each
 // thread has at most eight 16-byte loads, all issued together before the programmatic-launch
 // dependency wait; partial sums meet through warp shuffles (and shared memory when G spans warps).
+// For 2..8 rows a second kernel (gemv_quad_kernel) gives each warp 4 columns and stages x in shared
+// memory once per block, so x is no longer re-read per column group.
 #include "common.cuh"
 #include "kernels.cuh"
 
