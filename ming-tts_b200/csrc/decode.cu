@@ -5,8 +5,11 @@
 // (VAEDecoder.swift:86-107), over caller-owned fp32 KV caches in the reference's layout
 // (Qwen.swift:7-26). Per layer: RMSNorm -> q/k/v GEMV (+bias) -> RoPE + KV append + attention ->
 // o GEMV (+=) -> RMSNorm -> gate/up GEMV (SiLU gate) -> down GEMV (+=); then the final norm of every
-// row. Each RMSNorm is folded into the GEMV that consumes it (up to 6 rows, gains 16-byte aligned). Passes that fit run as one launch of the persistent stack kernel (stack.cu); the others as
-// one launch per kernel above.
+// row. Each RMSNorm is folded into the CUDA-core linear that consumes it (gains 16-byte aligned).
+// From 3 rows the residual linears (o, down) run on the tensor cores with split K, and from 5 rows
+// the gate/up linear too (behind a norm launch that writes its bf16 planes): the routes the engine
+// measured for these shapes. Passes that fit run as one launch of the persistent stack kernel
+// (stack.cu) when the context asks for it; the others as one launch per kernel above.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -18,14 +21,27 @@ constexpr int kDecodeMaxRows = 8;  // rows of all requests together: the CUDA-co
 
 // Scratch of one call, carved from the context's scratch area (fp32): normed rows, q/k/v rows,
 // attention rows and the gated MLP rows.
+struct Planes {  // bf16 hi/lo planes of M rows (the tensor-core route's input or output)
+    uint16_t *hi, *lo;
+    int ld;
+};
 struct DecodeScratch {
     float *normed, *qkv, *attn, *mlp;
+    Planes p_norm, p_attn, p_mlp;
 };
+
+// Rows from which the residual linears (o, down) and the gate/up linear take the tensor cores.
+// Config 2 in graph replay: 8 rows 1164 -> 857 us with both; from 2 rows the residual route was
+// 717 against 703 us, so two rows stay on the GEMV.
+constexpr int kTcResidualRows = 3;
+constexpr int kTcGateUpRows = 5;
 
 size_t decode_scratch_floats(const mt_qwen_config& c, int M) {
     const size_t qkvw = (size_t)(c.heads + 2 * c.kv_heads) * 64;
     auto up = [](size_t n) { return (n + 63) & ~size_t(63); };  // 256-byte aligned pieces
-    return up((size_t)M * c.hidden) + up((size_t)M * qkvw) + up((size_t)M * c.heads * 64) + up((size_t)M * c.intermediate);
+    // fp32 rows, then the plane pairs (two bf16 planes of M x ld take M x ld floats)
+    return 2 * (up((size_t)M * c.hidden) + up((size_t)M * c.heads * 64) + up((size_t)M * c.intermediate)) +
+           up((size_t)M * qkvw);
 }
 
 bool aligned(const void* p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0; }
@@ -77,20 +93,49 @@ mt_status ctx_stack_area(mt_ctx* ctx, size_t bytes, void** out) {
 DecodeScratch carve(float* base, const mt_qwen_config& c, int M) {
     const size_t qkvw = (size_t)(c.heads + 2 * c.kv_heads) * 64;
     auto up = [](size_t n) { return (n + 63) & ~size_t(63); };
+    auto planes = [&](float* at, int ld) {
+        Planes p;
+        p.hi = reinterpret_cast<uint16_t*>(at);
+        p.lo = p.hi + (size_t)M * ld;  // M * ld * 2 bytes: a multiple of 16 (ld % 8 == 0)
+        p.ld = ld;
+        return p;
+    };
     DecodeScratch s;
     s.normed = base;
     s.qkv = s.normed + up((size_t)M * c.hidden);
     s.attn = s.qkv + up((size_t)M * qkvw);
     s.mlp = s.attn + up((size_t)M * c.heads * 64);
+    float* pl = s.mlp + up((size_t)M * c.intermediate);
+    s.p_norm = planes(pl, c.hidden);
+    pl += up((size_t)M * c.hidden);
+    s.p_attn = planes(pl, c.heads * 64);
+    pl += up((size_t)M * c.heads * 64);
+    s.p_mlp = planes(pl, c.intermediate);
     return s;
 }
 
+// One tensor-core linear over bf16 planes: fp32 y (accumulated with MT_LINEAR_ACCUM, split K
+// chosen by the planner) or bf16 planes out.
+mt_status tc_linear(mt_ctx* ctx, const Planes& x, int m, const uint16_t* w, const uint16_t* w2, int n, int k, float* y,
+                    int ldy, const Planes* yp, uint32_t flags, cudaStream_t s) {
+    LinearArgs a{};
+    a.x_hi = x.hi; a.x_lo = x.lo; a.ld_split = x.ld;
+    a.m = m; a.n = n; a.k = k; a.w = w; a.w2 = w2;
+    a.y = y; a.ldy = ldy;
+    if (yp) { a.y_hi = yp->hi; a.y_lo = yp->lo; a.ld_ysplit = yp->ld; }
+    a.flags = flags; a.split_k = 0;
+    return launch_gemm_tc(ctx, a, s);
+}
+
 // One CUDA-core linear; with norm_w it reads RMSNorm(x) * norm_w (the norm folded in: no launch).
+// With yp the output goes to bf16 planes (for a tensor-core consumer) instead of y.
 void gemv(const float* x, int ldx, int m, const uint16_t* w, const uint16_t* w2, const uint16_t* bias, int n, int k,
-          float* y, int ldy, uint32_t flags, cudaStream_t s, const uint16_t* norm_w = nullptr, float eps = 0.f) {
+          float* y, int ldy, uint32_t flags, cudaStream_t s, const uint16_t* norm_w = nullptr, float eps = 0.f,
+          const Planes* yp = nullptr) {
     LinearArgs a{};
     a.x = x; a.ldx = ldx; a.m = m; a.n = n; a.k = k; a.w = w; a.w2 = w2; a.bias = bias;
-    a.y = y; a.ldy = ldy; a.flags = flags; a.split_k = 1;
+    a.y = yp ? nullptr : y; a.ldy = ldy; a.flags = flags; a.split_k = 1;
+    if (yp) { a.y_hi = yp->hi; a.y_lo = yp->lo; a.ld_ysplit = yp->ld; }
     a.norm_w = norm_w; a.norm_eps = eps;
     launch_gemv(a, s);
 }
@@ -101,15 +146,24 @@ void norm(const float* x, int ld, int rows, int width, const uint16_t* g, float 
     launch_rmsnorm(a, s);
 }
 
+void norm_planes(const float* x, int ld, int rows, int width, const uint16_t* g, float eps, const Planes& y,
+                 cudaStream_t s) {
+    RmsArgs a{};
+    a.x = x; a.ldx = ld; a.rows = rows; a.width = width; a.w = g; a.eps = eps;
+    a.y_hi = y.hi; a.y_lo = y.lo; a.ld_split = y.ld;
+    launch_rmsnorm(a, s);
+}
+
 // RMSNorm(x) * g, then the linear: folded into the GEMV (every row count it takes) when the gain
 // is 16-byte aligned (it loads as 16-byte vectors), else the norm's own launch into `normed` first.
 void norm_gemv(const float* x, int H, int m, const uint16_t* g, float eps, float* normed, const uint16_t* w,
-               const uint16_t* w2, const uint16_t* bias, int n, float* y, int ldy, uint32_t flags, cudaStream_t s) {
+               const uint16_t* w2, const uint16_t* bias, int n, float* y, int ldy, uint32_t flags, cudaStream_t s,
+               const Planes* yp = nullptr) {
     if (m <= 8 && ((uintptr_t)g & 15u) == 0) {
-        gemv(x, H, m, w, w2, bias, n, H, y, ldy, flags, s, g, eps);
+        gemv(x, H, m, w, w2, bias, n, H, y, ldy, flags, s, g, eps, yp);
     } else {
         norm(x, H, m, H, g, eps, normed, s);
-        gemv(normed, H, m, w, w2, bias, n, H, y, ldy, flags, s);
+        gemv(normed, H, m, w, w2, bias, n, H, y, ldy, flags, s, nullptr, 0.f, yp);
     }
 }
 
@@ -162,6 +216,7 @@ extern "C" mt_status mt_qwen_decode(mt_ctx* ctx, void* stream, const mt_qwen_wei
 
     const int H = c.hidden, qkvw = (c.heads + 2 * c.kv_heads) * 64, A = c.heads * 64;
     const size_t tensor = (size_t)c.kv_heads * capacity * 64;
+    const bool tc_res = M >= kTcResidualRows, tc_gu = M >= kTcGateUpRows;
     for (int l = 0; l < c.layers; l++) {
         const mt_qwen_layer& L = w->layers[l];
         float* kc = kv + (size_t)(2 * l) * tensor;
@@ -171,11 +226,29 @@ extern "C" mt_status mt_qwen_decode(mt_ctx* ctx, void* stream, const mt_qwen_wei
         da.hkv = c.kv_heads; da.pos0 = 0; da.pos_dev = positions; da.window = c.window; da.kc = kc; da.vc = kc + tensor;
         da.req_stride = kv_stride; da.cap = capacity; da.inv_freq = inv_freq; da.out = sc.attn; da.ldo = A;
         da.max_keys = c.window > 0 ? c.window : capacity; da.status = ctx->d_status;
+        if (tc_res) { da.out = nullptr; da.out_hi = sc.p_attn.hi; da.out_lo = sc.p_attn.lo; da.ld_split = A; }
         launch_attention_decode(da, s);
-        gemv(sc.attn, A, M, L.o_w, nullptr, nullptr, H, A, x, H, MT_LINEAR_ACCUM, s);
-        norm_gemv(x, H, M, L.norm2, c.eps, sc.normed, L.gate_w, L.up_w, nullptr, c.intermediate, sc.mlp, c.intermediate,
-                  MT_LINEAR_SILU_GATE, s);
-        gemv(sc.mlp, c.intermediate, M, L.down_w, nullptr, nullptr, H, c.intermediate, x, H, MT_LINEAR_ACCUM, s);
+        if (tc_res) {
+            st = tc_linear(ctx, sc.p_attn, M, L.o_w, nullptr, H, A, x, H, nullptr, MT_LINEAR_ACCUM, s);
+            if (st != MT_OK) return st;
+        } else {
+            gemv(sc.attn, A, M, L.o_w, nullptr, nullptr, H, A, x, H, MT_LINEAR_ACCUM, s);
+        }
+        if (tc_gu) {
+            norm_planes(x, H, M, H, L.norm2, c.eps, sc.p_norm, s);
+            st = tc_linear(ctx, sc.p_norm, M, L.gate_w, L.up_w, c.intermediate, H, nullptr, 0, &sc.p_mlp,
+                           MT_LINEAR_SILU_GATE, s);
+            if (st != MT_OK) return st;
+        } else {
+            norm_gemv(x, H, M, L.norm2, c.eps, sc.normed, L.gate_w, L.up_w, nullptr, c.intermediate, sc.mlp,
+                      c.intermediate, MT_LINEAR_SILU_GATE, s, tc_res ? &sc.p_mlp : nullptr);
+        }
+        if (tc_res) {
+            st = tc_linear(ctx, sc.p_mlp, M, L.down_w, nullptr, H, c.intermediate, x, H, nullptr, MT_LINEAR_ACCUM, s);
+            if (st != MT_OK) return st;
+        } else {
+            gemv(sc.mlp, c.intermediate, M, L.down_w, nullptr, nullptr, H, c.intermediate, x, H, MT_LINEAR_ACCUM, s);
+        }
     }
     norm(x, H, M, H, w->final_norm, c.eps, z, s);
     return check_launch(ctx, "mt_qwen_decode");
